@@ -1,0 +1,178 @@
+"""Data parallelism over flat, bucketed parameter / gradient arenas.
+
+Behaviour matched to what the reference drives in Megatron's DDP (elastic_megatron/megatron_manager/
+training_state.py:109-137, 176-197, 199-311): one contiguous param buffer and one fp32 gradient buffer per
+rank, bucketed; gradients are reduce-scattered (ZeRO-1) bucket by bucket, optionally overlapped with
+backward, then all-reduced across Group-ZeRO instances; after the optimizer step the parameter buckets
+are all-gathered.  The layout comes from ``planner/layout.py`` so the reshard planner sees exactly the
+buffers used here.
+
+Gradient scaling: buckets are reduced with SUM and the optimizer scales the own shard by ``1/(DP*CP)``
+(dense and expert alike: expert replicas jointly see the tokens of every DP*CP rank).  Parameters whose
+gradients are partial sums across TP ranks under sequence parallelism (norm weights, router) are first
+all-reduced over the TP group.
+"""
+from __future__ import annotations
+
+from typing import Dict, List, Optional
+
+import torch
+import torch.distributed as dist
+
+from ..planner.layout import BufferLayout, RankLayout
+
+
+def _rs_inplace(buf: torch.Tensor, shard_index: int, group) -> None:
+    """Reduce-scatter (SUM) ``buf`` over ``group``; shard ``shard_index`` of ``buf`` receives the result."""
+    n = dist.get_world_size(group)
+    if n == 1:
+        return
+    if buf.is_cuda:
+        c = buf.numel() // n
+        dist.reduce_scatter_tensor(buf[shard_index * c:(shard_index + 1) * c], buf, group=group)
+    else:
+        dist.all_reduce(buf, group=group)
+
+
+def _ag_inplace(buf: torch.Tensor, shard_index: int, group) -> None:
+    n = dist.get_world_size(group)
+    if n == 1:
+        return
+    c = buf.numel() // n
+    if buf.is_cuda:
+        dist.all_gather_into_tensor(buf, buf[shard_index * c:(shard_index + 1) * c], group=group)
+    else:
+        parts = list(buf.chunk(n))
+        mine = parts[shard_index].clone()
+        dist.all_gather(parts, mine, group=group)
+
+
+class DistributedDataParallel:
+    def __init__(self, layout: RankLayout, pstate, params: Dict[str, torch.nn.Parameter],
+                 param_arena: torch.Tensor, grad_arena: torch.Tensor, overlap_grad_reduce: bool = False):
+        self.layout, self.ps = layout, pstate
+        self.params = params
+        self.overlap = overlap_grad_reduce
+        self.param_arena, self.grad_arena = param_arena, grad_arena
+        s = pstate.strategy
+        self.sp = bool(s.sequence_parallel) and s.tensor_model_parallel_size > 1
+        self._hooks = []
+        self.bind(param_arena, grad_arena)
+        self._pending: List = []
+        self._ready: Dict[int, int] = {}
+        self._launched = set()
+        # gradient reduction is only started from backward hooks while this is True (the last
+        # micro-batch); earlier micro-batches just accumulate (the reference's ``no_sync``)
+        self.sync_enabled = True
+        for p in params.values():
+            self._hooks.append(p.register_post_accumulate_grad_hook(self._make_acc_hook(p)))
+            p._grad_ready = self._make_ready(p)
+
+    # ------------------------------------------------------------------ memory binding
+    def bind(self, param_arena: torch.Tensor, grad_arena: Optional[torch.Tensor]) -> None:
+        self.param_arena, self.grad_arena = param_arena, grad_arena
+        for name, p in self.params.items():
+            off = self.layout.offset_by_name[name]
+            n = p._local_param.numel
+            if grad_arena is not None:
+                p.main_grad = grad_arena[off:off + n].view(p._local_param.shape)
+            else:
+                p.main_grad = None
+
+    def _make_acc_hook(self, p):
+        def hook(param):
+            if param.grad is not None:
+                param.main_grad.add_(param.grad.view(param.main_grad.shape).to(param.main_grad.dtype))
+                param.grad = None
+                param._grad_ready()
+        return hook
+
+    def _make_ready(self, p):
+        def ready():
+            if not self.overlap or not self.sync_enabled:
+                return
+            # bucket bookkeeping for overlap: a bucket is reduced once all its params reported
+            b = self._bucket_of.get(id(p))
+            if b is None:
+                return
+            self._ready[b] = self._ready.get(b, 0) + 1
+            if self._ready[b] == self._bucket_sizes[b]:
+                self._launch_bucket(b)
+        return ready
+
+    # ------------------------------------------------------------------ grad sync
+    def _bucket_views(self):
+        """(kind, bucket index, grad view, shard index, zero group, inter group)."""
+        out = []
+        L = self.layout
+        for kind, bl, base, gname, iname, zi in (
+                ("dense", L.dense, 0, "zero", "zero_inter", L.dense_shard_index),
+                ("expert", L.expert, L.dense.numel, "expert_zero", "expert_zero_inter", L.expert_shard_index)):
+            if bl is None:
+                continue
+            for b, (s, e) in enumerate(bl.buckets):
+                out.append((kind, b, base + s, base + e, zi, self.ps.groups.get(gname), self.ps.groups.get(iname)))
+        return out
+
+    def prepare(self):
+        """Per-step bucket bookkeeping for overlapped reduction."""
+        self._ready = {}
+        self._pending = []
+        self._bucket_of = {}
+        self._bucket_sizes = {}
+        self._launched = set()
+        if not self.overlap:
+            return
+        for i, (kind, b, s, e, zi, g, ig) in enumerate(self._bucket_views()):
+            bl = self.layout.dense if kind == "dense" else self.layout.expert
+            names = [bl.params[j].name for j in bl.bucket_params[b]]
+            ps = [self.params[n] for n in names]
+            # SP-partial params need a TP all-reduce first: keep their buckets for the end of backward
+            if self.sp and any(p._local_param.sp_partial for p in ps):
+                continue
+            for p in ps:
+                self._bucket_of[id(p)] = i
+            self._bucket_sizes[i] = len(ps)
+
+    def _launch_bucket(self, i: int):
+        kind, b, s, e, zi, g, ig = self._bucket_views()[i]
+        if i in self._launched:
+            return
+        self._launched.add(i)
+        _rs_inplace(self.grad_arena[s:e], zi, g)
+
+    def zero_grad(self) -> None:
+        if self.grad_arena is not None:
+            self.grad_arena.zero_()
+        self.prepare()
+
+    def finish_grad_sync(self) -> None:
+        if self.sp and self.ps.size("tp") > 1:
+            parts = [p.main_grad.view(-1) for p in self.params.values() if p._local_param.sp_partial]
+            if parts:
+                flat = torch.cat(parts)
+                dist.all_reduce(flat, group=self.ps.group("tp"))
+                o = 0
+                for t in parts:
+                    t.copy_(flat[o:o + t.numel()])
+                    o += t.numel()
+        views = self._bucket_views()
+        for i, (kind, b, s, e, zi, g, ig) in enumerate(views):
+            if i not in getattr(self, "_launched", set()):
+                _rs_inplace(self.grad_arena[s:e], zi, g)
+        # Group-ZeRO: replicas of one shard all-reduce across instances
+        for i, (kind, b, s, e, zi, g, ig) in enumerate(views):
+            if ig is not None and dist.get_world_size(ig) > 1:
+                n = dist.get_world_size(g) if g is not None else 1
+                c = (e - s) // n
+                dist.all_reduce(self.grad_arena[s + zi * c:s + (zi + 1) * c], group=ig)
+
+    def start_param_sync(self) -> None:
+        for kind, b, s, e, zi, g, ig in self._bucket_views():
+            if g is not None:
+                _ag_inplace(self.param_arena[s:e], zi, g)
+
+    def remove_hooks(self):
+        for h in self._hooks:
+            h.remove()
+        self._hooks = []

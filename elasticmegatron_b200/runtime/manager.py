@@ -1,0 +1,236 @@
+"""``ElasticMegatronManager``: online switching between parallel strategies.
+
+Public API kept from the reference (elastic_megatron/elastic_manager.py:31-265):
+
+* ``ElasticMegatronManager.register(setup_model_and_optimizer_func, train_valid_test_datasets_provider)``
+* ``ElasticMegatronManager(parallel_strategy_list, model, optimizer, opt_param_scheduler, ...)``
+* ``reshard(new_parallel_strategy, logger=None, is_meta_device=False, save_ckpt=False) -> TrainingState | None``
+* ``build_iterators()``, ``get_data_parallel_group(strategy)``, ``global_barrier_by_gloo()``,
+  ``clear_meta_state(strategy)``.
+
+A switch (reference call stack: elastic_manager.py:189-258):
+
+1. build (lazily, cached per strategy) or rebuild the destination ``TrainingState``;
+2. plan once per (src, dst) pair (``planner/plan.py``) - exact shard-to-shard ranges for fp32 master /
+   exp_avg / exp_avg_sq *and* the parameters;
+3. execute the plan with the selected engine (direct peer-memory kernel on GPUs, batched P2P otherwise);
+   a Group-ZeRO instance-count change is the same plan (replica copies) instead of a separate code path;
+4. copy LR / scheduler / step counters from rank 0 over the union group;
+5. release the source state into the arena pool (no ``empty_cache``);
+6. log one JSON line with device time (MAX over the union), bytes moved and the NVLink roofline fraction.
+"""
+from __future__ import annotations
+
+import json
+import logging
+from typing import Callable, Dict, List, Optional, Union
+
+import torch
+import torch.distributed as dist
+
+from ..config import get_args
+from ..parallel.process_groups import (ProcessGroupPool, create_all_groups, global_barrier_by_gloo,
+                                       set_world_group)
+from ..parallel.strategy import ParallelStrategy, union_ranks
+from ..planner.plan import KIND_OPT, KIND_PARAM, build_plan
+from ..utils.logging import log_json
+from ..utils.timers import DeviceTimer, HostTimer, max_over_ranks
+from .data import DataloaderState
+from .training_state import TrainingState
+
+NVLINK_GBS = 770.0  # measured per-direction peer copy bandwidth on this pool's B200s
+
+
+def default_setup_model_and_optimizer(strategy: ParallelStrategy, is_meta_device: bool = False) -> TrainingState:
+    return TrainingState(strategy, is_meta_device=is_meta_device)
+
+
+class ElasticMegatronManager:
+    @classmethod
+    def register(cls, setup_model_and_optimizer_func: Optional[Callable] = None,
+                 train_valid_test_datasets_provider: Optional[Callable] = None) -> None:
+        TrainingState.setup_model_and_optimizer_func = setup_model_and_optimizer_func
+        DataloaderState.register(train_valid_test_datasets_provider)
+
+    def __init__(self, parallel_strategy_list: List[Union[Dict, ParallelStrategy]], model=None, optimizer=None,
+                 opt_param_scheduler=None, training_state: Optional[TrainingState] = None,
+                 engine: Optional[str] = None, warmup: bool = True):
+        self._rank = dist.get_rank() if dist.is_initialized() else 0
+        self.strategies = [ParallelStrategy.from_any(s) for s in parallel_strategy_list]
+        assert len(set(self.strategies)) == len(self.strategies), "duplicate strategies"
+        backend = dist.get_backend() if dist.is_initialized() else "gloo"
+        create_all_groups(self.strategies, backend)
+        if training_state is None and model is not None:
+            training_state = model[0]._training_state
+        self._states: Dict[ParallelStrategy, Optional[TrainingState]] = {s: None for s in self.strategies}
+        self.current = self.strategies[0]
+        if training_state is not None:
+            assert training_state.strategy == self.strategies[0], "strategy 0 must match the live model"
+            self._states[self.current] = training_state
+        self._plans: Dict[tuple, object] = {}
+        self.engine_name = engine or ("native" if torch.cuda.is_available() else "torch")
+        self.engine = self._make_engine(self.engine_name)
+        self.last_switch: Dict = {}
+        set_world_group(ProcessGroupPool.get(self.current.ranks))
+
+    # ------------------------------------------------------------------ helpers
+    def _make_engine(self, name: str):
+        if name == "torch":
+            from ..transfer.torch_engine import TorchP2PEngine
+
+            return TorchP2PEngine()
+        if name == "reference":
+            from ..transfer.reference_engine import ReferenceAlgorithmEngine
+
+            return ReferenceAlgorithmEngine()
+        if name == "native":
+            from ..transfer.native_engine import NativeP2PEngine
+
+            return NativeP2PEngine()
+        raise ValueError(name)
+
+    @property
+    def training_state(self) -> Optional[TrainingState]:
+        return self._states.get(self.current)
+
+    def state_for(self, strategy) -> Optional[TrainingState]:
+        return self._states.get(ParallelStrategy.from_any(strategy))
+
+    def plan(self, src: ParallelStrategy, dst: ParallelStrategy):
+        key = (src.key(), dst.key())
+        p = self._plans.get(key)
+        if p is None:
+            p = build_plan(src, dst)
+            self._plans[key] = p
+        return p
+
+    def _get_or_build(self, s: ParallelStrategy, is_meta: bool) -> Optional[TrainingState]:
+        if self._rank >= s.world_size:
+            return None
+        ts = self._states.get(s)
+        if ts is None:
+            fn = TrainingState.setup_model_and_optimizer_func or default_setup_model_and_optimizer
+            ts = fn(s, is_meta_device=is_meta)
+            self._states[s] = ts
+        elif not is_meta:
+            ts.rebuild()
+        return ts
+
+    # ------------------------------------------------------------------ API
+    def build_iterators(self, consumed_samples: Optional[int] = None):
+        ts = self.training_state
+        if ts is None:
+            return None, None, None
+        if consumed_samples is None:
+            consumed_samples = get_args().consumed_train_samples
+        # consumed samples from rank 0 (reference: dataloader_state.py:135-141)
+        t = torch.tensor([consumed_samples], dtype=torch.float64)
+        if dist.is_initialized() and self.current.world_size > 1:
+            dist.broadcast(t, src=0, group=ProcessGroupPool.get(self.current.ranks, "gloo"))
+        return DataloaderState.build_iterators(ts, int(t.item()))
+
+    def get_data_parallel_group(self, parallel_strategy):
+        s = ParallelStrategy.from_any(parallel_strategy)
+        if self._rank >= s.world_size:
+            return None
+        return ProcessGroupPool.get(s.get_ranks("dp"))
+
+    @classmethod
+    def global_barrier_by_gloo(cls):
+        global_barrier_by_gloo()
+
+    def clear_meta_state(self, parallel_strategy) -> None:
+        s = ParallelStrategy.from_any(parallel_strategy)
+        ts = self._states.get(s)
+        if ts is not None:
+            assert ts.is_meta_device
+        self._states[s] = None
+
+    def reshard(self, new_parallel_strategy, logger: Optional[logging.Logger] = None, is_meta_device: bool = False,
+                save_ckpt: bool = False, ckpt_dir: Optional[str] = None) -> Optional[TrainingState]:
+        assert not (is_meta_device and save_ckpt), "Can't save checkpoint in meta device"
+        dst_s = ParallelStrategy.from_any(new_parallel_strategy)
+        assert dst_s in self._states, f"strategy {dst_s} was not declared at construction"
+        src_s = self.current
+        src = self._states.get(src_s)
+        if save_ckpt and src is not None:
+            from .checkpoint import save_checkpoint
+
+            save_checkpoint(src, ckpt_dir or "before_reshard")
+        if dst_s == src_s:
+            return src
+        union = union_ranks(src_s, dst_s)
+        if self._rank not in union:
+            self.current = dst_s
+            set_world_group(ProcessGroupPool.get(dst_s.ranks))
+            return None
+        ugroup = ProcessGroupPool.get(union)
+        same_layout = src_s.layout_key() == dst_s.layout_key()
+        with HostTimer(sync=False) as t_build:
+            dst = self._get_or_build(dst_s, is_meta_device)
+        if src is not None and src.model_released:
+            src.rebuild()
+        plan = self.plan(src_s, dst_s)
+        kinds_moved = None
+        if is_meta_device:
+            # meta mode: no data moves; only pre-build state / connections (reference "fake transfer")
+            ms, nbytes = 0.0, 0
+            if hasattr(self.engine, "warmup"):
+                self.engine.warmup(plan, self._rank, src, dst, ugroup)
+        else:
+            ms, nbytes = self._transfer(plan, src, dst, ugroup, same_layout)
+        self._transfer_lr(src, dst, union)
+        if src is not None and src is not dst:
+            src.release()
+        self.current = dst_s
+        set_world_group(ProcessGroupPool.get(dst_s.ranks))
+        if dst is not None and not is_meta_device:
+            dst.ddp.zero_grad()
+        mx = max_over_ranks([ms, nbytes / 1e9], group=ProcessGroupPool.get(union, "gloo")
+                            if dist.is_initialized() else None)
+        roof = plan.nvlink_roofline_ms(NVLINK_GBS, 4, torch.finfo(get_args().model.torch_dtype).bits // 8)
+        self.last_switch = {"src": str(src_s), "dst": str(dst_s), "engine": self.engine_name,
+                            "transfer_ms": mx[0], "gbytes": mx[1],
+                            "bandwidth_gbs": (mx[1] / (mx[0] / 1e3)) if mx[0] > 0 else None,
+                            "nvlink_roofline_ms": roof,
+                            "roofline_frac": (roof / mx[0]) if mx[0] > 0 else None,
+                            "build_ms": t_build.elapsed}
+        if self._rank == 0 or logger is not None:
+            log_json("reshard", logger, **self.last_switch)
+        if save_ckpt and dst is not None:
+            from .checkpoint import save_checkpoint
+
+            save_checkpoint(dst, ckpt_dir or "after_reshard")
+        return dst
+
+    # ------------------------------------------------------------------ internals
+    def _transfer(self, plan, src, dst, ugroup, same_layout: bool):
+        eng = self.engine
+        if hasattr(eng, "reset_counters"):
+            eng.reset_counters()
+        sp = src.param_flat if src is not None else None
+        so = src.opt_flat if src is not None else None
+        dp = dst.param_flat if dst is not None else None
+        do = dst.opt_flat if dst is not None else None
+        timer = DeviceTimer() if torch.cuda.is_available() else HostTimer(sync=False)
+        with timer:
+            eng.execute(plan, self._rank, sp, so, dp, do, ugroup)
+        d = plan.desc
+        el_p = torch.finfo(get_args().model.torch_dtype).bits // 8
+        mine = d[((d["src_rank"] == self._rank) | (d["dst_rank"] == self._rank)) & (d["src_rank"] != d["dst_rank"])]
+        nbytes = int(((mine["rows"] * mine["cols"]) * (mine["kind"] == KIND_OPT) * 12).sum()
+                     + ((mine["rows"] * mine["cols"]) * (mine["kind"] == KIND_PARAM) * el_p).sum())
+        return timer.elapsed, nbytes
+
+    def _transfer_lr(self, src, dst, union):
+        """Optimizer step counters, LR and scheduler position from rank 0 (reference: transfer.py:393-433).
+
+        Rank 0 is always in the union: active ranks are the prefix ``0..world_size-1`` of every strategy."""
+        obj = [None]
+        if self._rank == 0 and src is not None:
+            obj = [{"opt": src.optimizer.state_dict(), "sched": src.opt_param_scheduler.state_dict()}]
+        if dist.is_initialized():
+            dist.broadcast_object_list(obj, src=0, group=ProcessGroupPool.get(union, "gloo"))
+        if dst is not None and obj[0] is not None:
+            dst.optimizer.load_state_dict(obj[0]["opt"])
+            dst.opt_param_scheduler.load_state_dict(obj[0]["sched"])

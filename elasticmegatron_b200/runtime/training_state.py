@@ -1,0 +1,200 @@
+"""``TrainingState``: model + optimizer + scheduler of one strategy, over pooled flat arenas.
+
+Reference counterpart: elastic_megatron/megatron_manager/training_state.py (427 lines) which holds Megatron
+model chunks / optimizer / scheduler and frees memory without destroying tensor objects.  Here the stage's
+parameters, ``main_grad`` views and the optimizer all point into three arenas (param, grad, optimizer) that
+``release_*`` hands back to the pool and ``rebuild_*`` takes again; every Python object (modules, hooks,
+optimizer, scheduler) survives a release.
+"""
+from __future__ import annotations
+
+from typing import Callable, Dict, Optional
+
+import torch
+
+from ..config import ModelConfig, TrainConfig, get_args
+from ..models.llama import GPTStage
+from ..parallel.ddp import DistributedDataParallel
+from ..parallel.optimizer import DistributedAdam
+from ..parallel.process_groups import ParallelState
+from ..parallel.scheduler import OptimizerParamScheduler
+from ..parallel.strategy import ParallelStrategy
+from ..planner.layout import RankLayout, rank_layout
+from .memory import Arena, get_pool
+
+
+class TrainingState:
+    setup_model_and_optimizer_func: Optional[Callable] = None
+
+    @classmethod
+    def set_setup_model_and_optimizer_func(cls, fn: Callable) -> None:
+        assert callable(fn)
+        cls.setup_model_and_optimizer_func = fn
+
+    def __init__(self, strategy: ParallelStrategy, cfg: Optional[ModelConfig] = None,
+                 train_cfg: Optional[TrainConfig] = None, device=None, is_meta_device: bool = False):
+        args = get_args()
+        self.cfg = cfg or args.model
+        self.train_cfg = train_cfg or args.train
+        self.strategy = strategy
+        self.ps = ParallelState(strategy)
+        self.rank = self.ps.rank
+        self.is_meta_device = is_meta_device
+        if device is None:
+            device = torch.device("cuda", torch.cuda.current_device()) if torch.cuda.is_available() else \
+                torch.device("cpu")
+        self.device = torch.device(device)
+        self.pool = get_pool(self.device)
+        tc = self.train_cfg
+        self.layout: RankLayout = rank_layout(self.cfg, strategy, self.rank, tc.overlap_grad_reduce,
+                                              tc.ddp_bucket_size)
+        self.param_dtype = self.cfg.torch_dtype
+        self.param_arena: Optional[Arena] = None
+        self.grad_arena: Optional[Arena] = None
+        self.opt_arena: Optional[Arena] = None
+        if not is_meta_device:
+            self._alloc_model()
+            self._alloc_opt()
+        views = self._param_views() if not is_meta_device else self._meta_views()
+        self.stage = GPTStage(self.cfg, self.ps, self.layout.params, views, tc.micro_batch_size)
+        self.stage._training_state = self
+        self.model = [self.stage]
+        self.ddp = DistributedDataParallel(self.layout, self.ps, self.stage.params_by_name, self.param_flat,
+                                           self.grad_flat, tc.overlap_grad_reduce)
+        self.optimizer = DistributedAdam(self.layout, self.ps, self.param_flat, self.grad_flat, self.opt_flat, tc)
+        gbs = tc.global_batch_size
+        decay = (tc.lr_decay_iters or tc.train_iters) * gbs
+        self.opt_param_scheduler = OptimizerParamScheduler(self.optimizer, tc.lr, tc.min_lr,
+                                                           tc.lr_warmup_iters * gbs, decay, tc.lr_decay_style)
+        self.model_released = is_meta_device
+        self.optimizer_released = is_meta_device
+
+    # ------------------------------------------------------------------ arenas
+    @property
+    def param_flat(self) -> Optional[torch.Tensor]:
+        return self.param_arena.view(self.param_dtype, (self.layout.param_numel,)) if self.param_arena else None
+
+    @property
+    def grad_flat(self) -> Optional[torch.Tensor]:
+        return self.grad_arena.view(torch.float32, (self.layout.param_numel,)) if self.grad_arena else None
+
+    @property
+    def opt_flat(self) -> Optional[torch.Tensor]:
+        return self.opt_arena.view(torch.float32, (3, self.layout.opt_numel)) if self.opt_arena else None
+
+    def _alloc_model(self):
+        n = self.layout.param_numel
+        el = torch.finfo(self.param_dtype).bits // 8
+        self.param_arena = self.pool.alloc(n * el)
+        self.grad_arena = self.pool.alloc(n * 4)
+        # padding elements must be zero (they travel in all-gathers and reductions)
+        self.param_flat.zero_()
+        self.grad_flat.zero_()
+
+    def _alloc_opt(self):
+        self.opt_arena = self.pool.alloc(3 * self.layout.opt_numel * 4)
+        self.opt_flat.zero_()
+
+    def _param_views(self) -> Dict[str, torch.Tensor]:
+        P = self.param_flat
+        return {lp.name: P[self.layout.offset_by_name[lp.name]:self.layout.offset_by_name[lp.name] + lp.numel]
+                .view(lp.shape) for lp in self.layout.params}
+
+    def _meta_views(self) -> Dict[str, torch.Tensor]:
+        return {lp.name: torch.empty(lp.shape, dtype=self.param_dtype, device="meta") for lp in self.layout.params}
+
+    def release_model(self) -> None:
+        if self.model_released:
+            return
+        self.pool.free(self.param_arena)
+        self.pool.free(self.grad_arena)
+        self.param_arena = self.grad_arena = None
+        self.model_released = True
+
+    def release_optimizer(self) -> None:
+        if self.optimizer_released:
+            return
+        self.pool.free(self.opt_arena)
+        self.opt_arena = None
+        self.optimizer_released = True
+
+    def rebuild_model(self) -> None:
+        if not self.model_released:
+            return
+        self._alloc_model()
+        self.stage.rebind(self._param_views())
+        self.ddp.bind(self.param_flat, self.grad_flat)
+        self.optimizer.bind(self.param_flat, self.grad_flat, self.opt_flat)
+        self.model_released = False
+        self.is_meta_device = False
+
+    def rebuild_optimizer(self) -> None:
+        if not self.optimizer_released:
+            return
+        self._alloc_opt()
+        self.optimizer.bind(self.param_flat, self.grad_flat, self.opt_flat)
+        self.optimizer_released = False
+
+    def release(self):
+        self.release_model()
+        self.release_optimizer()
+
+    def rebuild(self):
+        self.rebuild_model()
+        self.rebuild_optimizer()
+
+    # ------------------------------------------------------------------ init
+    def init_weights(self, seed: int = 0, method: str = "global") -> None:
+        """Random-init params (N(0, std), norms = 1) and set master = param, moments = 0.
+
+        ``global``: layout-independent values (every strategy holds the same model; small models / tests).
+        ``local``: device-side per-shard init, identical across DP replicas (fast; benchmarks).
+        """
+        P, O = self.param_flat, self.opt_flat
+        P.zero_()
+        O.zero_()
+        if method == "global":
+            from ..planner.materialize import init_global_params, scatter_to_rank
+
+            g = init_global_params(self.cfg, seed)
+            g = {k: v.to(self.param_dtype).float() for k, v in g.items()}
+            Pc = torch.zeros(P.shape, dtype=torch.float32)
+            Oc = torch.zeros(O.shape, dtype=torch.float32)
+            scatter_to_rank(self.cfg, self.strategy, self.rank, g, Pc, Oc, None, self.train_cfg.overlap_grad_reduce,
+                            self.train_cfg.ddp_bucket_size)
+            P.copy_(Pc.to(self.param_dtype))
+            O.copy_(Oc)
+        else:
+            c = self.strategy.coords(self.rank)
+            for lp in self.layout.params:
+                off = self.layout.offset_by_name[lp.name]
+                vp = lp.members[0][0]
+                v = P[off:off + lp.numel]
+                if vp.init == "ones":
+                    v.fill_(1.0)
+                else:
+                    gen = torch.Generator(device=P.device)
+                    gen.manual_seed(seed * 7919 + vp.index * 131 + (c["etp"] if lp.is_expert else c["tp"]) * 17
+                                    + (c["ep"] if lp.is_expert else 0))
+                    v.normal_(0.0, self.cfg.init_method_std, generator=gen)
+            for a, o, n, wd, cnt in self.optimizer.segs:
+                O[0, o:o + n].copy_(P[a:a + n].float())
+
+    # ------------------------------------------------------------------ misc (reference API)
+    @property
+    def optimizers(self):
+        return [self.optimizer]
+
+    @staticmethod
+    def refresh_config(model, optimizer):
+        """Re-wire grad-sync hooks for the active model (hooks are owned by DDP here, so nothing to do)."""
+        return None
+
+    def update_model_weight(self) -> None:
+        """Regenerate params from the fp32 master of the own shard and all-gather over DP (reference:
+        training_state.py:176-197).  The direct transfer engine already delivers params, so the manager only
+        calls this for engines that move optimizer state alone."""
+        P, O = self.param_flat, self.opt_flat
+        for a, o, n, wd, c in self.optimizer.segs:
+            P[a:a + n].copy_(O[0, o:o + n].to(P.dtype))
+        self.ddp.start_param_sync()
