@@ -1,0 +1,70 @@
+// Python bindings of the elasticmegatron_b200._C extension.
+#include <torch/extension.h>
+
+namespace emb {
+int64_t launch_count();
+void reset_launch_count();
+torch::Tensor arena_alloc(int64_t nbytes, int64_t device);
+torch::Tensor ipc_get_handle(torch::Tensor arena);
+int64_t ipc_open(torch::Tensor handle);
+void ipc_close_all();
+int64_t ipc_open_count();
+std::vector<torch::Tensor> rmsnorm_fwd(torch::Tensor x, torch::Tensor w, double eps);
+std::vector<torch::Tensor> rmsnorm_bwd(torch::Tensor dy, torch::Tensor x, torch::Tensor w, torch::Tensor rstd,
+                                       c10::optional<torch::Tensor> dw_accum);
+torch::Tensor swiglu_fwd(torch::Tensor h);
+torch::Tensor swiglu_bwd(torch::Tensor dy, torch::Tensor h);
+torch::Tensor rope_fwd(torch::Tensor qkv, torch::Tensor cosv, torch::Tensor sinv, int64_t nrot, bool inverse);
+torch::Tensor ce_local_max(torch::Tensor logits);
+torch::Tensor ce_local_stats(torch::Tensor logits, torch::Tensor labels, torch::Tensor lmax, int64_t vstart);
+torch::Tensor ce_bwd(torch::Tensor logits, torch::Tensor labels, torch::Tensor lmax, torch::Tensor sumexp,
+                     torch::Tensor dloss, int64_t vstart);
+torch::Tensor embedding_fwd(torch::Tensor ids, torch::Tensor w, int64_t vstart);
+void embedding_bwd(torch::Tensor ids, torch::Tensor dy, torch::Tensor target, int64_t vstart);
+void adam_segments(torch::Tensor O, torch::Tensor G, torch::Tensor P, torch::Tensor chunks, double lr, double b1,
+                   double b2, double eps, double wd, int64_t step, double grad_scale, double max_norm,
+                   c10::optional<torch::Tensor> sumsq);
+torch::Tensor seg_sumsq(torch::Tensor G, torch::Tensor chunks);
+void reshard_copy(torch::Tensor tasks, int64_t ntasks, int64_t grid);
+int64_t copy_task_bytes();
+torch::Tensor gemm(torch::Tensor a, torch::Tensor b, bool trans_a, bool trans_b, c10::optional<torch::Tensor> out,
+                   bool accumulate);
+torch::Tensor gemm_tc(torch::Tensor a, torch::Tensor b, bool trans_a, bool trans_b, c10::optional<torch::Tensor> out,
+                      bool accumulate);
+bool gemm_tc_supported(torch::Tensor a, torch::Tensor b, bool trans_a, bool trans_b, c10::optional<torch::Tensor> out,
+                       bool accumulate);
+}  // namespace emb
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  using namespace emb;
+  m.def("launch_count", &launch_count);
+  m.def("reset_launch_count", &reset_launch_count);
+  m.def("arena_alloc", &arena_alloc);
+  m.def("ipc_get_handle", &ipc_get_handle);
+  m.def("ipc_open", &ipc_open);
+  m.def("ipc_close_all", &ipc_close_all);
+  m.def("ipc_open_count", &ipc_open_count);
+  m.def("rmsnorm_fwd", &rmsnorm_fwd);
+  m.def("rmsnorm_bwd", &rmsnorm_bwd, py::arg("dy"), py::arg("x"), py::arg("w"), py::arg("rstd"),
+        py::arg("dw_accum") = py::none());
+  m.def("swiglu_fwd", &swiglu_fwd);
+  m.def("swiglu_bwd", &swiglu_bwd);
+  m.def("rope_fwd", &rope_fwd);
+  m.def("ce_local_max", &ce_local_max);
+  m.def("ce_local_stats", &ce_local_stats);
+  m.def("ce_bwd", &ce_bwd);
+  m.def("embedding_fwd", &embedding_fwd);
+  m.def("embedding_bwd", &embedding_bwd);
+  m.def("adam_segments", &adam_segments, py::arg("O"), py::arg("G"), py::arg("P"), py::arg("chunks"), py::arg("lr"),
+        py::arg("b1"), py::arg("b2"), py::arg("eps"), py::arg("wd"), py::arg("step"), py::arg("grad_scale"),
+        py::arg("max_norm") = 0.0, py::arg("sumsq") = py::none());
+  m.def("seg_sumsq", &seg_sumsq);
+  m.def("reshard_copy", &reshard_copy, py::arg("tasks"), py::arg("ntasks"), py::arg("grid") = 0);
+  m.def("copy_task_bytes", &copy_task_bytes);
+  m.def("gemm", &gemm, py::arg("a"), py::arg("b"), py::arg("trans_a") = false, py::arg("trans_b") = false,
+        py::arg("out") = py::none(), py::arg("accumulate") = false);
+  m.def("gemm_tc", &gemm_tc, py::arg("a"), py::arg("b"), py::arg("trans_a") = false, py::arg("trans_b") = false,
+        py::arg("out") = py::none(), py::arg("accumulate") = false);
+  m.def("gemm_tc_supported", &gemm_tc_supported, py::arg("a"), py::arg("b"), py::arg("trans_a") = false,
+        py::arg("trans_b") = false, py::arg("out") = py::none(), py::arg("accumulate") = false);
+}

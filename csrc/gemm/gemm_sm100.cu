@@ -1,0 +1,453 @@
+// K3: dense bf16 GEMM on the 5th-generation tensor cores (tcgen05 + TMEM + TMA), sm_100a.
+//
+//   C[M, N] (=|+=) A[M, K] * B[K, N]      A, B bf16;  C bf16 (store) or fp32 (store / accumulate)
+//
+// Operand layouts (per the torch-style call gemm(a, b, trans_a, trans_b)):
+//   A is K-major when a is [M, K] row-major, MN-major when a is [K, M] row-major (trans_a);
+//   B is K-major when b is [N, K] row-major (trans_b), MN-major when b is [K, N] row-major.
+// So fprop (x @ W^T), dgrad (dy @ W) and wgrad (dy^T @ x, accumulated into the fp32 main_grad) all run
+// without a transpose copy.
+//
+// Structure: persistent kernel, one CTA per SM, 192 threads, warp-specialised:
+//   warp 0      - TMA producer: one elected thread streams 128x64 A and 256x64 B tiles (128-byte swizzle)
+//                 into a 4-stage shared-memory ring, completing on per-stage mbarriers;
+//   warp 1      - allocates 512 TMEM columns (two 128x256 fp32 accumulators) and one elected thread issues
+//                 tcgen05.mma (M=128, N=256, K=16) with shared-memory descriptors, committing each stage back
+//                 to the producer and each finished accumulator to the epilogue;
+//   warps 2..5  - epilogue: tcgen05.ld 32x32b from their TMEM lane quarter, convert, store to global memory,
+//                 while the MMA warp already accumulates the next tile into the other TMEM buffer.
+// No TMA multicast is used anywhere (this kernel also runs inside multi-GPU jobs).
+//
+// Every mbarrier wait is bounded; on a timeout the kernel records an error code in a device flag that the
+// host checks, and the waiting role stops issuing work (no trap).
+#include <cudaTypedefs.h>
+
+#include "../include/common.cuh"
+
+namespace emb {
+namespace gk {
+
+constexpr int BM = 128, BN = 256, BK = 64, STAGES = 4;
+constexpr int A_STAGE_BYTES = BM * BK * 2;  // 16 KiB
+constexpr int B_STAGE_BYTES = BN * BK * 2;  // 32 KiB
+constexpr int STAGE_BYTES = A_STAGE_BYTES + B_STAGE_BYTES;
+constexpr int TMEM_COLS = 512;
+constexpr int NUM_THREADS = 192;
+constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+constexpr uint32_t WAIT_LIMIT = 1u << 28;  // ~seconds of polling before giving up
+
+// ------------------------------------------------------------------------------------------ PTX helpers
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Bounded wait: returns false (and records `code` in *err) if the phase never completes.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, int code) {
+  for (uint32_t i = 0; i < WAIT_LIMIT; ++i) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if (i > 64) __nanosleep(32);
+  }
+  atomicExch(err, code);
+  return false;
+}
+__device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* map, uint64_t* bar, int x, int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+          smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+      : "memory");
+}
+__device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// Shared-memory matrix descriptor (sm100 "version 1"), 128-byte swizzle.
+__device__ __forceinline__ uint64_t smem_desc(uint32_t addr, uint32_t lbo_bytes, uint32_t sbo_bytes) {
+  uint64_t d = 0;
+  d |= (uint64_t)((addr >> 4) & 0x3FFF);
+  d |= (uint64_t)((lbo_bytes >> 4) & 0x3FFF) << 16;
+  d |= (uint64_t)((sbo_bytes >> 4) & 0x3FFF) << 32;
+  d |= (uint64_t)1 << 46;  // version
+  d |= (uint64_t)2 << 61;  // SWIZZLE_128B
+  return d;
+}
+
+// Instruction descriptor for kind::f16: bf16 x bf16 -> fp32, M=128, N=256.
+__host__ __device__ constexpr uint32_t make_idesc(bool a_mn_major, bool b_mn_major) {
+  return (1u << 4)                     // D = F32
+         | (1u << 7)                   // A = BF16
+         | (1u << 10)                  // B = BF16
+         | ((a_mn_major ? 1u : 0u) << 15) | ((b_mn_major ? 1u : 0u) << 16) | ((uint32_t)(BN >> 3) << 17) |
+         ((uint32_t)(BM >> 4) << 24);
+}
+
+__device__ __forceinline__ void mma_bf16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                         uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate));
+}
+__device__ __forceinline__ void mma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+
+#define TMEM_LD_32(taddr, r)                                                                                        \
+  asm volatile(                                                                                                     \
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19," \
+      "%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"                                                    \
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]), \
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),      \
+        "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),     \
+        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])                   \
+      : "r"(taddr))
+
+struct Params {
+  void* C;
+  int M, N, K;
+  int ldc;
+  int out_fp32;    // C is fp32 (else bf16)
+  int accumulate;  // C += (fp32 only)
+  int a_mn, b_mn;  // operand majorness
+  int* err;
+};
+
+__global__ void __launch_bounds__(NUM_THREADS, 1)
+    gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + STAGES * A_STAGE_BYTES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
+  uint64_t* empty = full + STAGES;
+  uint64_t* tfull = empty + STAGES;  // [2]
+  uint64_t* tempty = tfull + 2;      // [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int tiles_m = (p.M + BM - 1) / BM;
+  const int tiles_n = (p.N + BN - 1) / BN;
+  const int num_tiles = tiles_m * tiles_n;
+  const int nk = (p.K + BK - 1) / BK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tfull[b], 1);
+      mbar_init(&tempty[b], 4);  // one arrive per epilogue warp
+    }
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(TMEM_COLS));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      int it = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+        const int m0 = (t % tiles_m) * BM;
+        const int n0 = (t / tiles_m) * BN;
+        for (int kb = 0; kb < nk; ++kb, ++it) {
+          const int s = it % STAGES;
+          const uint32_t ph = (it / STAGES) & 1;
+          if (!mbar_wait(&empty[s], ph ^ 1, p.err, 1) || *abort_flag) { ok = false; *abort_flag = 1; break; }
+          mbar_expect_tx(&full[s], STAGE_BYTES);
+          uint8_t* a_dst = sA + s * A_STAGE_BYTES;
+          uint8_t* b_dst = sB + s * B_STAGE_BYTES;
+          const int k0 = kb * BK;
+          if (!p.a_mn) {
+            tma_load_2d(a_dst, &tmA, &full[s], k0, m0);
+          } else {
+            tma_load_2d(a_dst, &tmA, &full[s], m0, k0);
+            tma_load_2d(a_dst + 8192, &tmA, &full[s], m0 + 64, k0);
+          }
+          if (!p.b_mn) {
+            tma_load_2d(b_dst, &tmB, &full[s], k0, n0);
+          } else {
+#pragma unroll
+            for (int j = 0; j < 4; ++j) tma_load_2d(b_dst + j * 8192, &tmB, &full[s], n0 + 64 * j, k0);
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      const uint32_t idesc = make_idesc(p.a_mn, p.b_mn);
+      // per-K16-step descriptor advance and LBO/SBO for each operand layout
+      const uint32_t a_lbo = p.a_mn ? 8192 : 16, a_sbo = 1024, a_step = p.a_mn ? 2048 : 32;
+      const uint32_t b_lbo = p.b_mn ? 8192 : 16, b_sbo = 1024, b_step = p.b_mn ? 2048 : 32;
+      int it = 0, local = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x, ++local) {
+        const int buf = local & 1;
+        const uint32_t tph = (local >> 1) & 1;
+        if (!mbar_wait(&tempty[buf], tph ^ 1, p.err, 2) || *abort_flag) { ok = false; *abort_flag = 1; break; }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + buf * BN;
+        for (int kb = 0; kb < nk; ++kb, ++it) {
+          const int s = it % STAGES;
+          const uint32_t ph = (it / STAGES) & 1;
+          if (!mbar_wait(&full[s], ph, p.err, 3) || *abort_flag) { ok = false; *abort_flag = 1; break; }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(sA + s * A_STAGE_BYTES);
+          const uint32_t b_addr = smem_u32(sB + s * B_STAGE_BYTES);
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k) {
+            const uint64_t ad = smem_desc(a_addr + k * a_step, a_lbo, a_sbo);
+            const uint64_t bd = smem_desc(b_addr + k * b_step, b_lbo, b_sbo);
+            mma_bf16(d_tmem, ad, bd, idesc, (kb | k) != 0);
+          }
+          mma_commit(&empty[s]);  // frees the smem stage once these MMAs have read it
+        }
+        if (ok) mma_commit(&tfull[buf]);  // accumulator ready for the epilogue
+      }
+    }
+  } else {
+    // ------------------------------------------------------------------ epilogue (warps 2..5)
+    const int quarter = warp & 3;  // TMEM lane quarter this warp may access
+    const int row_in_tile = quarter * 32 + lane;
+    int local = 0;
+    for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++local) {
+      const int buf = local & 1;
+      const uint32_t tph = (local >> 1) & 1;
+      if (!mbar_wait(&tfull[buf], tph, p.err, 4) || *abort_flag) { *abort_flag = 1; break; }
+      tc_fence_after();
+      const int m0 = (t % tiles_m) * BM;
+      const int n0 = (t / tiles_m) * BN;
+      const int row = m0 + row_in_tile;
+      const bool row_ok = row < p.M;
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; ++c) {
+        uint32_t r[32];
+        const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + buf * BN + c * 32;
+        TMEM_LD_32(taddr, r);
+        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+        const int col0 = n0 + c * 32;
+        if (!row_ok || col0 >= p.N) continue;
+        const int ncols = min(32, p.N - col0);
+        if (p.out_fp32) {
+          float* dst = reinterpret_cast<float*>(p.C) + (size_t)row * p.ldc + col0;
+          if (ncols == 32 && ((reinterpret_cast<uintptr_t>(dst) & 15) == 0)) {
+#pragma unroll
+            for (int v = 0; v < 8; ++v) {
+              float4 o = make_float4(__uint_as_float(r[4 * v]), __uint_as_float(r[4 * v + 1]),
+                                     __uint_as_float(r[4 * v + 2]), __uint_as_float(r[4 * v + 3]));
+              float4* d4 = reinterpret_cast<float4*>(dst) + v;
+              if (p.accumulate) {
+                float4 old = *d4;
+                o.x += old.x; o.y += old.y; o.z += old.z; o.w += old.w;
+              }
+              *d4 = o;
+            }
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              if (j < ncols) {
+                float v = __uint_as_float(r[j]);
+                dst[j] = p.accumulate ? dst[j] + v : v;
+              }
+            }
+          }
+        } else {
+          __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(p.C) + (size_t)row * p.ldc + col0;
+          if (ncols == 32 && ((reinterpret_cast<uintptr_t>(dst) & 15) == 0)) {
+#pragma unroll
+            for (int v = 0; v < 4; ++v) {
+              float f[8];
+#pragma unroll
+              for (int j = 0; j < 8; ++j) f[j] = __uint_as_float(r[8 * v + j]);
+              reinterpret_cast<uint4*>(dst)[v] = pack8(f);
+            }
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              if (j < ncols) dst[j] = __float2bfloat16_rn(__uint_as_float(r[j]));
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty[buf]);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(TMEM_COLS));
+  }
+}
+
+// ------------------------------------------------------------------------------------------ host side
+static PFN_cuTensorMapEncodeTiled_v12000 get_encode() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (!fn) {
+    cudaDriverEntryPointQueryResult q;
+    void* p = nullptr;
+    EMB_CUDA_CHECK(cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q));
+    TORCH_CHECK(q == cudaDriverEntryPointSuccess && p, "cuTensorMapEncodeTiled not available");
+    fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  }
+  return fn;
+}
+
+// 2-D bf16 tensor map over a row-major matrix [rows, cols] (cols contiguous), box {box_cols, box_rows}.
+static CUtensorMap make_map(const void* base, int64_t rows, int64_t cols, int64_t ld, int box_cols, int box_rows) {
+  CUtensorMap m;
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)(ld * 2)};
+  cuuint32_t box[2] = {(cuuint32_t)box_cols, (cuuint32_t)box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = get_encode()(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+                            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  TORCH_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled failed: ", (int)r);
+  return m;
+}
+
+static int* err_flag() {
+  static int* f = nullptr;
+  static int dev_of = -1;
+  int dev;
+  cudaGetDevice(&dev);
+  if (!f || dev_of != dev) {
+    EMB_CUDA_CHECK(cudaMalloc(&f, sizeof(int)));
+    EMB_CUDA_CHECK(cudaMemset(f, 0, sizeof(int)));
+    dev_of = dev;
+  }
+  return f;
+}
+
+}  // namespace gk
+
+static bool ok_2d(const at::Tensor& t) {
+  return t.dim() == 2 && t.stride(1) == 1 && t.stride(0) % 8 == 0 && (reinterpret_cast<uintptr_t>(t.data_ptr()) % 16) == 0;
+}
+
+bool gemm_tc_supported(at::Tensor a, at::Tensor b, bool trans_a, bool trans_b, c10::optional<at::Tensor> out,
+                       bool accumulate) {
+  if (!a.is_cuda() || a.scalar_type() != at::kBFloat16 || b.scalar_type() != at::kBFloat16) return false;
+  if (!ok_2d(a) || !ok_2d(b)) return false;
+  if (out.has_value() && out->defined()) {
+    auto& c = *out;
+    if (c.dim() != 2 || c.stride(1) != 1) return false;
+    if (c.scalar_type() != at::kFloat && c.scalar_type() != at::kBFloat16) return false;
+    if (accumulate && c.scalar_type() != at::kFloat) return false;
+  }
+  return true;
+}
+
+at::Tensor gemm_tc(at::Tensor a, at::Tensor b, bool trans_a, bool trans_b, c10::optional<at::Tensor> out,
+                      bool accumulate) {
+  using namespace gk;
+  TORCH_CHECK(gemm_tc_supported(a, b, trans_a, trans_b, out, accumulate), "gemm_tc: unsupported operands");
+  const int64_t M = trans_a ? a.size(1) : a.size(0);
+  const int64_t K = trans_a ? a.size(0) : a.size(1);
+  const int64_t N = trans_b ? b.size(0) : b.size(1);
+  TORCH_CHECK((trans_b ? b.size(1) : b.size(0)) == K, "gemm: inner dimensions differ");
+  at::Tensor C;
+  if (out.has_value() && out->defined()) {
+    C = *out;
+    TORCH_CHECK(C.size(0) == M && C.size(1) == N, "gemm: bad output shape");
+  } else {
+    C = at::empty({M, N}, a.options());
+  }
+  if (M == 0 || N == 0) return C;
+  if (K == 0) {
+    if (!accumulate) C.zero_();
+    return C;
+  }
+  const bool a_mn = trans_a, b_mn = !trans_b;
+  CUtensorMap tA = a_mn ? make_map(a.data_ptr(), K, M, a.stride(0), 64, 64) : make_map(a.data_ptr(), M, K, a.stride(0), 64, BM);
+  CUtensorMap tB = b_mn ? make_map(b.data_ptr(), K, N, b.stride(0), 64, 64) : make_map(b.data_ptr(), N, K, b.stride(0), 64, BN);
+  Params p;
+  p.C = C.data_ptr();
+  p.M = (int)M;
+  p.N = (int)N;
+  p.K = (int)K;
+  p.ldc = (int)C.stride(0);
+  p.out_fp32 = C.scalar_type() == at::kFloat;
+  p.accumulate = accumulate ? 1 : 0;
+  p.a_mn = a_mn;
+  p.b_mn = b_mn;
+  p.err = err_flag();
+  static bool attr_set = false;
+  if (!attr_set) {
+    EMB_CUDA_CHECK(cudaFuncSetAttribute(gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
+    attr_set = true;
+  }
+  const int tiles = (int)(((M + BM - 1) / BM) * ((N + BN - 1) / BN));
+  const int grid = std::min(tiles, num_sms());
+  gemm_kernel<<<grid, NUM_THREADS, SMEM_BYTES, cur_stream()>>>(tA, tB, p);
+  EMB_LAUNCH_CHECK();
+  count_launch();
+  return C;
+}
+
+int64_t gemm_error_flag() {
+  int v = 0;
+  EMB_CUDA_CHECK(cudaMemcpy(&v, gk::err_flag(), sizeof(int), cudaMemcpyDeviceToHost));
+  return v;
+}
+
+void gemm_clear_error() { EMB_CUDA_CHECK(cudaMemset(gk::err_flag(), 0, sizeof(int))); }
+
+// Library fallback for operands the tensor-core kernel does not take (e.g. fp32 inputs or unaligned strides).
+at::Tensor gemm(at::Tensor a, at::Tensor b, bool trans_a, bool trans_b, c10::optional<at::Tensor> out,
+                   bool accumulate) {
+  if (gemm_tc_supported(a, b, trans_a, trans_b, out, accumulate)) return gemm_tc(a, b, trans_a, trans_b, out, accumulate);
+  auto A = trans_a ? a.t() : a;
+  auto B = trans_b ? b.t() : b;
+  if (out.has_value() && out->defined()) {
+    auto C = *out;
+    if (accumulate) {
+      C.add_(at::matmul(A.to(C.scalar_type()), B.to(C.scalar_type())));
+    } else {
+      C.copy_(at::matmul(A, B));
+    }
+    return C;
+  }
+  return at::matmul(A, B);
+}
+
+}  // namespace emb

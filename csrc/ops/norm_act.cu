@@ -1,0 +1,317 @@
+// RMSNorm (fwd/bwd), SwiGLU (fwd/bwd) and RoPE on the fused QKV layout; bf16 I/O, fp32 math.
+// Memory-bound kernels: 16-byte vector loads/stores, one CTA per row for the norms, persistent CTAs with
+// per-CTA fp32 partials (reduced in a fixed order, so results are deterministic) for the weight gradient.
+#include "../include/common.cuh"
+
+namespace emb {
+
+// ------------------------------------------------------------------------------------------ RMSNorm fwd
+template <int VPT>
+__global__ void rmsnorm_fwd_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ w,
+                                   __nv_bfloat16* __restrict__ y, float* __restrict__ rstd_out, int H, float eps) {
+  __shared__ float sh[32];
+  const int row = blockIdx.x;
+  const int nvec = H / 8;
+  const uint4* xr = reinterpret_cast<const uint4*>(x + (size_t)row * H);
+  float v[VPT][8];
+  float ss = 0.f;
+#pragma unroll
+  for (int k = 0; k < VPT; ++k) {
+    int i = threadIdx.x + k * blockDim.x;
+    if (i < nvec) {
+      uint4 u = xr[i];
+      unpack8(u, v[k]);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) ss += v[k][j] * v[k][j];
+    }
+  }
+  ss = block_sum(ss, sh);
+  const float r = rsqrtf(ss / H + eps);
+  if (threadIdx.x == 0) rstd_out[row] = r;
+  const uint4* wr = reinterpret_cast<const uint4*>(w);
+  uint4* yr = reinterpret_cast<uint4*>(y + (size_t)row * H);
+#pragma unroll
+  for (int k = 0; k < VPT; ++k) {
+    int i = threadIdx.x + k * blockDim.x;
+    if (i < nvec) {
+      float wf[8], o[8];
+      unpack8(wr[i], wf);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) o[j] = v[k][j] * r * wf[j];
+      yr[i] = pack8(o);
+    }
+  }
+}
+
+// threads per row so that each thread holds at most 4 16-byte vectors of the row in registers
+static int pick_threads(int nvec, int& vpt) {
+  int t = ((nvec + 3) / 4 + 31) / 32 * 32;
+  t = std::max(32, std::min(1024, t));
+  vpt = (nvec + t - 1) / t;
+  return t;
+}
+
+std::vector<at::Tensor> rmsnorm_fwd(at::Tensor x, at::Tensor w, double eps) {
+  check_cuda_bf16(x, "x");
+  check_cuda_bf16(w, "w");
+  const int64_t T = x.size(0), H = x.size(1);
+  TORCH_CHECK(H % 8 == 0 && H <= 8 * 4 * 1024, "hidden size must be a multiple of 8 and <= 32768");
+  auto y = at::empty_like(x);
+  auto rstd = at::empty({T}, x.options().dtype(at::kFloat));
+  if (T == 0) return {y, rstd};
+  int vpt;
+  int threads = pick_threads((int)(H / 8), vpt);
+  auto st = cur_stream();
+#define L(V) rmsnorm_fwd_kernel<V><<<T, threads, 0, st>>>((const __nv_bfloat16*)x.data_ptr(),          \
+      (const __nv_bfloat16*)w.data_ptr(), (__nv_bfloat16*)y.data_ptr(), rstd.data_ptr<float>(), (int)H, \
+      (float)eps)
+  if (vpt <= 1) L(1); else if (vpt == 2) L(2); else if (vpt == 3) L(3); else L(4);
+#undef L
+  EMB_LAUNCH_CHECK();
+  count_launch();
+  return {y, rstd};
+}
+
+// ------------------------------------------------------------------------------------------ RMSNorm bwd
+template <int VPT>
+__global__ void rmsnorm_bwd_kernel(const __nv_bfloat16* __restrict__ dy, const __nv_bfloat16* __restrict__ x,
+                                   const __nv_bfloat16* __restrict__ w, const float* __restrict__ rstd,
+                                   __nv_bfloat16* __restrict__ dx, float* __restrict__ dw_part, int T, int H) {
+  __shared__ float sh[32];
+  const int nvec = H / 8;
+  const uint4* wr = reinterpret_cast<const uint4*>(w);
+  float wf[VPT][8], acc[VPT][8];
+#pragma unroll
+  for (int k = 0; k < VPT; ++k) {
+    int i = threadIdx.x + k * blockDim.x;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) acc[k][j] = 0.f;
+    if (i < nvec) unpack8(wr[i], wf[k]);
+  }
+  for (int row = blockIdx.x; row < T; row += gridDim.x) {
+    const uint4* xr = reinterpret_cast<const uint4*>(x + (size_t)row * H);
+    const uint4* dr = reinterpret_cast<const uint4*>(dy + (size_t)row * H);
+    const float r = rstd[row];
+    float xv[VPT][8], gv[VPT][8];
+    float dot = 0.f;
+#pragma unroll
+    for (int k = 0; k < VPT; ++k) {
+      int i = threadIdx.x + k * blockDim.x;
+      if (i < nvec) {
+        float d[8];
+        unpack8(xr[i], xv[k]);
+        unpack8(dr[i], d);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          float xh = xv[k][j] * r;
+          xv[k][j] = xh;
+          gv[k][j] = d[j] * wf[k][j];
+          dot += gv[k][j] * xh;
+          acc[k][j] += d[j] * xh;
+        }
+      }
+    }
+    dot = block_sum(dot, sh) / H;
+    uint4* o = reinterpret_cast<uint4*>(dx + (size_t)row * H);
+#pragma unroll
+    for (int k = 0; k < VPT; ++k) {
+      int i = threadIdx.x + k * blockDim.x;
+      if (i < nvec) {
+        float t[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) t[j] = r * (gv[k][j] - xv[k][j] * dot);
+        o[i] = pack8(t);
+      }
+    }
+  }
+  float* part = dw_part + (size_t)blockIdx.x * H;
+#pragma unroll
+  for (int k = 0; k < VPT; ++k) {
+    int i = threadIdx.x + k * blockDim.x;
+    if (i < nvec) {
+      float4* p4 = reinterpret_cast<float4*>(part + i * 8);
+      p4[0] = make_float4(acc[k][0], acc[k][1], acc[k][2], acc[k][3]);
+      p4[1] = make_float4(acc[k][4], acc[k][5], acc[k][6], acc[k][7]);
+    }
+  }
+}
+
+// dw[h] = sum_b part[b, h] in a fixed order; optionally accumulated into an fp32 target.
+__global__ void colsum_kernel(const float* __restrict__ part, float* __restrict__ out, int nb, int H, int accumulate) {
+  int h = blockIdx.x * blockDim.x + threadIdx.x;
+  if (h >= H) return;
+  float s = 0.f;
+  for (int b = 0; b < nb; ++b) s += part[(size_t)b * H + h];
+  out[h] = accumulate ? out[h] + s : s;
+}
+
+std::vector<at::Tensor> rmsnorm_bwd(at::Tensor dy, at::Tensor x, at::Tensor w, at::Tensor rstd,
+                                       c10::optional<at::Tensor> dw_accum) {
+  check_cuda_bf16(dy, "dy");
+  check_cuda_bf16(x, "x");
+  const int64_t T = x.size(0), H = x.size(1);
+  auto dx = at::empty_like(x);
+  int vpt;
+  int threads = pick_threads((int)(H / 8), vpt);
+  int grid = (int)std::min<int64_t>(T, (int64_t)num_sms() * 2);
+  if (grid < 1) grid = 1;
+  auto part = at::empty({grid, H}, x.options().dtype(at::kFloat));
+  auto st = cur_stream();
+#define L(V) rmsnorm_bwd_kernel<V><<<grid, threads, 0, st>>>((const __nv_bfloat16*)dy.data_ptr(),                  \
+      (const __nv_bfloat16*)x.data_ptr(), (const __nv_bfloat16*)w.data_ptr(), rstd.data_ptr<float>(),               \
+      (__nv_bfloat16*)dx.data_ptr(), part.data_ptr<float>(), (int)T, (int)H)
+  if (vpt <= 1) L(1); else if (vpt == 2) L(2); else if (vpt == 3) L(3); else L(4);
+#undef L
+  EMB_LAUNCH_CHECK();
+  at::Tensor dw;
+  bool acc = dw_accum.has_value() && dw_accum->defined();
+  if (acc) {
+    dw = *dw_accum;
+    TORCH_CHECK(dw.scalar_type() == at::kFloat && dw.is_contiguous() && dw.numel() == H);
+  } else {
+    dw = at::empty({H}, x.options().dtype(at::kFloat));
+  }
+  colsum_kernel<<<(H + 255) / 256, 256, 0, st>>>(part.data_ptr<float>(), dw.data_ptr<float>(), grid, (int)H, acc);
+  EMB_LAUNCH_CHECK();
+  count_launch(2);
+  return {dx, dw};
+}
+
+// ------------------------------------------------------------------------------------------ SwiGLU
+__global__ void swiglu_fwd_kernel(const __nv_bfloat16* __restrict__ h, __nv_bfloat16* __restrict__ y, int64_t T,
+                                  int F) {
+  const int fv = F / 8;
+  const int64_t n = T * fv;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    int64_t t = i / fv;
+    int j = (int)(i - t * fv);
+    const uint4* hr = reinterpret_cast<const uint4*>(h + t * 2 * F);
+    float g[8], u[8], o[8];
+    unpack8(hr[j], g);
+    unpack8(hr[fv + j], u);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) o[k] = g[k] / (1.f + __expf(-g[k])) * u[k];
+    reinterpret_cast<uint4*>(y + t * F)[j] = pack8(o);
+  }
+}
+
+__global__ void swiglu_bwd_kernel(const __nv_bfloat16* __restrict__ dy, const __nv_bfloat16* __restrict__ h,
+                                  __nv_bfloat16* __restrict__ dh, int64_t T, int F) {
+  const int fv = F / 8;
+  const int64_t n = T * fv;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    int64_t t = i / fv;
+    int j = (int)(i - t * fv);
+    const uint4* hr = reinterpret_cast<const uint4*>(h + t * 2 * F);
+    float g[8], u[8], d[8], dg[8], du[8];
+    unpack8(hr[j], g);
+    unpack8(hr[fv + j], u);
+    unpack8(reinterpret_cast<const uint4*>(dy + t * F)[j], d);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      float s = 1.f / (1.f + __expf(-g[k]));
+      float silu = g[k] * s;
+      dg[k] = d[k] * u[k] * (s * (1.f + g[k] * (1.f - s)));
+      du[k] = d[k] * silu;
+    }
+    uint4* o = reinterpret_cast<uint4*>(dh + t * 2 * F);
+    o[j] = pack8(dg);
+    o[fv + j] = pack8(du);
+  }
+}
+
+static int ew_grid(int64_t n) {
+  int64_t g = (n + 255) / 256;
+  int64_t cap = (int64_t)num_sms() * 8;
+  return (int)std::max<int64_t>(1, std::min(g, cap));
+}
+
+at::Tensor swiglu_fwd(at::Tensor h) {
+  check_cuda_bf16(h, "h");
+  const int64_t T = h.numel() / h.size(-1);
+  const int F = (int)(h.size(-1) / 2);
+  TORCH_CHECK(F % 8 == 0, "ffn size must be a multiple of 8");
+  auto sizes = h.sizes().vec();
+  sizes.back() = F;
+  auto y = at::empty(sizes, h.options());
+  if (T == 0) return y;
+  swiglu_fwd_kernel<<<ew_grid(T * F / 8), 256, 0, cur_stream()>>>((const __nv_bfloat16*)h.data_ptr(),
+                                                                  (__nv_bfloat16*)y.data_ptr(), T, F);
+  EMB_LAUNCH_CHECK();
+  count_launch();
+  return y;
+}
+
+at::Tensor swiglu_bwd(at::Tensor dy, at::Tensor h) {
+  check_cuda_bf16(dy, "dy");
+  check_cuda_bf16(h, "h");
+  const int64_t T = h.numel() / h.size(-1);
+  const int F = (int)(h.size(-1) / 2);
+  auto dh = at::empty_like(h);
+  if (T == 0) return dh;
+  swiglu_bwd_kernel<<<ew_grid(T * F / 8), 256, 0, cur_stream()>>>((const __nv_bfloat16*)dy.data_ptr(),
+                                                                  (const __nv_bfloat16*)h.data_ptr(),
+                                                                  (__nv_bfloat16*)dh.data_ptr(), T, F);
+  EMB_LAUNCH_CHECK();
+  count_launch();
+  return dh;
+}
+
+// ------------------------------------------------------------------------------------------ RoPE
+// qkv: [s, b, G, S, d] bf16; slots [0, nrot) are rotated (rotate-half pairs (i, i + d/2)); others copied.
+// cos/sin: [s, d/2] fp32.  inverse: rotate by -angle (the backward pass).
+__global__ void rope_kernel(const __nv_bfloat16* __restrict__ in, __nv_bfloat16* __restrict__ out,
+                            const float* __restrict__ cosv, const float* __restrict__ sinv, int64_t S_tok, int B,
+                            int GS, int S, int d, int nrot, int inverse) {
+  const int half = d / 2;
+  const int pv = half / 8;  // 8-pair vectors per slot
+  const int64_t n = S_tok * B * GS * pv;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    int64_t r = i / pv;
+    int v = (int)(i - r * pv);
+    int slot = (int)(r % GS) % S;
+    int64_t tok = r / GS;  // s * B + b
+    int64_t s = tok / B;
+    const __nv_bfloat16* src = in + r * d;
+    __nv_bfloat16* dst = out + r * d;
+    uint4 a = reinterpret_cast<const uint4*>(src)[v];
+    uint4 b = reinterpret_cast<const uint4*>(src + half)[v];
+    if (slot < nrot) {
+      float x1[8], x2[8], o1[8], o2[8];
+      unpack8(a, x1);
+      unpack8(b, x2);
+      const float* cp = cosv + s * half + v * 8;
+      const float* sp = sinv + s * half + v * 8;
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        float c = cp[k], sn = inverse ? -sp[k] : sp[k];
+        o1[k] = x1[k] * c - x2[k] * sn;
+        o2[k] = x2[k] * c + x1[k] * sn;
+      }
+      a = pack8(o1);
+      b = pack8(o2);
+    }
+    reinterpret_cast<uint4*>(dst)[v] = a;
+    reinterpret_cast<uint4*>(dst + half)[v] = b;
+  }
+}
+
+at::Tensor rope_fwd(at::Tensor qkv, at::Tensor cosv, at::Tensor sinv, int64_t nrot, bool inverse) {
+  check_cuda_bf16(qkv, "qkv");
+  TORCH_CHECK(qkv.dim() == 5, "qkv must be [s, b, G, slots, d]");
+  const int64_t s = qkv.size(0), b = qkv.size(1), G = qkv.size(2), S = qkv.size(3), d = qkv.size(4);
+  TORCH_CHECK(d % 16 == 0, "head dim must be a multiple of 16");
+  TORCH_CHECK(cosv.is_cuda() && cosv.scalar_type() == at::kFloat && cosv.size(0) == s && cosv.size(1) == d / 2);
+  auto out = at::empty_like(qkv);
+  int64_t n = s * b * G * S * (d / 16);
+  if (n == 0) return out;
+  rope_kernel<<<ew_grid(n), 256, 0, cur_stream()>>>((const __nv_bfloat16*)qkv.data_ptr(),
+                                                    (__nv_bfloat16*)out.data_ptr(), cosv.data_ptr<float>(),
+                                                    sinv.data_ptr<float>(), s, (int)b, (int)(G * S), (int)S, (int)d,
+                                                    (int)nrot, inverse ? 1 : 0);
+  EMB_LAUNCH_CHECK();
+  count_launch();
+  return out;
+}
+
+}  // namespace emb

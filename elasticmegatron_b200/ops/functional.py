@@ -215,10 +215,19 @@ class RMSNormFn(torch.autograd.Function):
     def backward(ctx, dy):
         x2, w, rstd = ctx.saved_tensors
         dy2 = dy.reshape(-1, dy.shape[-1]).contiguous()
+        mg = getattr(w, "main_grad", None)
         if use_native(x2):
-            dx, dw = ext().rmsnorm_bwd(dy2, x2, w, rstd)
+            # the weight gradient is reduced in fp32 straight into main_grad when the weight has one
+            dx, dw = ext().rmsnorm_bwd(dy2, x2, w, rstd, mg.view(-1) if mg is not None else None)
         else:
             dx, dw = ref.rmsnorm_bwd(dy2, x2, w, rstd)
+            if mg is not None:
+                mg.view(-1).add_(dw)
+        if mg is not None:
+            hook = getattr(w, "_grad_ready", None)
+            if hook is not None:
+                hook()
+            return dx.view(dy.shape), None, None
         return dx.view(dy.shape), dw.to(w.dtype), None
 
 
@@ -321,7 +330,26 @@ class AttentionFn(torch.autograd.Function):
         return dx.to(qkv.dtype), None
 
 
+def _has_native_attention() -> bool:
+    try:
+        return hasattr(ext(), "attn_fwd")
+    except RuntimeError:
+        return False
+
+
+def _sdpa_attention(qkv, hpg):
+    """Interim CUDA path for shapes the native attention kernel does not cover: PyTorch SDPA (library)."""
+    s, b, G, _, d = qkv.shape
+    q = qkv[:, :, :, :hpg].reshape(s, b, G * hpg, d).permute(1, 2, 0, 3)
+    k = qkv[:, :, :, hpg].permute(1, 2, 0, 3)
+    v = qkv[:, :, :, hpg + 1].permute(1, 2, 0, 3)
+    o = torch.nn.functional.scaled_dot_product_attention(q, k, v, is_causal=True, enable_gqa=hpg > 1)
+    return o.permute(2, 0, 1, 3).reshape(s, b, G * hpg * d)
+
+
 def attention(qkv, hpg):
+    if qkv.is_cuda and not _has_native_attention():
+        return _sdpa_attention(qkv, hpg)
     return AttentionFn.apply(qkv, hpg)
 
 

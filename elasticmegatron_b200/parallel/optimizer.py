@@ -91,52 +91,65 @@ class DistributedAdam:
     def step_count(self) -> int:
         return self.param_groups[0]["step"]
 
+    CHUNK = 1 << 16
+
     def _table(self, device):
+        """Segments split into chunks of at most CHUNK elements: one CTA per chunk in the native kernels."""
         if self._seg_table is None or self._seg_table.device != device:
-            arr = np.array([(a, o, n, int(wd), int(c)) for a, o, n, wd, c in self.segs], dtype=np.int64)
-            self._seg_table = torch.from_numpy(arr.reshape(-1, 5)).to(device)
+            rows = []
+            for a, o, n, wd, c in self.segs:
+                for s0 in range(0, n, self.CHUNK):
+                    k = min(self.CHUNK, n - s0)
+                    rows.append((a + s0, o + s0, k, int(wd), int(c)))
+            arr = np.array(rows, dtype=np.int64).reshape(-1, 5)
+            self._seg_table = torch.from_numpy(arr).to(device)
         return self._seg_table
 
-    def grad_norm(self) -> float:
+    def _sumsq(self) -> torch.Tensor:
+        """All-reduced sum of squares of the counted own-shard gradients, as a 1-element fp32 tensor."""
         g = self.grad_arena
         if use_native(g):
             sq = ext().seg_sumsq(g, self._table(g.device))
         else:
-            sq = torch.zeros((), dtype=torch.float64)
+            acc = torch.zeros((), dtype=torch.float64)
             for a, o, n, wd, c in self.segs:
                 if c:
-                    sq += g[a:a + n].double().pow(2).sum()
-            sq = sq.float()
-        sq = sq.reshape(1)
+                    acc += g[a:a + n].double().pow(2).sum()
+            sq = acc.float().reshape(1)
         world = self.ps.group("world")
         if world is not None and dist.get_world_size(world) > 1:
             dist.all_reduce(sq, group=world)
-        return math.sqrt(float(sq.item())) * self.grad_scale
+        return sq
 
-    def step(self) -> Tuple[bool, float]:
+    def grad_norm(self) -> float:
+        return math.sqrt(float(self._sumsq().item())) * self.grad_scale
+
+    def step(self):
+        """One AdamW step.  Returns (update_successful, grad_norm); on CUDA the norm is a device tensor and the
+        clip coefficient is applied inside the kernel, so the step does not synchronise with the host."""
         cfg = self.cfg
-        norm = self.grad_norm()
-        clip = 1.0
-        if cfg.clip_grad and cfg.clip_grad > 0:
-            clip = min(1.0, cfg.clip_grad / (norm + 1e-6))
-        if not math.isfinite(norm):
-            return False, norm
+        sq = self._sumsq()
         for g in self.param_groups:
             g["step"] += 1
         step = self.param_groups[0]["step"]
         lr = self.param_groups[0]["lr"]
         b1, b2 = cfg.adam_beta1, cfg.adam_beta2
-        gscale = self.grad_scale * clip
         O, G, P = self.opt_arena, self.grad_arena, self.param_arena
+        max_norm = float(cfg.clip_grad or 0.0)
         if use_native(O):
-            ext().adam_segments(O, G, P, self._table(O.device), lr, b1, b2, cfg.adam_eps, cfg.weight_decay,
-                                step, gscale)
-        else:
-            for a, o, n, wd, c in self.segs:
-                m, ea, es = O[0, o:o + n], O[1, o:o + n], O[2, o:o + n]
-                ref.adam_step(m, ea, es, G[a:a + n], lr, b1, b2, cfg.adam_eps, cfg.weight_decay if wd else 0.0,
-                              step, gscale)
-                P[a:a + n].copy_(m.to(P.dtype))
+            ext().adam_segments(O, G, P, self._table(O.device), lr, b1, b2, cfg.adam_eps, cfg.weight_decay, step,
+                                self.grad_scale, max_norm, sq)
+            return True, sq.sqrt() * self.grad_scale
+        norm = math.sqrt(float(sq.item())) * self.grad_scale
+        clip = 1.0
+        if max_norm > 0:
+            clip = min(1.0, max_norm / (norm + 1e-6))
+        gscale = self.grad_scale * clip
+        for a, o, n, wd, c in self.segs:
+            m, ea, es = O[0, o:o + n], O[1, o:o + n], O[2, o:o + n]
+            ref.adam_step(m, ea, es, G[a:a + n], lr, b1, b2, cfg.adam_eps, cfg.weight_decay if wd else 0.0,
+                          step, gscale)
+            P[a:a + n].copy_(m.to(P.dtype))
         return True, norm
 
     # ------------------------------------------------------------------ state

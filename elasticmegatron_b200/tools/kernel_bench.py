@@ -1,0 +1,124 @@
+"""Kernel micro-benchmarks with CUDA-event timing and roofline fractions.
+
+    python -m elasticmegatron_b200.tools.kernel_bench gemm --m 16384 --n 4096 --k 4096 --layout fprop
+    python -m elasticmegatron_b200.tools.kernel_bench all
+
+Each case runs a warm-up, then ``--iters`` timed launches bracketed by ``cuda.synchronize``, on inputs larger
+than L2 where the op is memory-bound.  Fractions are reported against the measured peaks in
+MEASURED_PEAKS.json at the repository root when present (``bf16_tflops``, ``hbm_gbs``), else the pool
+fallback (1590 TFLOP/s, 6650 GB/s).  ``--baseline`` also times the torch / cuBLAS equivalent.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+
+import torch
+
+
+def peaks():
+    p = os.path.join(os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__)))),
+                     "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return d.get("bf16_tflops", 1590.0), d.get("hbm_gbs", 6650.0), "measured"
+    return 1590.0, 6650.0, "fallback"
+
+
+def timeit(fn, iters=20, warmup=5):
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(iters):
+        fn()
+    e1.record()
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / iters
+
+
+def bench_gemm(m, n, k, layout, iters, baseline):
+    from elasticmegatron_b200.ops.native import ext
+
+    dev = "cuda"
+    if layout == "fprop":
+        a, b = torch.randn(m, k, device=dev).bfloat16(), torch.randn(n, k, device=dev).bfloat16()
+        fn = lambda: ext().gemm_tc(a, b, False, True)
+        ref = lambda: torch.matmul(a, b.t())
+    elif layout == "dgrad":
+        a, b = torch.randn(m, k, device=dev).bfloat16(), torch.randn(k, n, device=dev).bfloat16()
+        fn = lambda: ext().gemm_tc(a, b, False, False)
+        ref = lambda: torch.matmul(a, b)
+    else:
+        a, b = torch.randn(k, m, device=dev).bfloat16(), torch.randn(k, n, device=dev).bfloat16()
+        c = torch.zeros(m, n, device=dev)
+        fn = lambda: ext().gemm_tc(a, b, True, False, c, True)
+        ref = lambda: c.addmm_(a.t().float(), b.float()) if False else torch.matmul(a.t(), b)
+    ms = timeit(fn, iters)
+    tf = 2 * m * n * k / ms / 1e9
+    pk, _, src = peaks()
+    out = {"op": f"gemm_{layout}", "m": m, "n": n, "k": k, "ms": ms, "tflops": tf, "frac": tf / pk, "peak": src}
+    if baseline:
+        bms = timeit(ref, iters)
+        out.update({"cublas_ms": bms, "cublas_tflops": 2 * m * n * k / bms / 1e9})
+    return out
+
+
+def bench_mem(name, fn, nbytes, iters):
+    ms = timeit(fn, iters)
+    _, hbm, src = peaks()
+    gbs = nbytes / ms / 1e6
+    return {"op": name, "ms": ms, "gbs": gbs, "frac": gbs / hbm, "peak": src}
+
+
+def bench_elementwise(iters):
+    from elasticmegatron_b200.ops.native import ext
+
+    T, H, F = 32768, 4096, 11008
+    x = torch.randn(T, H, device="cuda").bfloat16()
+    w = torch.ones(H, device="cuda").bfloat16()
+    out = [bench_mem("rmsnorm_fwd", lambda: ext().rmsnorm_fwd(x, w, 1e-5), 2 * T * H * 2, iters)]
+    y, rstd = ext().rmsnorm_fwd(x, w, 1e-5)
+    out.append(bench_mem("rmsnorm_bwd", lambda: ext().rmsnorm_bwd(x, x, w, rstd), 3 * T * H * 2, iters))
+    h = torch.randn(8192, 2 * F, device="cuda").bfloat16()
+    out.append(bench_mem("swiglu_fwd", lambda: ext().swiglu_fwd(h), 8192 * 3 * F * 2, iters))
+    n = 1 << 28
+    O = torch.zeros(3, n, device="cuda")
+    G = torch.zeros(n, device="cuda")
+    P = torch.zeros(n, device="cuda", dtype=torch.bfloat16)
+    ch = torch.tensor([[i, i, 1 << 16, 1, 1] for i in range(0, n, 1 << 16)], device="cuda")
+    out.append(bench_mem("adam", lambda: ext().adam_segments(O, G, P, ch, 1e-4, 0.9, 0.95, 1e-8, 0.1, 1, 1.0),
+                         n * (12 + 4 + 12 + 2), iters))
+    return out
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("what", choices=["gemm", "elementwise", "all"])
+    ap.add_argument("--m", type=int, default=16384)
+    ap.add_argument("--n", type=int, default=4096)
+    ap.add_argument("--k", type=int, default=4096)
+    ap.add_argument("--layout", default="fprop")
+    ap.add_argument("--iters", type=int, default=20)
+    ap.add_argument("--baseline", action="store_true")
+    a = ap.parse_args()
+    res = []
+    if a.what == "gemm":
+        res.append(bench_gemm(a.m, a.n, a.k, a.layout, a.iters, a.baseline))
+    if a.what == "all":
+        # the Llama-2 7B training GEMMs at 4096 tokens per micro-batch
+        for (m, n, k) in ((4096, 12288, 4096), (4096, 4096, 4096), (4096, 22016, 4096), (4096, 4096, 11008),
+                          (4096, 32000, 4096)):
+            for lay in ("fprop", "dgrad", "wgrad"):
+                mm, nn, kk = (m, n, k) if lay == "fprop" else ((m, k, n) if lay == "dgrad" else (n, k, m))
+                res.append(bench_gemm(mm, nn, kk, lay, a.iters, a.baseline))
+    if a.what in ("elementwise", "all"):
+        res += bench_elementwise(a.iters)
+    for r in res:
+        print(json.dumps(r))
+
+
+if __name__ == "__main__":
+    main()

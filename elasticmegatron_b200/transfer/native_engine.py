@@ -1,0 +1,189 @@
+"""Direct peer-memory transfer engine (K1 driver).
+
+Every rank exports its state arenas (source and destination parameters / optimizer state) as CUDA IPC
+handles once; peers map them once (the mappings are cached for the life of the process and the arena pool
+reuses arenas, so repeated switches map nothing new).  For a switch each rank turns the plan's descriptors
+into 64-byte copy tasks with *device* addresses - its own arenas or a peer's mapping - and runs them all in one
+``reshard_copy`` launch.  In pull mode (default) a rank executes the copies whose destination it owns, reading
+peers over NVLink; in push mode it executes the copies whose source it owns, writing peers.
+
+Ordering: a 1-element NCCL all-reduce over the union group is issued on the compute stream before and after
+the launch.  The first guarantees every peer finished producing its source state (previous optimizer step)
+before any rank reads it; the second guarantees nobody reuses or frees a source arena while a peer may still
+be reading it.  Both are stream-ordered, so the host never blocks.
+
+This replaces the reference's three-phase, per-(parameter, tensor, peer) blocking NCCL broadcasts
+(elastic_megatron/transfer/transfer.py:291-341) and its CUDA-IPC staging clone (transfer/ipc_manager.py).
+"""
+from __future__ import annotations
+
+from typing import Dict, Optional, Tuple
+
+import numpy as np
+import torch
+import torch.distributed as dist
+
+from ..ops.native import ext
+from ..parallel.process_groups import ProcessGroupPool
+from ..planner.plan import KIND_OPT, KIND_PARAM, ReshardPlan
+
+TASK_DTYPE = np.dtype([
+    ("src", np.uint64), ("dst", np.uint64), ("src_stride", np.uint64), ("dst_stride", np.uint64),
+    ("src_plane", np.uint64), ("dst_plane", np.uint64), ("rows", np.uint32), ("row_bytes", np.uint32),
+    ("planes", np.uint32), ("flags", np.uint32),
+])
+assert TASK_DTYPE.itemsize == 64
+# staging layout while splitting (row_bytes can exceed 32 bits before the split)
+_TMP_DTYPE = np.dtype([(n, np.uint64) for n in TASK_DTYPE.names])
+
+
+def _handle_of(t: Optional[torch.Tensor]):
+    if t is None:
+        return None
+    return bytes(ext().ipc_get_handle(t).numpy().tobytes())
+
+
+class NativeP2PEngine:
+    name = "native"
+
+    def __init__(self, mode: str = "pull", task_bytes: int = 1 << 20):
+        assert mode in ("pull", "push")
+        self.mode = mode
+        self.task_bytes = task_bytes
+        self._handles: Dict[int, bytes] = {}
+        self._cache: Dict[tuple, Tuple[torch.Tensor, int, int]] = {}
+        self._flag = None
+        self.bytes_moved = 0
+
+    def reset_counters(self):
+        self.bytes_moved = 0
+
+    # ------------------------------------------------------------------ address exchange
+    def _local_handle(self, t: Optional[torch.Tensor]):
+        if t is None:
+            return None
+        k = t.data_ptr()
+        h = self._handles.get(k)
+        if h is None:
+            h = _handle_of(t)
+            self._handles[k] = h
+        return h
+
+    def _exchange(self, rank, sp, so, dp, do, union):
+        """All ranks' arena base addresses as seen from this process: {rank: (sp, so, dp, do)}."""
+        mine = (self._local_handle(sp), self._local_handle(so), self._local_handle(dp), self._local_handle(do))
+        objs = [None] * len(union)
+        dist.all_gather_object(objs, (rank, mine), group=ProcessGroupPool.get(union, "gloo"))
+        out = {}
+        local = (sp, so, dp, do)
+        for r, hs in objs:
+            if r == rank:
+                out[r] = tuple(t.data_ptr() if t is not None else 0 for t in local)
+            else:
+                out[r] = tuple(int(ext().ipc_open(torch.frombuffer(bytearray(h), dtype=torch.uint8))) if h else 0
+                               for h in hs)
+        return out
+
+    # ------------------------------------------------------------------ task building
+    def _tasks(self, plan: ReshardPlan, rank: int, addrs, el_param: int) -> np.ndarray:
+        d = plan.desc
+        sel = d["dst_rank"] == rank if self.mode == "pull" else d["src_rank"] == rank
+        d = d[sel]
+        if len(d) == 0:
+            return np.zeros(0, dtype=TASK_DTYPE)
+        is_opt = d["kind"] == KIND_OPT
+        el = np.where(is_opt, 4, el_param).astype(np.uint64)
+        src_base = np.array([addrs[int(r)][1] if o else addrs[int(r)][0] for r, o in zip(d["src_rank"], is_opt)],
+                            dtype=np.uint64)
+        dst_base = np.array([addrs[int(r)][3] if o else addrs[int(r)][2] for r, o in zip(d["dst_rank"], is_opt)],
+                            dtype=np.uint64)
+        t = np.zeros(len(d), dtype=_TMP_DTYPE)
+        t["src"] = src_base + d["src_off"].astype(np.uint64) * el
+        t["dst"] = dst_base + d["dst_off"].astype(np.uint64) * el
+        t["src_stride"] = d["src_stride"].astype(np.uint64) * el
+        t["dst_stride"] = d["dst_stride"].astype(np.uint64) * el
+        t["rows"] = d["rows"].astype(np.uint64)
+        t["row_bytes"] = d["cols"].astype(np.uint64) * el
+        t["planes"] = np.where(is_opt, 3, 1).astype(np.uint64)
+        sn = np.array(plan.src_opt_numel, dtype=np.uint64)
+        dn = np.array(plan.dst_opt_numel, dtype=np.uint64)
+        t["src_plane"] = np.where(is_opt, sn[d["src_rank"]] * 4, 0).astype(np.uint64)
+        t["dst_plane"] = np.where(is_opt, dn[d["dst_rank"]] * 4, 0).astype(np.uint64)
+        t = self._split(t)
+        aligned = ((t["src"] | t["dst"] | t["src_stride"] | t["dst_stride"] | t["src_plane"] | t["dst_plane"]
+                    | t["row_bytes"]) & np.uint64(15)) == 0
+        t["flags"] = aligned.astype(np.uint64)
+        assert (t["rows"] < (1 << 32)).all() and (t["row_bytes"] < (1 << 32)).all()
+        t = t.astype(TASK_DTYPE)
+        # big tasks first so the grid-stride assignment balances
+        size = t["rows"].astype(np.uint64) * t["row_bytes"] * t["planes"]
+        return t[np.argsort(-size.astype(np.int64), kind="stable")]
+
+    def _split(self, t: np.ndarray) -> np.ndarray:
+        out = []
+        cap = self.task_bytes
+        for r in t:
+            rows, rb, planes = int(r["rows"]), int(r["row_bytes"]), int(r["planes"])
+            total = rows * rb * planes
+            if total <= cap:
+                out.append(r)
+                continue
+            if rows > 1:
+                per = max(1, cap // max(1, rb * planes))
+                for r0 in range(0, rows, per):
+                    x = r.copy()
+                    x["rows"] = min(per, rows - r0)
+                    x["src"] = r["src"] + np.uint64(r0) * r["src_stride"]
+                    x["dst"] = r["dst"] + np.uint64(r0) * r["dst_stride"]
+                    out.append(x)
+            else:
+                per = max(16, (cap // planes) // 16 * 16)
+                for c0 in range(0, rb, per):
+                    x = r.copy()
+                    x["row_bytes"] = min(per, rb - c0)
+                    x["src"] = r["src"] + np.uint64(c0)
+                    x["dst"] = r["dst"] + np.uint64(c0)
+                    out.append(x)
+        return np.array(out, dtype=_TMP_DTYPE) if out else np.zeros(0, dtype=_TMP_DTYPE)
+
+    # ------------------------------------------------------------------ execution
+    def _barrier(self, group, device):
+        if self._flag is None or self._flag.device != device:
+            self._flag = torch.zeros(1, dtype=torch.float32, device=device)
+        if group is not None and dist.get_world_size(group) > 1:
+            dist.all_reduce(self._flag, group=group)
+
+    def prepare(self, plan: ReshardPlan, rank: int, sp, so, dp, do, group) -> Tuple[torch.Tensor, int]:
+        union = sorted(set(range(plan.src.world_size)) | set(range(plan.dst.world_size)))
+        # The exchange is collective and cheap (handles are cached, mappings too); it runs on every switch
+        # because any peer may have moved to a different pooled arena since the plan was last executed.
+        addrs = self._exchange(rank, sp, so, dp, do, union)
+        key = (id(plan), rank, tuple(sorted(addrs.items())), self.mode)
+        hit = self._cache.get(key)
+        if hit is not None:
+            return hit[0], hit[1]
+        ref = next(x for x in (dp, sp) if x is not None)
+        el_param = ref.element_size()
+        tasks = self._tasks(plan, rank, addrs, el_param)
+        dev = next(x for x in (dp, do, sp, so) if x is not None).device
+        buf = torch.from_numpy(tasks.view(np.uint8).copy()).to(dev) if len(tasks) else torch.zeros(64, dtype=torch.uint8,
+                                                                                                    device=dev)
+        nbytes = int((tasks["rows"].astype(np.int64) * tasks["row_bytes"] * tasks["planes"]).sum()) if len(tasks) else 0
+        self._cache[key] = (buf, len(tasks), nbytes)
+        return buf, len(tasks)
+
+    def warmup(self, plan, rank, src, dst, group):
+        sp = src.param_flat if src is not None and not src.model_released else None
+        so = src.opt_flat if src is not None and not src.optimizer_released else None
+        dp = dst.param_flat if dst is not None and not dst.model_released else None
+        do = dst.opt_flat if dst is not None and not dst.optimizer_released else None
+        if any(x is not None for x in (sp, so, dp, do)):
+            self.prepare(plan, rank, sp, so, dp, do, group)
+
+    def execute(self, plan: ReshardPlan, rank: int, sp, so, dp, do, group=None) -> None:
+        buf, n = self.prepare(plan, rank, sp, so, dp, do, group)
+        dev = buf.device
+        self._barrier(group, dev)
+        if n:
+            ext().reshard_copy(buf, n, 0)
+        self._barrier(group, dev)

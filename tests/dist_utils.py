@@ -14,7 +14,7 @@ def free_port() -> int:
         return s.getsockname()[1]
 
 
-def _entry(rank, world, port, fn, args, q):
+def _entry(rank, world, port, fn, args, q, backend="gloo"):
     import torch.distributed as dist
 
     os.environ["MASTER_ADDR"] = "127.0.0.1"
@@ -25,7 +25,12 @@ def _entry(rank, world, port, fn, args, q):
         import torch
 
         torch.set_num_threads(max(1, (os.cpu_count() or 2) // world))
-        dist.init_process_group("gloo", rank=rank, world_size=world)
+        if backend == "nccl":
+            torch.cuda.set_device(rank)
+            os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+        import datetime
+
+        dist.init_process_group(backend, rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120))
         res = fn(rank, world, *args)
         q.put((rank, "ok", res))
         dist.barrier()
@@ -35,11 +40,11 @@ def _entry(rank, world, port, fn, args, q):
         raise
 
 
-def run_distributed(fn, world: int, *args, timeout: float = 600.0):
+def run_distributed(fn, world: int, *args, timeout: float = 600.0, backend: str = "gloo"):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = free_port()
-    procs = [ctx.Process(target=_entry, args=(r, world, port, fn, args, q)) for r in range(world)]
+    procs = [ctx.Process(target=_entry, args=(r, world, port, fn, args, q, backend)) for r in range(world)]
     for p in procs:
         p.start()
     results = {}

@@ -1,0 +1,48 @@
+"""tcgen05 GEMM against an fp32 torch reference, for the fprop / dgrad / wgrad operand layouts."""
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def _ext():
+    from elasticmegatron_b200.ops.native import ext
+
+    return ext()
+
+
+SHAPES = [(128, 256, 64), (256, 512, 128), (300, 520, 200), (1024, 4096, 4096), (4096, 1024, 512), (8, 8, 8)]
+
+
+@pytest.mark.parametrize("M,N,K", SHAPES)
+@pytest.mark.parametrize("layout", ["fprop", "dgrad", "wgrad"])
+def test_gemm_layouts(M, N, K, layout):
+    torch.manual_seed(0)
+    dev = "cuda"
+    if layout == "fprop":  # a [M,K], b [N,K], trans_b
+        a = torch.randn(M, K, device=dev).bfloat16()
+        b = torch.randn(N, K, device=dev).bfloat16()
+        out = _ext().gemm_tc(a, b, False, True)
+        exp = a.float() @ b.float().t()
+    elif layout == "dgrad":  # a [M,K], b [K,N]
+        a = torch.randn(M, K, device=dev).bfloat16()
+        b = torch.randn(K, N, device=dev).bfloat16()
+        out = _ext().gemm_tc(a, b, False, False)
+        exp = a.float() @ b.float()
+    else:  # a [K,M] (trans_a), b [K,N]; accumulate into fp32
+        a = torch.randn(K, M, device=dev).bfloat16()
+        b = torch.randn(K, N, device=dev).bfloat16()
+        c = torch.ones(M, N, device=dev)
+        out = _ext().gemm_tc(a, b, True, False, c, True)
+        exp = a.float().t() @ b.float() + 1
+    torch.cuda.synchronize()
+    tol = 2e-2 * (K ** 0.5)
+    torch.testing.assert_close(out.float(), exp, atol=tol, rtol=2e-2)
+
+
+def test_gemm_fp32_out_store():
+    a = torch.randn(256, 128, device="cuda").bfloat16()
+    b = torch.randn(512, 128, device="cuda").bfloat16()
+    c = torch.full((256, 512), 7.0, device="cuda")
+    _ext().gemm_tc(a, b, False, True, c, False)
+    torch.testing.assert_close(c, a.float() @ b.float().t(), atol=0.3, rtol=2e-2)

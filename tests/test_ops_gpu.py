@@ -1,0 +1,122 @@
+"""Numerics of the native sm_100a kernels against plain PyTorch fp32 references."""
+import math
+
+import pytest
+import torch
+
+from elasticmegatron_b200.ops import reference as ref
+
+pytestmark = pytest.mark.gpu
+
+
+def _ext():
+    from elasticmegatron_b200.ops.native import ext
+
+    return ext()
+
+
+def _close(a, b, atol, rtol):
+    torch.testing.assert_close(a.float(), b.float(), atol=atol, rtol=rtol)
+
+
+@pytest.mark.parametrize("T,H", [(257, 512), (1024, 4096), (64, 5120)])
+def test_rmsnorm(T, H):
+    torch.manual_seed(0)
+    x = torch.randn(T, H, device="cuda").bfloat16()
+    w = (1 + 0.1 * torch.randn(H, device="cuda")).bfloat16()
+    y, rstd = _ext().rmsnorm_fwd(x, w, 1e-5)
+    y_ref, rstd_ref = ref.rmsnorm_fwd(x.float(), w.float(), 1e-5)
+    _close(y, y_ref, 2e-2, 2e-2)
+    _close(rstd, rstd_ref, 1e-4, 1e-4)
+    dy = torch.randn(T, H, device="cuda").bfloat16()
+    dx, dw = _ext().rmsnorm_bwd(dy, x, w, rstd)
+    dx_ref, dw_ref = ref.rmsnorm_bwd(dy.float(), x.float(), w.float(), rstd_ref)
+    _close(dx, dx_ref, 3e-2, 3e-2)
+    _close(dw, dw_ref, 5e-2 * math.sqrt(T / 64), 1e-2)
+    acc = torch.ones(H, device="cuda")
+    _ext().rmsnorm_bwd(dy, x, w, rstd, acc)
+    _close(acc, dw_ref + 1, 5e-2 * math.sqrt(T / 64), 1e-2)
+
+
+def test_swiglu():
+    torch.manual_seed(0)
+    h = torch.randn(333, 2 * 1376, device="cuda").bfloat16()
+    _close(_ext().swiglu_fwd(h), ref.swiglu_fwd(h.float()), 2e-2, 2e-2)
+    dy = torch.randn(333, 1376, device="cuda").bfloat16()
+    _close(_ext().swiglu_bwd(dy, h), ref.swiglu_bwd(dy.float(), h.float()), 3e-2, 3e-2)
+
+
+@pytest.mark.parametrize("inverse", [False, True])
+def test_rope(inverse):
+    torch.manual_seed(0)
+    s, b, G, hpg, d = 64, 2, 4, 2, 128
+    qkv = torch.randn(s, b, G, hpg + 2, d, device="cuda").bfloat16()
+    cos, sin = ref.rope_cos_sin(torch.arange(s), d, 10000.0)
+    cos, sin = cos.cuda(), sin.cuda()
+    out = _ext().rope_fwd(qkv, cos, sin, hpg + 1, inverse)
+    exp = qkv.float().clone()
+    x = exp[:, :, :, :hpg + 1].reshape(s, b, -1, d)
+    exp[:, :, :, :hpg + 1] = ref.rope_apply(x, cos, sin, inverse).view(s, b, G, hpg + 1, d)
+    _close(out, exp, 2e-2, 2e-2)
+
+
+def test_cross_entropy_pieces():
+    torch.manual_seed(0)
+    T, V, vs = 300, 1024, 512
+    logits = (3 * torch.randn(T, V, device="cuda")).bfloat16()
+    labels = torch.randint(0, 2048, (T,), device="cuda")
+    lmax = _ext().ce_local_max(logits)
+    _close(lmax, logits.float().max(-1).values, 0, 0)
+    st = _ext().ce_local_stats(logits, labels, lmax, vs)
+    lf = logits.float()
+    se = torch.exp(lf - lmax[:, None]).sum(-1)
+    _close(st[0], se, 1e-3, 1e-4)
+    loc = labels - vs
+    inr = (loc >= 0) & (loc < V)
+    tgt = torch.where(inr, lf.gather(1, loc.clamp(0, V - 1)[:, None]).squeeze(1) - lmax, torch.zeros_like(lmax))
+    _close(st[1], tgt, 1e-5, 1e-5)
+    dl = torch.rand(T, device="cuda")
+    d = _ext().ce_bwd(logits, labels, lmax, se, dl, vs)
+    p = torch.exp(lf - lmax[:, None]) / se[:, None]
+    rows = torch.nonzero(inr).squeeze(1)
+    p[rows, loc[rows]] -= 1
+    _close(d, p * dl[:, None], 1e-2, 1e-2)
+
+
+def test_embedding():
+    torch.manual_seed(0)
+    V, H, T, vs = 100, 256, 500, 50
+    w = torch.randn(V, H, device="cuda").bfloat16()
+    ids = torch.randint(0, 200, (T,), device="cuda")
+    out = _ext().embedding_fwd(ids, w, vs)
+    loc = ids - vs
+    m = (loc >= 0) & (loc < V)
+    exp = torch.zeros(T, H, device="cuda")
+    exp[m] = w.float()[loc[m]]
+    _close(out, exp, 0, 0)
+    dy = torch.randn(T, H, device="cuda").bfloat16()
+    tgt = torch.zeros(V, H, device="cuda")
+    _ext().embedding_bwd(ids, dy, tgt, vs)
+    ref_t = torch.zeros(V, H, device="cuda").index_add_(0, loc[m], dy.float()[m])
+    _close(tgt, ref_t, 1e-4, 1e-4)
+
+
+def test_adam_and_sumsq():
+    torch.manual_seed(0)
+    n = 70000
+    O = torch.randn(3, n, device="cuda")
+    O[2].abs_()
+    G = torch.randn(n, device="cuda")
+    P = torch.empty(n, device="cuda", dtype=torch.bfloat16)
+    chunks = torch.tensor([[0, 0, 40000, 1, 1], [40000, 40000, 30000, 0, 0]], device="cuda")
+    sq = _ext().seg_sumsq(G, chunks)
+    _close(sq, (G[:40000].double() ** 2).sum().float().reshape(1), 1e-2, 1e-5)
+    O_ref = O.clone()
+    _ext().adam_segments(O, G, P, chunks, 1e-3, 0.9, 0.95, 1e-8, 0.1, 3, 0.5, 1.0, sq)
+    norm = math.sqrt(float(sq)) * 0.5
+    clip = min(1.0, 1.0 / (norm + 1e-6))
+    for a, o, k, wd in ((0, 0, 40000, 0.1), (40000, 40000, 30000, 0.0)):
+        m, e1, e2 = O_ref[0, o:o + k], O_ref[1, o:o + k], O_ref[2, o:o + k]
+        ref.adam_step(m, e1, e2, G[a:a + k], 1e-3, 0.9, 0.95, 1e-8, wd, 3, 0.5 * clip)
+    _close(O, O_ref, 1e-6, 1e-5)
+    _close(P, O_ref[0], 1e-2, 1e-2)
