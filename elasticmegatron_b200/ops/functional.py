@@ -371,7 +371,7 @@ class VocabParallelCE(torch.autograd.Function):
             stats = ext().ce_local_stats(logits, labels, lmax, vocab_start)  # [2, T]: sumexp, target
             if group is not None and dist.get_world_size(group) > 1:
                 dist.all_reduce(stats, group=group)
-            loss = torch.log(stats[0]) + lmax - stats[1]
+            loss = torch.log(stats[0]) - stats[1]  # stats[1] = target logit - global max
             ctx.save_for_backward(logits, labels, lmax, stats[0])
             ctx.vocab_start = vocab_start
             return loss

@@ -24,6 +24,8 @@ from ..planner.layout import BufferLayout, RankLayout
 
 def _rs_inplace(buf: torch.Tensor, shard_index: int, group) -> None:
     """Reduce-scatter (SUM) ``buf`` over ``group``; shard ``shard_index`` of ``buf`` receives the result."""
+    if group is None:
+        return
     n = dist.get_world_size(group)
     if n == 1:
         return
@@ -35,6 +37,8 @@ def _rs_inplace(buf: torch.Tensor, shard_index: int, group) -> None:
 
 
 def _ag_inplace(buf: torch.Tensor, shard_index: int, group) -> None:
+    if group is None:
+        return
     n = dist.get_world_size(group)
     if n == 1:
         return

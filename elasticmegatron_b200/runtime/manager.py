@@ -215,6 +215,8 @@ class ElasticMegatronManager:
         timer = DeviceTimer() if torch.cuda.is_available() else HostTimer(sync=False)
         with timer:
             eng.execute(plan, self._rank, sp, so, dp, do, ugroup)
+            if not getattr(eng, "moves_params", True) and dst is not None:
+                dst.update_model_weight()
         d = plan.desc
         el_p = torch.finfo(get_args().model.torch_dtype).bits // 8
         mine = d[((d["src_rank"] == self._rank) | (d["dst_rank"] == self._rank)) & (d["src_rank"] != d["dst_rank"])]

@@ -1,0 +1,179 @@
+"""The reference's transfer *algorithm*, re-implemented on this framework's layouts (NCCL / Gloo baseline).
+
+This is not the reference's own build (that needs Megatron-LM); it reproduces its communication schedule
+so a same-box baseline exists for the reshard latency metric (elastic_megatron/transfer/transfer.py:143-341):
+
+1. **pre** - for every virtual parameter, every ZeRO shard of each source TP shard is sent to the *aligned*
+   source rank (the lowest shard index holding part of it), which assembles the padded full TP-local fp32
+   master / exp_avg / exp_avg_sq;
+2. **main** - each aligned source rank sends every destination TP chunk that overlaps its TP shard to the
+   aligned destination rank, which assembles the full destination TP-local tensors; TP-replicated
+   parameters go from the TP-rank-0 copy to every destination TP rank (resharding_tp.py:119-139);
+3. **post** - the aligned destination rank scatters each destination ZeRO shard to its owner;
+
+every (parameter, tensor, peer) exchange is its own blocking point-to-point call, in a fixed global order.
+Afterwards the bf16 parameters are regenerated from the master of the own shard and all-gathered over DP
+(``TrainingState.update_model_weight``, training_state.py:176-197); the manager does that because this
+engine sets ``moves_params = False``.
+"""
+from __future__ import annotations
+
+from typing import Dict, List
+
+import torch
+import torch.distributed as dist
+
+from ..config import get_args
+from ..planner.layout import virtual_params
+from ..planner.plan import ReshardPlan, _StrategyView, _intersect
+
+
+def _numel(shape):
+    n = 1
+    for s in shape:
+        n *= s
+    return n
+
+
+class ReferenceAlgorithmEngine:
+    name = "reference_algorithm"
+    moves_params = False
+
+    def __init__(self):
+        self.bytes_sent = 0
+
+    def reset_counters(self):
+        self.bytes_sent = 0
+
+    def execute(self, plan: ReshardPlan, rank: int, sp, so, dp, do, group=None) -> None:
+        args = get_args()
+        cfg, tc = args.model, args.train
+        sv = _StrategyView(cfg, plan.src, tc.overlap_grad_reduce, tc.ddp_bucket_size)
+        dv = _StrategyView(cfg, plan.dst, tc.overlap_grad_reduce, tc.ddp_bucket_size)
+        dev = (so if so is not None else do).device
+        for vp in virtual_params(cfg):
+            src_groups = self._tp_groups(sv, vp, sv.holders(vp), True)
+            dst_groups = self._tp_groups(dv, vp, dv.holders(vp), False)
+            full_src: Dict[int, torch.Tensor] = {}
+            # pre: gather ZeRO shards onto the aligned source rank of each TP shard
+            for key, ranks in sorted(src_groups.items()):
+                aligned = ranks[0]
+                shape = sv.layouts[aligned].vp_loc[vp.index][1]
+                if rank == aligned:
+                    full_src[key] = torch.zeros((3, _numel(shape)), dtype=torch.float32, device=dev)
+                for r in ranks:
+                    self._gather_piece(sv, vp, r, aligned, rank, so, full_src.get(key), dev)
+            # main: aligned src -> aligned dst per overlapping TP chunk
+            full_dst: Dict[int, torch.Tensor] = {}
+            for dkey, dranks in sorted(dst_groups.items()):
+                dal = dranks[0]
+                dshape = dv.layouts[dal].vp_loc[vp.index][1]
+                if rank == dal:
+                    full_dst[dkey] = torch.zeros((3, _numel(dshape)), dtype=torch.float32, device=dev)
+                dpieces = dv.param_pieces(vp, dal)
+                for skey, sranks in sorted(src_groups.items()):
+                    sal = sranks[0]
+                    self._move_boxes(sal, dal, sv.param_pieces(vp, sal), dpieces, rank, full_src.get(skey),
+                                     full_dst.get(dkey), sv.layouts[sal].vp_loc[vp.index][0],
+                                     dv.layouts[dal].vp_loc[vp.index][0], dev)
+            # post: scatter from the aligned destination rank to every ZeRO owner
+            for dkey, dranks in sorted(dst_groups.items()):
+                for r in dranks:
+                    self._scatter_piece(dv, vp, r, dranks[0], rank, do, full_dst.get(dkey), dev)
+        if dev.type == "cuda":
+            torch.cuda.synchronize()
+
+    # ------------------------------------------------------------------ helpers
+    @staticmethod
+    def _tp_groups(view, vp, holders, is_src: bool) -> Dict[int, List[int]]:
+        """Ranks holding each TP shard (instance 0 only), ordered by ZeRO shard index."""
+        out: Dict[int, List[int]] = {}
+        for r in holders:
+            if view.layouts[r].instance != 0:
+                continue
+            c = view.coords[r]
+            out.setdefault(c["etp"] if vp.is_expert else c["tp"], []).append(r)
+        for t in out:
+            out[t].sort(key=lambda r: (view.layouts[r].expert_shard_index if vp.is_expert
+                                       else view.layouts[r].dense_shard_index, r))
+        if vp.tp_dim is None and is_src:
+            out = {0: out.get(0, [])}
+        return out
+
+    @staticmethod
+    def _owned_ranges(view, vp, r):
+        rl = view.layouts[r]
+        P, shape = rl.vp_loc[vp.index]
+        n = _numel(shape)
+        out = []
+        for s, e, o in rl.owned():
+            lo, hi = max(s, P), min(e, P + n)
+            if lo < hi:
+                out.append((lo - P, hi - P, o + (lo - s)))
+        return out
+
+    def _p2p(self, t: torch.Tensor, src: int, dst: int, rank: int):
+        if src == dst:
+            return
+        if rank == src:
+            dist.send(t.contiguous(), dst)
+            self.bytes_sent += t.numel() * t.element_size()
+        elif rank == dst:
+            dist.recv(t, src)
+
+    def _gather_piece(self, view, vp, r, aligned, rank, opt, full, dev):
+        for f0, f1, o in self._owned_ranges(view, vp, r):
+            n = f1 - f0
+            for k in range(3):
+                if r == aligned:
+                    if rank == r:
+                        full[k, f0:f1].copy_(opt[k, o:o + n])
+                    continue
+                if rank == r:
+                    self._p2p(opt[k, o:o + n], r, aligned, rank)
+                elif rank == aligned:
+                    buf = torch.empty(n, dtype=torch.float32, device=dev)
+                    self._p2p(buf, r, aligned, rank)
+                    full[k, f0:f1].copy_(buf)
+
+    def _scatter_piece(self, view, vp, r, aligned, rank, opt, full, dev):
+        for f0, f1, o in self._owned_ranges(view, vp, r):
+            n = f1 - f0
+            for k in range(3):
+                if r == aligned:
+                    if rank == r:
+                        opt[k, o:o + n].copy_(full[k, f0:f1])
+                    continue
+                if rank == aligned:
+                    self._p2p(full[k, f0:f1].contiguous(), aligned, r, rank)
+                elif rank == r:
+                    buf = torch.empty(n, dtype=torch.float32, device=dev)
+                    self._p2p(buf, aligned, r, rank)
+                    opt[k, o:o + n].copy_(buf)
+
+    def _move_boxes(self, sal, dal, spieces, dpieces, rank, sfull, dfull, sbase, dbase, dev):
+        for spc in spieces:
+            for dpc in dpieces:
+                box = _intersect(spc, dpc)
+                if box is None:
+                    continue
+                r0, r1, c0, c1 = box
+                rows, cols = r1 - r0, c1 - c0
+                so = spc.off(r0, c0) - sbase
+                do = dpc.off(r0, c0) - dbase
+                for k in range(3):
+                    src = dst = None
+                    if rank == sal:
+                        src = sfull[k].as_strided((rows, cols), (spc.ld, 1), sfull[k].storage_offset() + so)
+                    if rank == dal:
+                        dst = dfull[k].as_strided((rows, cols), (dpc.ld, 1), dfull[k].storage_offset() + do)
+                    if sal == dal:
+                        if rank == sal:
+                            dst.copy_(src)
+                        continue
+                    if rank == sal:
+                        self._p2p(src.contiguous(), sal, dal, rank)
+                    elif rank == dal:
+                        buf = torch.empty((rows, cols), dtype=torch.float32, device=dev)
+                        self._p2p(buf, sal, dal, rank)
+                        dst.copy_(buf)

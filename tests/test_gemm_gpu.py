@@ -11,7 +11,8 @@ def _ext():
     return ext()
 
 
-SHAPES = [(128, 256, 64), (256, 512, 128), (300, 520, 200), (1024, 4096, 4096), (4096, 1024, 512), (8, 8, 8)]
+SHAPES = [(128, 256, 64), (256, 512, 128), (296, 520, 200), (1024, 4096, 4096), (4096, 1024, 512), (8, 8, 8),
+          (136, 264, 72)]
 
 
 @pytest.mark.parametrize("M,N,K", SHAPES)
@@ -46,3 +47,12 @@ def test_gemm_fp32_out_store():
     c = torch.full((256, 512), 7.0, device="cuda")
     _ext().gemm_tc(a, b, False, True, c, False)
     torch.testing.assert_close(c, a.float() @ b.float().t(), atol=0.3, rtol=2e-2)
+
+
+def test_gemm_unaligned_falls_back():
+    """Operands whose leading dimension breaks the 16-byte TMA stride rule take the library path."""
+    a = torch.randn(200, 300, device="cuda").bfloat16()
+    b = torch.randn(200, 520, device="cuda").bfloat16()
+    assert not _ext().gemm_tc_supported(a, b, True, False)
+    out = _ext().gemm(a, b, True, False)
+    torch.testing.assert_close(out.float(), a.float().t() @ b.float(), atol=0.5, rtol=2e-2)
