@@ -315,3 +315,71 @@ at::Tensor rope_fwd(at::Tensor qkv, at::Tensor cosv, at::Tensor sinv, int64_t nr
 }
 
 }  // namespace emb
+
+// ------------------------------------------------------------------------------------------ allocation-free
+// RMSNorm backward for callers that cannot allocate device memory (see csrc/include/noalloc.h): the per-CTA
+// weight-gradient partials go to a fixed file-scope device array instead of a per-call allocation.
+#include "../include/noalloc.h"
+
+#include <cstdio>
+#include <mutex>
+
+namespace emb {
+namespace {
+
+static __device__ __align__(256) float g_noalloc_scratch[EMB_NOALLOC_SCRATCH_FLOATS];
+
+constexpr int kMaxDevices = 64;
+float* g_scratch_ptr[kMaxDevices] = {nullptr};
+std::mutex g_scratch_mu;
+
+// Device address of the scratch array for the current device (looked up once per device).
+cudaError_t scratch_for_current_device(float** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
+  std::lock_guard<std::mutex> g(g_scratch_mu);
+  if (g_scratch_ptr[dev] == nullptr) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess) return e;
+    g_scratch_ptr[dev] = static_cast<float*>(p);
+  }
+  *out = g_scratch_ptr[dev];
+  return cudaSuccess;
+}
+
+}  // namespace
+}  // namespace emb
+
+extern "C" int emb_rmsnorm_bwd_noalloc(const void* dy, const void* x, const void* w, const float* rstd, void* dx,
+                                       float* dw, int64_t T, int64_t H, int accumulate, cudaStream_t stream) {
+  using namespace emb;
+  if (T < 0 || H <= 0 || H % 8 != 0 || H > 8 * 4 * 1024 || H > EMB_NOALLOC_SCRATCH_FLOATS) {
+    std::fprintf(stderr,
+                 "emb_rmsnorm_bwd_noalloc: unsupported shape T=%lld H=%lld (need H %% 8 == 0, 0 < H <= 32768)\n",
+                 (long long)T, (long long)H);
+    return EMB_NOALLOC_EBADSIZE;
+  }
+  if (T == 0) return 0;
+  float* scratch = nullptr;
+  cudaError_t e = scratch_for_current_device(&scratch);
+  if (e != cudaSuccess) return (int)e;
+  int vpt;
+  const int threads = pick_threads((int)(H / 8), vpt);
+  int64_t grid = std::min<int64_t>(T, (int64_t)num_sms() * 2);
+  grid = std::min<int64_t>(grid, EMB_NOALLOC_SCRATCH_FLOATS / H);
+  if (grid < 1) grid = 1;
+  const __nv_bfloat16* dyp = static_cast<const __nv_bfloat16*>(dy);
+  const __nv_bfloat16* xp = static_cast<const __nv_bfloat16*>(x);
+  const __nv_bfloat16* wp = static_cast<const __nv_bfloat16*>(w);
+  __nv_bfloat16* dxp = static_cast<__nv_bfloat16*>(dx);
+#define L(V) rmsnorm_bwd_kernel<V><<<(int)grid, threads, 0, stream>>>(dyp, xp, wp, rstd, dxp, scratch, (int)T, (int)H)
+  if (vpt <= 1) L(1); else if (vpt == 2) L(2); else if (vpt == 3) L(3); else L(4);
+#undef L
+  colsum_kernel<<<(int)((H + 255) / 256), 256, 0, stream>>>(scratch, dw, (int)grid, (int)H, accumulate ? 1 : 0);
+  e = cudaGetLastError();
+  count_launch(2);
+  return (int)e;
+}
