@@ -30,7 +30,7 @@ int64_t copy_task_bytes();
 torch::Tensor gemm(torch::Tensor a, torch::Tensor b, bool trans_a, bool trans_b, c10::optional<torch::Tensor> out,
                    bool accumulate);
 torch::Tensor gemm_tc(torch::Tensor a, torch::Tensor b, bool trans_a, bool trans_b, c10::optional<torch::Tensor> out,
-                      bool accumulate);
+                      bool accumulate, int64_t variant);
 bool gemm_tc_supported(torch::Tensor a, torch::Tensor b, bool trans_a, bool trans_b, c10::optional<torch::Tensor> out,
                        bool accumulate);
 }  // namespace emb
@@ -64,7 +64,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm", &gemm, py::arg("a"), py::arg("b"), py::arg("trans_a") = false, py::arg("trans_b") = false,
         py::arg("out") = py::none(), py::arg("accumulate") = false);
   m.def("gemm_tc", &gemm_tc, py::arg("a"), py::arg("b"), py::arg("trans_a") = false, py::arg("trans_b") = false,
-        py::arg("out") = py::none(), py::arg("accumulate") = false);
+        py::arg("out") = py::none(), py::arg("accumulate") = false, py::arg("variant") = 0);
   m.def("gemm_tc_supported", &gemm_tc_supported, py::arg("a"), py::arg("b"), py::arg("trans_a") = false,
         py::arg("trans_b") = false, py::arg("out") = py::none(), py::arg("accumulate") = false);
 }

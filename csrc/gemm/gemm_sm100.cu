@@ -318,6 +318,258 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   }
 }
 
+}  // namespace gk
+
+// ------------------------------------------------------------------------------------------ 2-SM variant
+// A cluster of two CTAs on two SMs computes a 256x256 tile with tcgen05.mma.cta_group::2 (M=256, N=256):
+// CTA r loads rows [128r, 128r+128) of the A tile and rows [128r, 128r+128) of the B tile (N-half) into its
+// own shared memory, so each SM streams 32 KiB per 64-deep k-block instead of 48 KiB for the same MMA work,
+// and each SM's TMEM holds its 128 rows x 256 columns of the accumulator.  Protocol:
+//   full[s]   - leader CTA only; its producer arms it with the bytes of both CTAs; both CTAs' TMA loads
+//               complete on it (cta_group::2 form, barrier addressed in the leader through mapa);
+//   empty[s]  - in both CTAs; the leader's MMA commit arrives on both (multicast to the pair, mask 0b11);
+//   tfull[b]  - in both CTAs; the leader's commit after the last k-block of a tile arrives on both;
+//   tempty[b] - leader only; all 8 epilogue warps of the pair arrive (remote arrive from the peer).
+// TMA loads never use cluster multicast.
+namespace gk2 {
+constexpr int BM = 256, BN = 256, BK = 64, STAGES = 6;
+constexpr int A_HALF = 128 * BK * 2;  // 16 KiB per CTA
+constexpr int B_HALF = 128 * BK * 2;  // 16 KiB per CTA
+constexpr int STAGE_BYTES = A_HALF + B_HALF;
+constexpr int TMEM_COLS = 512;
+constexpr int NUM_THREADS = 192;
+constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 256;
+
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ uint32_t mapa(uint32_t addr, uint32_t cta) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(cta));
+  return r;
+}
+__device__ __forceinline__ void remote_arrive(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+__device__ __forceinline__ void tma_load_2d_pair(void* smem_dst, const CUtensorMap* map, uint32_t bar_cluster, int x,
+                                                 int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], "
+      "[%4];" ::"r"(gk::smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar_cluster)
+      : "memory");
+}
+__device__ __forceinline__ void mma_pair(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                         uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate));
+}
+__device__ __forceinline__ void commit_pair(uint64_t* bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
+          gk::smem_u32(bar)),
+      "h"((uint16_t)0x3)
+      : "memory");
+}
+__host__ __device__ constexpr uint32_t make_idesc2(bool a_mn, bool b_mn) {
+  return (1u << 4) | (1u << 7) | (1u << 10) | ((a_mn ? 1u : 0u) << 15) | ((b_mn ? 1u : 0u) << 16) |
+         ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+}
+
+__global__ void __launch_bounds__(NUM_THREADS, 1)
+    gemm2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, gk::Params p) {
+  using namespace gk;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + STAGES * A_HALF;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
+  uint64_t* empty = full + STAGES;
+  uint64_t* tfull = empty + STAGES;  // [2]
+  uint64_t* tempty = tfull + 2;      // [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_rank();
+  const bool leader = rank == 0;
+  const int cluster_id = blockIdx.x >> 1;
+  const int num_clusters = gridDim.x >> 1;
+  const int tiles_m = (p.M + BM - 1) / BM;
+  const int tiles_n = (p.N + BN - 1) / BN;
+  const int num_tiles = tiles_m * tiles_n;
+  const int nk = (p.K + BK - 1) / BK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tfull[b], 1);
+      mbar_init(&tempty[b], 8);
+    }
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(TMEM_COLS));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;");
+  }
+  tc_fence_before();
+  cluster_sync();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int it = 0;
+      bool ok = true;
+      for (int t = cluster_id; t < num_tiles && ok; t += num_clusters) {
+        const int m0 = (t % tiles_m) * BM + 128 * rank;
+        const int n0 = (t / tiles_m) * BN + 128 * rank;
+        for (int kb = 0; kb < nk; ++kb, ++it) {
+          const int s = it % STAGES;
+          const uint32_t ph = (it / STAGES) & 1;
+          if (!mbar_wait(&empty[s], ph ^ 1, p.err, 11) || *abort_flag) { ok = false; *abort_flag = 1; break; }
+          const uint32_t bar = mapa(smem_u32(&full[s]), 0);
+          if (leader) mbar_expect_tx(&full[s], 2 * STAGE_BYTES);
+          uint8_t* a_dst = sA + s * A_HALF;
+          uint8_t* b_dst = sB + s * B_HALF;
+          const int k0 = kb * BK;
+          if (!p.a_mn) {
+            tma_load_2d_pair(a_dst, &tmA, bar, k0, m0);
+          } else {
+            tma_load_2d_pair(a_dst, &tmA, bar, m0, k0);
+            tma_load_2d_pair(a_dst + 8192, &tmA, bar, m0 + 64, k0);
+          }
+          if (!p.b_mn) {
+            tma_load_2d_pair(b_dst, &tmB, bar, k0, n0);
+          } else {
+            tma_load_2d_pair(b_dst, &tmB, bar, n0, k0);
+            tma_load_2d_pair(b_dst + 8192, &tmB, bar, n0 + 64, k0);
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (leader && lane == 0) {
+      const uint32_t idesc = make_idesc2(p.a_mn, p.b_mn);
+      const uint32_t a_lbo = p.a_mn ? 8192 : 16, a_step = p.a_mn ? 2048 : 32;
+      const uint32_t b_lbo = p.b_mn ? 8192 : 16, b_step = p.b_mn ? 2048 : 32;
+      int it = 0, local = 0;
+      bool ok = true;
+      for (int t = cluster_id; t < num_tiles && ok; t += num_clusters, ++local) {
+        const int buf = local & 1;
+        const uint32_t tph = (local >> 1) & 1;
+        if (!mbar_wait(&tempty[buf], tph ^ 1, p.err, 12) || *abort_flag) { ok = false; *abort_flag = 1; break; }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + buf * BN;
+        for (int kb = 0; kb < nk; ++kb, ++it) {
+          const int s = it % STAGES;
+          const uint32_t ph = (it / STAGES) & 1;
+          if (!mbar_wait(&full[s], ph, p.err, 13) || *abort_flag) { ok = false; *abort_flag = 1; break; }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(sA + s * A_HALF);
+          const uint32_t b_addr = smem_u32(sB + s * B_HALF);
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k) {
+            mma_pair(d_tmem, smem_desc(a_addr + k * a_step, a_lbo, 1024), smem_desc(b_addr + k * b_step, b_lbo, 1024),
+                     idesc, (kb | k) != 0);
+          }
+          commit_pair(&empty[s]);
+        }
+        if (ok) commit_pair(&tfull[buf]);
+      }
+    }
+  } else {
+    const int quarter = warp & 3;
+    const int row_in_half = quarter * 32 + lane;
+    int local = 0;
+    for (int t = cluster_id; t < num_tiles; t += num_clusters, ++local) {
+      const int buf = local & 1;
+      const uint32_t tph = (local >> 1) & 1;
+      if (!mbar_wait(&tfull[buf], tph, p.err, 14) || *abort_flag) { *abort_flag = 1; break; }
+      tc_fence_after();
+      const int row = (t % tiles_m) * BM + 128 * rank + row_in_half;
+      const int n0 = (t / tiles_m) * BN;
+      const bool row_ok = row < p.M;
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; ++c) {
+        uint32_t r[32];
+        const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + buf * BN + c * 32;
+        TMEM_LD_32(taddr, r);
+        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+        const int col0 = n0 + c * 32;
+        if (!row_ok || col0 >= p.N) continue;
+        const int ncols = min(32, p.N - col0);
+        if (p.out_fp32) {
+          float* dst = reinterpret_cast<float*>(p.C) + (size_t)row * p.ldc + col0;
+          if (ncols == 32 && ((reinterpret_cast<uintptr_t>(dst) & 15) == 0)) {
+#pragma unroll
+            for (int v = 0; v < 8; ++v) {
+              float4 o = make_float4(__uint_as_float(r[4 * v]), __uint_as_float(r[4 * v + 1]),
+                                     __uint_as_float(r[4 * v + 2]), __uint_as_float(r[4 * v + 3]));
+              float4* d4 = reinterpret_cast<float4*>(dst) + v;
+              if (p.accumulate) {
+                float4 old = *d4;
+                o.x += old.x; o.y += old.y; o.z += old.z; o.w += old.w;
+              }
+              *d4 = o;
+            }
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              if (j < ncols) {
+                float v = __uint_as_float(r[j]);
+                dst[j] = p.accumulate ? dst[j] + v : v;
+              }
+            }
+          }
+        } else {
+          __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(p.C) + (size_t)row * p.ldc + col0;
+          if (ncols == 32 && ((reinterpret_cast<uintptr_t>(dst) & 15) == 0)) {
+#pragma unroll
+            for (int v = 0; v < 4; ++v) {
+              float f[8];
+#pragma unroll
+              for (int j = 0; j < 8; ++j) f[j] = __uint_as_float(r[8 * v + j]);
+              reinterpret_cast<uint4*>(dst)[v] = pack8(f);
+            }
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              if (j < ncols) dst[j] = __float2bfloat16_rn(__uint_as_float(r[j]));
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) remote_arrive(mapa(smem_u32(&tempty[buf]), 0));
+    }
+  }
+
+  tc_fence_before();
+  cluster_sync();
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(TMEM_COLS));
+  }
+}
+}  // namespace gk2
+
+namespace gk {
 // ------------------------------------------------------------------------------------------ host side
 static PFN_cuTensorMapEncodeTiled_v12000 get_encode() {
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
@@ -378,7 +630,7 @@ bool gemm_tc_supported(at::Tensor a, at::Tensor b, bool trans_a, bool trans_b, c
 }
 
 at::Tensor gemm_tc(at::Tensor a, at::Tensor b, bool trans_a, bool trans_b, c10::optional<at::Tensor> out,
-                      bool accumulate) {
+                      bool accumulate, int64_t variant) {
   using namespace gk;
   TORCH_CHECK(gemm_tc_supported(a, b, trans_a, trans_b, out, accumulate), "gemm_tc: unsupported operands");
   const int64_t M = trans_a ? a.size(1) : a.size(0);
@@ -411,14 +663,42 @@ at::Tensor gemm_tc(at::Tensor a, at::Tensor b, bool trans_a, bool trans_b, c10::
   p.a_mn = a_mn;
   p.b_mn = b_mn;
   p.err = err_flag();
-  static bool attr_set = false;
-  if (!attr_set) {
-    EMB_CUDA_CHECK(cudaFuncSetAttribute(gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
-    attr_set = true;
+  const int64_t tiles2 = ((M + 255) / 256) * ((N + 255) / 256);
+  const bool pair = variant == 2 || (variant <= 0 && tiles2 >= num_sms() / 2);
+  if (pair) {
+    // 2-SM clusters: each CTA loads a 128-row half of the A tile and of the B tile
+    CUtensorMap tA2 = a_mn ? tA : make_map(a.data_ptr(), M, K, a.stride(0), 64, 128);
+    CUtensorMap tB2 = b_mn ? tB : make_map(b.data_ptr(), N, K, b.stride(0), 64, 128);
+    static bool attr2 = false;
+    if (!attr2) {
+      EMB_CUDA_CHECK(cudaFuncSetAttribute(gk2::gemm2_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          gk2::SMEM_BYTES));
+      attr2 = true;
+    }
+    const int clusters = (int)std::min<int64_t>(tiles2, num_sms() / 2);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2 * clusters, 1, 1);
+    cfg.blockDim = dim3(gk2::NUM_THREADS, 1, 1);
+    cfg.dynamicSmemBytes = gk2::SMEM_BYTES;
+    cfg.stream = cur_stream();
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    EMB_CUDA_CHECK(cudaLaunchKernelEx(&cfg, gk2::gemm2_kernel, tA2, tB2, p));
+  } else {
+    static bool attr_set = false;
+    if (!attr_set) {
+      EMB_CUDA_CHECK(cudaFuncSetAttribute(gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
+      attr_set = true;
+    }
+    const int tiles = (int)(((M + BM - 1) / BM) * ((N + BN - 1) / BN));
+    const int grid = std::min(tiles, num_sms());
+    gemm_kernel<<<grid, NUM_THREADS, SMEM_BYTES, cur_stream()>>>(tA, tB, p);
   }
-  const int tiles = (int)(((M + BM - 1) / BM) * ((N + BN - 1) / BN));
-  const int grid = std::min(tiles, num_sms());
-  gemm_kernel<<<grid, NUM_THREADS, SMEM_BYTES, cur_stream()>>>(tA, tB, p);
   EMB_LAUNCH_CHECK();
   count_launch();
   return C;
@@ -435,7 +715,7 @@ void gemm_clear_error() { EMB_CUDA_CHECK(cudaMemset(gk::err_flag(), 0, sizeof(in
 // Library fallback for operands the tensor-core kernel does not take (e.g. fp32 inputs or unaligned strides).
 at::Tensor gemm(at::Tensor a, at::Tensor b, bool trans_a, bool trans_b, c10::optional<at::Tensor> out,
                    bool accumulate) {
-  if (gemm_tc_supported(a, b, trans_a, trans_b, out, accumulate)) return gemm_tc(a, b, trans_a, trans_b, out, accumulate);
+  if (gemm_tc_supported(a, b, trans_a, trans_b, out, accumulate)) return gemm_tc(a, b, trans_a, trans_b, out, accumulate, 0);
   auto A = trans_a ? a.t() : a;
   auto B = trans_b ? b.t() : b;
   if (out.has_value() && out->defined()) {

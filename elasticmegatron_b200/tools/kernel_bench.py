@@ -39,27 +39,27 @@ def timeit(fn, iters=20, warmup=5):
     return e0.elapsed_time(e1) / iters
 
 
-def bench_gemm(m, n, k, layout, iters, baseline):
+def bench_gemm(m, n, k, layout, iters, baseline, variant=0):
     from elasticmegatron_b200.ops.native import ext
 
     dev = "cuda"
     if layout == "fprop":
         a, b = torch.randn(m, k, device=dev).bfloat16(), torch.randn(n, k, device=dev).bfloat16()
-        fn = lambda: ext().gemm_tc(a, b, False, True)
+        fn = lambda: ext().gemm_tc(a, b, False, True, variant=variant)
         ref = lambda: torch.matmul(a, b.t())
     elif layout == "dgrad":
         a, b = torch.randn(m, k, device=dev).bfloat16(), torch.randn(k, n, device=dev).bfloat16()
-        fn = lambda: ext().gemm_tc(a, b, False, False)
+        fn = lambda: ext().gemm_tc(a, b, False, False, variant=variant)
         ref = lambda: torch.matmul(a, b)
     else:
         a, b = torch.randn(k, m, device=dev).bfloat16(), torch.randn(k, n, device=dev).bfloat16()
         c = torch.zeros(m, n, device=dev)
-        fn = lambda: ext().gemm_tc(a, b, True, False, c, True)
+        fn = lambda: ext().gemm_tc(a, b, True, False, c, True, variant=variant)
         ref = lambda: c.addmm_(a.t().float(), b.float()) if False else torch.matmul(a.t(), b)
     ms = timeit(fn, iters)
     tf = 2 * m * n * k / ms / 1e9
     pk, _, src = peaks()
-    out = {"op": f"gemm_{layout}", "m": m, "n": n, "k": k, "ms": ms, "tflops": tf, "frac": tf / pk, "peak": src}
+    out = {"op": f"gemm_{layout}", "variant": variant, "m": m, "n": n, "k": k, "ms": ms, "tflops": tf, "frac": tf / pk, "peak": src}
     if baseline:
         bms = timeit(ref, iters)
         out.update({"cublas_ms": bms, "cublas_tflops": 2 * m * n * k / bms / 1e9})
@@ -103,17 +103,19 @@ def main():
     ap.add_argument("--layout", default="fprop")
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--baseline", action="store_true")
+    ap.add_argument("--variant", type=int, default=0, help="0 both, 1 one-SM tiles, 2 two-SM cluster tiles")
     a = ap.parse_args()
     res = []
     if a.what == "gemm":
-        res.append(bench_gemm(a.m, a.n, a.k, a.layout, a.iters, a.baseline))
+        res.append(bench_gemm(a.m, a.n, a.k, a.layout, a.iters, a.baseline, a.variant))
     if a.what == "all":
         # the Llama-2 7B training GEMMs at 4096 tokens per micro-batch
         for (m, n, k) in ((4096, 12288, 4096), (4096, 4096, 4096), (4096, 22016, 4096), (4096, 4096, 11008),
                           (4096, 32000, 4096)):
             for lay in ("fprop", "dgrad", "wgrad"):
                 mm, nn, kk = (m, n, k) if lay == "fprop" else ((m, k, n) if lay == "dgrad" else (n, k, m))
-                res.append(bench_gemm(mm, nn, kk, lay, a.iters, a.baseline))
+                for var in ((1, 2) if a.variant == 0 else (a.variant,)):
+                    res.append(bench_gemm(mm, nn, kk, lay, a.iters, a.baseline and var == 2, var))
     if a.what in ("elementwise", "all"):
         res += bench_elementwise(a.iters)
     for r in res:

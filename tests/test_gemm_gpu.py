@@ -15,26 +15,27 @@ SHAPES = [(128, 256, 64), (256, 512, 128), (296, 520, 200), (1024, 4096, 4096), 
           (136, 264, 72)]
 
 
+@pytest.mark.parametrize("variant", [1, 2])
 @pytest.mark.parametrize("M,N,K", SHAPES)
 @pytest.mark.parametrize("layout", ["fprop", "dgrad", "wgrad"])
-def test_gemm_layouts(M, N, K, layout):
+def test_gemm_layouts(M, N, K, layout, variant):
     torch.manual_seed(0)
     dev = "cuda"
     if layout == "fprop":  # a [M,K], b [N,K], trans_b
         a = torch.randn(M, K, device=dev).bfloat16()
         b = torch.randn(N, K, device=dev).bfloat16()
-        out = _ext().gemm_tc(a, b, False, True)
+        out = _ext().gemm_tc(a, b, False, True, variant=variant)
         exp = a.float() @ b.float().t()
     elif layout == "dgrad":  # a [M,K], b [K,N]
         a = torch.randn(M, K, device=dev).bfloat16()
         b = torch.randn(K, N, device=dev).bfloat16()
-        out = _ext().gemm_tc(a, b, False, False)
+        out = _ext().gemm_tc(a, b, False, False, variant=variant)
         exp = a.float() @ b.float()
     else:  # a [K,M] (trans_a), b [K,N]; accumulate into fp32
         a = torch.randn(K, M, device=dev).bfloat16()
         b = torch.randn(K, N, device=dev).bfloat16()
         c = torch.ones(M, N, device=dev)
-        out = _ext().gemm_tc(a, b, True, False, c, True)
+        out = _ext().gemm_tc(a, b, True, False, c, True, variant=variant)
         exp = a.float().t() @ b.float() + 1
     torch.cuda.synchronize()
     tol = 2e-2 * (K ** 0.5)
