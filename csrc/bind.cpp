@@ -33,6 +33,10 @@ torch::Tensor gemm_tc(torch::Tensor a, torch::Tensor b, bool trans_a, bool trans
                       bool accumulate, int64_t variant);
 bool gemm_tc_supported(torch::Tensor a, torch::Tensor b, bool trans_a, bool trans_b, c10::optional<torch::Tensor> out,
                        bool accumulate);
+std::vector<torch::Tensor> attn_fwd(torch::Tensor qkv, int64_t hpg, bool causal);
+bool attn_supported(torch::Tensor qkv);
+int64_t attn_error_flag();
+int64_t gemm_error_flag();
 }  // namespace emb
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -65,6 +69,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("out") = py::none(), py::arg("accumulate") = false);
   m.def("gemm_tc", &gemm_tc, py::arg("a"), py::arg("b"), py::arg("trans_a") = false, py::arg("trans_b") = false,
         py::arg("out") = py::none(), py::arg("accumulate") = false, py::arg("variant") = 0);
+  m.def("attn_fwd", &attn_fwd, py::arg("qkv"), py::arg("hpg"), py::arg("causal") = true);
+  m.def("attn_supported", &attn_supported);
+  m.def("attn_error_flag", &attn_error_flag);
+  m.def("gemm_error_flag", &gemm_error_flag);
   m.def("gemm_tc_supported", &gemm_tc_supported, py::arg("a"), py::arg("b"), py::arg("trans_a") = false,
         py::arg("trans_b") = false, py::arg("out") = py::none(), py::arg("accumulate") = false);
 }

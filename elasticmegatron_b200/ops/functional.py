@@ -332,7 +332,7 @@ class AttentionFn(torch.autograd.Function):
 
 def _has_native_attention() -> bool:
     try:
-        return hasattr(ext(), "attn_fwd")
+        return hasattr(ext(), "attn_bwd")
     except RuntimeError:
         return False
 

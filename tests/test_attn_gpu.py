@@ -1,0 +1,34 @@
+"""Native flash attention against the fp32 PyTorch reference on the fused QKV layout."""
+import math
+
+import pytest
+import torch
+
+from elasticmegatron_b200.ops import reference as ref
+
+pytestmark = pytest.mark.gpu
+
+
+def _ref(qkv, hpg, causal):
+    s, b, G, _, d = qkv.shape
+    x = qkv.float()
+    q = x[:, :, :, :hpg].reshape(s, b, G * hpg, d).permute(1, 2, 0, 3)
+    k = x[:, :, :, hpg].permute(1, 2, 0, 3)
+    v = x[:, :, :, hpg + 1].permute(1, 2, 0, 3)
+    o, lse = ref.attention_fwd(q, k, v, causal=causal)
+    return o.permute(2, 0, 1, 3).reshape(s, b, -1), lse
+
+
+@pytest.mark.parametrize("s,b,G,hpg", [(128, 1, 1, 1), (256, 2, 2, 2), (512, 1, 4, 1), (384, 2, 1, 4)])
+@pytest.mark.parametrize("causal", [True, False])
+def test_flash_fwd(s, b, G, hpg, causal):
+    from elasticmegatron_b200.ops.native import ext
+
+    torch.manual_seed(0)
+    qkv = torch.randn(s, b, G, hpg + 2, 128, device="cuda").bfloat16()
+    o, lse = ext().attn_fwd(qkv, hpg, causal)
+    torch.cuda.synchronize()
+    assert ext().attn_error_flag() == 0
+    o_ref, lse_ref = _ref(qkv, hpg, causal)
+    torch.testing.assert_close(o.float(), o_ref, atol=2e-2, rtol=2e-2)
+    torch.testing.assert_close(lse, lse_ref, atol=1e-3, rtol=1e-3)
