@@ -1,0 +1,444 @@
+// K10 (backward): causal GQA flash attention backward on tcgen05 / TMEM / TMA, sm_100a, head dim 128.
+//
+// One CTA = one (128-row key/value tile j, batch, query group g).  K_j and V_j stay in shared memory; the CTA
+// walks every head of the group and every query tile i >= j (causal), so dK_j and dV_j accumulate in TMEM
+// across all of them and are written once, with no atomics.  Per (head, query tile) step:
+//   S^T  = K_j Q_i^T          (TMEM cols   0..127; later reused for dQ)
+//   dP^T = V_j dO_i^T         (TMEM cols 128..255)
+//   one thread per key row:   P^T = exp(S^T * scale - lse), dS^T = P^T * (dP^T - Delta) * scale, both written
+//                             as bf16 128-byte-swizzled tiles [key rows x query cols]
+//   dV  += P^T dO_i            (cols 256..383; dO as an MN-major operand)
+//   dK  += dS^T Q_i            (cols 384..511; Q as an MN-major operand)
+//   dQ_i = dS K_j              (cols 0..127; the dS^T tile read as an MN-major A operand, K_j as MN-major B)
+//   one thread per query row adds its dQ row into an fp32 accumulator with 16-byte vector atomics.
+// Delta = rowsum(dO * O) comes from a small preprocessing kernel; a finishing kernel casts the dQ accumulator
+// into the query slots of dqkv.  Waits are bounded (error flag); no TMA multicast.
+#include <cudaTypedefs.h>
+
+#include "../include/common.cuh"
+
+namespace emb {
+namespace fa {
+CUtensorMap qkv_map(const at::Tensor& qkv);
+}
+
+namespace fab {
+
+constexpr int D = 128, T = 128;
+constexpr int TILE = 128 * 128 * 2;
+constexpr int SMEM_BYTES = 6 * TILE + 1024 /*lse, delta*/ + 1024 /*align*/ + 256 /*barriers*/;
+constexpr uint32_t WAIT_LIMIT = 1u << 26;
+
+__device__ __forceinline__ uint32_t su32(const void* p) { return static_cast<uint32_t>(__cvta_generic_to_shared(p)); }
+__device__ __forceinline__ void bar_init(uint64_t* b, uint32_t n) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(su32(b)), "r"(n));
+}
+__device__ __forceinline__ void bar_expect(uint64_t* b, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(su32(b)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void bar_arrive(uint64_t* b) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(su32(b)) : "memory");
+}
+__device__ __forceinline__ bool bar_wait(uint64_t* b, uint32_t parity, int* err, int code) {
+  for (uint32_t i = 0; i < WAIT_LIMIT; ++i) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok)
+        : "r"(su32(b)), "r"(parity)
+        : "memory");
+    if (ok) return true;
+    if (i > 64) __nanosleep(64);
+  }
+  atomicExch(err, code);
+  return false;
+}
+__device__ __forceinline__ void tma4(void* dst, const CUtensorMap* m, uint64_t* bar, int x, int slot, int bb, int s) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, %5}], "
+      "[%6];" ::"r"(su32(dst)),
+      "l"(reinterpret_cast<uint64_t>(m)), "r"(x), "r"(slot), "r"(bb), "r"(s), "r"(su32(bar))
+      : "memory");
+}
+__device__ __forceinline__ void fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ uint64_t desc(uint32_t addr, uint32_t lbo, uint32_t sbo) {
+  return (uint64_t)((addr >> 4) & 0x3FFF) | ((uint64_t)((lbo >> 4) & 0x3FFF) << 16) |
+         ((uint64_t)((sbo >> 4) & 0x3FFF) << 32) | ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+__host__ __device__ constexpr uint32_t idesc(bool a_mn, bool b_mn) {
+  return (1u << 4) | (1u << 7) | (1u << 10) | ((a_mn ? 1u : 0u) << 15) | ((b_mn ? 1u : 0u) << 16) |
+         ((uint32_t)(128 >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
+}
+__device__ __forceinline__ void mma(uint32_t d, uint64_t a, uint64_t b, uint32_t id, uint32_t acc) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(d),
+      "l"(a), "l"(b), "r"(id), "r"(acc));
+}
+__device__ __forceinline__ void commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(su32(bar))
+               : "memory");
+}
+#define FAB_LD32(taddr, r)                                                                                          \
+  asm volatile(                                                                                                     \
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19," \
+      "%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"                                                    \
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]), \
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),      \
+        "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),     \
+        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])                   \
+      : "r"(taddr))
+
+__device__ __forceinline__ uint32_t swz_off(int row, int col) {
+  const int panel = col >> 6, c = col & 63;
+  return panel * 16384 + row * 128 + (((c >> 3) ^ (row & 7)) << 4) + (c & 7) * 2;
+}
+
+struct Params {
+  const float* lse;    // [b, H, s]
+  const float* delta;  // [b, H, s]
+  float* dq_acc;       // [s, b, H, d] fp32, zero-initialised
+  __nv_bfloat16* dqkv; // [s, b, G, hpg + 2, d]
+  int s, b, G, hpg;
+  float scale, scale_log2;
+  int causal;
+  int* err;
+};
+
+__global__ void __launch_bounds__(192, 1)
+    flash_bwd_kernel(const __grid_constant__ CUtensorMap tqkv, const __grid_constant__ CUtensorMap tdo, Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sK = sm;
+  uint8_t* sV = sm + TILE;
+  uint8_t* sQ = sm + 2 * TILE;
+  uint8_t* sdO = sm + 3 * TILE;
+  uint8_t* sP = sm + 4 * TILE;   // P^T  [key rows x query cols]
+  uint8_t* sdS = sm + 5 * TILE;  // dS^T [key rows x query cols]
+  float* s_lse = reinterpret_cast<float*>(sm + 6 * TILE);
+  float* s_delta = s_lse + 128;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + 6 * TILE + 1024);
+  uint64_t* kv_full = bars;
+  uint64_t* qdo_full = bars + 1;
+  uint64_t* qdo_empty = bars + 2;
+  uint64_t* s_full = bars + 3;
+  uint64_t* ds_full = bars + 4;
+  uint64_t* mma2_done = bars + 5;
+  uint64_t* dq_empty = bars + 6;
+  uint64_t* stats_full = bars + 7;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 8);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nq = p.s / T;
+  const int jt = blockIdx.x;  // key/value tile
+  const int bg = blockIdx.y;
+  const int bidx = bg / p.G, g = bg % p.G;
+  const int H = p.G * p.hpg;
+  const int slots = p.hpg + 2;
+  const int k_slot = g * slots + p.hpg, v_slot = k_slot + 1;
+  const int i0 = p.causal ? jt : 0;
+  const int nsteps = p.hpg * (nq - i0);
+
+  if (threadIdx.x == 0) {
+    bar_init(kv_full, 1);
+    bar_init(qdo_full, 1);
+    bar_init(qdo_empty, 1);
+    bar_init(s_full, 1);
+    bar_init(ds_full, 4);
+    bar_init(mma2_done, 1);
+    bar_init(dq_empty, 4);
+    bar_init(stats_full, 4);
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(su32(tmem_slot)), "r"(512));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  fence_before();
+  __syncthreads();
+  fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      bar_expect(kv_full, 2 * TILE);
+      tma4(sK, &tqkv, kv_full, 0, k_slot, bidx, jt * T);
+      tma4(sK + 16384, &tqkv, kv_full, 64, k_slot, bidx, jt * T);
+      tma4(sV, &tqkv, kv_full, 0, v_slot, bidx, jt * T);
+      tma4(sV + 16384, &tqkv, kv_full, 64, v_slot, bidx, jt * T);
+      for (int n = 0; n < nsteps; ++n) {
+        const int hj = n / (nq - i0), it = i0 + n % (nq - i0);
+        const int h = g * p.hpg + hj;
+        if (!bar_wait(qdo_empty, (n & 1) ^ 1, p.err, 41) || *abort_flag) { *abort_flag = 1; break; }
+        bar_expect(qdo_full, 2 * TILE);
+        tma4(sQ, &tqkv, qdo_full, 0, g * slots + hj, bidx, it * T);
+        tma4(sQ + 16384, &tqkv, qdo_full, 64, g * slots + hj, bidx, it * T);
+        tma4(sdO, &tdo, qdo_full, 0, h, bidx, it * T);
+        tma4(sdO + 16384, &tdo, qdo_full, 64, h, bidx, it * T);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      const uint32_t id_kk = idesc(false, false), id_kmn = idesc(false, true), id_mnmn = idesc(true, true);
+      const uint32_t aK = su32(sK), aV = su32(sV), aQ = su32(sQ), adO = su32(sdO), aP = su32(sP), adS = su32(sdS);
+      bool ok = bar_wait(kv_full, 0, p.err, 42) && !*abort_flag;
+      for (int n = 0; n < nsteps && ok; ++n) {
+        const uint32_t ph = n & 1;
+        if (!bar_wait(qdo_full, ph, p.err, 43) || !bar_wait(dq_empty, ph ^ 1, p.err, 44) || *abort_flag) {
+          ok = false;
+          break;
+        }
+        fence_after();
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {  // reduce over d: K-major panels of the K/V/Q/dO tiles
+          const uint32_t off = (k >> 2) * 16384 + (k & 3) * 32;
+          mma(tmem + 0, desc(aK + off, 16, 1024), desc(aQ + off, 16, 1024), id_kk, k != 0);
+          mma(tmem + 128, desc(aV + off, 16, 1024), desc(adO + off, 16, 1024), id_kk, k != 0);
+        }
+        commit(s_full);
+        if (!bar_wait(ds_full, ph, p.err, 45) || *abort_flag) { ok = false; break; }
+        fence_after();
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {  // reduce over the query index
+          const uint32_t offa = (k >> 2) * 16384 + (k & 3) * 32;  // P^T / dS^T as K-major A (rows = keys)
+          const uint32_t offb = k * 2048;                          // dO / Q as MN-major B (rows = queries)
+          mma(tmem + 256, desc(aP + offa, 16, 1024), desc(adO + offb, 16384, 1024), id_kmn, (n | k) != 0);
+          mma(tmem + 384, desc(adS + offa, 16, 1024), desc(aQ + offb, 16384, 1024), id_kmn, (n | k) != 0);
+        }
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {  // dQ = dS K: reduce over keys; dS^T tile as MN-major A, K tile MN-major B
+          mma(tmem + 0, desc(adS + k * 2048, 16384, 1024), desc(aK + k * 2048, 16384, 1024), id_mnmn, k != 0);
+        }
+        commit(qdo_empty);
+        commit(mma2_done);
+      }
+      if (!ok) *abort_flag = 1;
+    }
+  } else {
+    const int quarter = warp & 3;
+    const int r = quarter * 32 + lane;  // TMEM lane: key row for S^T/dP^T/dK/dV, query row for dQ
+    const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
+    const int kpos = jt * T + r;
+    bool ok = true;
+    for (int n = 0; n < nsteps; ++n) {
+      const int hj = n / (nq - i0), it = i0 + n % (nq - i0);
+      const int h = g * p.hpg + hj;
+      const uint32_t ph = n & 1;
+      // per-query statistics of this step (the previous step's readers finished before dq_empty completed)
+      if (n > 0 && (!bar_wait(dq_empty, ph ^ 1, p.err, 46) || *abort_flag)) { ok = false; break; }
+      {
+        const size_t base = ((size_t)bidx * H + h) * p.s + it * T;
+        s_lse[r] = p.lse[base + r] * 1.4426950408889634f;
+        s_delta[r] = p.delta[base + r];
+      }
+      asm volatile("bar.sync 1, 128;" ::: "memory");
+      if (!bar_wait(s_full, ph, p.err, 47) || *abort_flag) { ok = false; break; }
+      fence_after();
+      const bool diag = p.causal && it == jt;
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        uint32_t sv[32], dv[32];
+        FAB_LD32(tmem + lane_base + c * 32, sv);
+        FAB_LD32(tmem + lane_base + 128 + c * 32, dv);
+        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+        float pf[32], df[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const int q = c * 32 + i;
+          const int qpos = it * T + q;
+          float pr = exp2f(__uint_as_float(sv[i]) * p.scale_log2 - s_lse[q]);
+          if (diag && qpos < kpos) pr = 0.f;
+          pf[i] = pr;
+          df[i] = pr * (__uint_as_float(dv[i]) - s_delta[q]) * p.scale;
+        }
+#pragma unroll
+        for (int v8 = 0; v8 < 4; ++v8) {
+          *reinterpret_cast<uint4*>(sP + swz_off(r, c * 32 + v8 * 8)) = pack8(pf + v8 * 8);
+          *reinterpret_cast<uint4*>(sdS + swz_off(r, c * 32 + v8 * 8)) = pack8(df + v8 * 8);
+        }
+      }
+      fence_before();
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      __syncwarp();
+      if (lane == 0) bar_arrive(ds_full);
+      // dQ tile (TMEM cols 0..127, lane = query row) -> fp32 accumulator
+      if (!bar_wait(mma2_done, ph, p.err, 48) || *abort_flag) { ok = false; break; }
+      fence_after();
+      float* dst = p.dq_acc + (((size_t)(it * T + r) * p.b + bidx) * H + h) * D;
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        uint32_t qv[32];
+        FAB_LD32(tmem + lane_base + c * 32, qv);
+        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+        for (int v4 = 0; v4 < 8; ++v4) {
+          float4 val = make_float4(__uint_as_float(qv[4 * v4]), __uint_as_float(qv[4 * v4 + 1]),
+                                   __uint_as_float(qv[4 * v4 + 2]), __uint_as_float(qv[4 * v4 + 3]));
+          atomicAdd(reinterpret_cast<float4*>(dst + c * 32 + 4 * v4), val);
+        }
+      }
+      fence_before();
+      __syncwarp();
+      if (lane == 0) bar_arrive(dq_empty);
+    }
+    if (!ok) {
+      *abort_flag = 1;
+    } else if (nsteps > 0) {
+      // dK (cols 384..) and dV (cols 256..) rows of this key tile -> dqkv key / value slots
+      if (!bar_wait(dq_empty, ((nsteps - 1) & 1), p.err, 49)) { *abort_flag = 1; }
+      fence_after();
+      __nv_bfloat16* dk = p.dqkv + ((((size_t)kpos * p.b + bidx) * p.G + g) * slots + p.hpg) * D;
+      __nv_bfloat16* dvp = dk + D;
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        uint32_t kv[32], vv[32];
+        FAB_LD32(tmem + lane_base + 384 + c * 32, kv);
+        FAB_LD32(tmem + lane_base + 256 + c * 32, vv);
+        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+        float kf[32], vf[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          kf[i] = __uint_as_float(kv[i]);
+          vf[i] = __uint_as_float(vv[i]);
+        }
+#pragma unroll
+        for (int v8 = 0; v8 < 4; ++v8) {
+          reinterpret_cast<uint4*>(dk + c * 32)[v8] = pack8(kf + v8 * 8);
+          reinterpret_cast<uint4*>(dvp + c * 32)[v8] = pack8(vf + v8 * 8);
+        }
+      }
+    }
+  }
+  fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(512));
+  }
+}
+
+// delta[b, h, q] = sum_d dO[q, b, h, d] * O[q, b, h, d]; one warp per row
+__global__ void delta_kernel(const __nv_bfloat16* __restrict__ dO, const __nv_bfloat16* __restrict__ O,
+                             float* __restrict__ delta, int s, int b, int H) {
+  const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= s * b * H) return;
+  const int q = row / (b * H), rem = row % (b * H), bi = rem / H, h = rem % H;
+  const __nv_bfloat16* a = dO + (size_t)row * D;
+  const __nv_bfloat16* c = O + (size_t)row * D;
+  float acc = 0.f;
+  for (int i = lane; i < D; i += 32) acc += bf2f(a[i]) * bf2f(c[i]);
+  acc = warp_sum(acc);
+  if (lane == 0) delta[((size_t)bi * H + h) * s + q] = acc;
+}
+
+// dqkv query slots <- bf16(dq_acc)
+__global__ void dq_cast_kernel(const float* __restrict__ dq, __nv_bfloat16* __restrict__ dqkv, int s, int b, int G,
+                               int hpg) {
+  const int64_t n = (int64_t)s * b * G * hpg * (D / 8);
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t row = i / (D / 8);
+    const int v = (int)(i % (D / 8));
+    const int hj = (int)(row % hpg);
+    const int64_t tg = row / hpg;  // (token, group)
+    const float* src = dq + row * D + v * 8;
+    float f[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) f[k] = src[k];
+    __nv_bfloat16* dst = dqkv + (tg * (hpg + 2) + hj) * D + v * 8;
+    *reinterpret_cast<uint4*>(dst) = pack8(f);
+  }
+}
+
+static int* err_flag() {
+  static int* f = nullptr;
+  if (!f) {
+    EMB_CUDA_CHECK(cudaMalloc(&f, sizeof(int)));
+    EMB_CUDA_CHECK(cudaMemset(f, 0, sizeof(int)));
+  }
+  return f;
+}
+
+static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (!fn) {
+    cudaDriverEntryPointQueryResult q;
+    void* ptr = nullptr;
+    EMB_CUDA_CHECK(cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q));
+    TORCH_CHECK(q == cudaDriverEntryPointSuccess && ptr, "cuTensorMapEncodeTiled not available");
+    fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  }
+  return fn;
+}
+
+// {d, head, b, s} view of dO [s, b, H*d].
+static CUtensorMap do_map(const at::Tensor& dO, int64_t s, int64_t b, int64_t H) {
+  CUtensorMap m;
+  cuuint64_t dims[4] = {(cuuint64_t)D, (cuuint64_t)H, (cuuint64_t)b, (cuuint64_t)s};
+  cuuint64_t strides[3] = {(cuuint64_t)(D * 2), (cuuint64_t)(H * D * 2), (cuuint64_t)(b * H * D * 2)};
+  cuuint32_t box[4] = {64, 1, 1, 128};
+  cuuint32_t es[4] = {1, 1, 1, 1};
+  CUresult r = encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, dO.data_ptr(), dims, strides, box, es,
+                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  TORCH_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled(dO) failed: ", (int)r);
+  return m;
+}
+
+}  // namespace fab
+
+// dqkv [s, b, G, hpg + 2, d] for the causal attention whose forward returned (o, lse).
+at::Tensor attn_bwd(at::Tensor dO, at::Tensor qkv, at::Tensor o, at::Tensor lse, int64_t hpg, bool causal) {
+  using namespace fab;
+  TORCH_CHECK(qkv.is_cuda() && qkv.scalar_type() == at::kBFloat16 && qkv.is_contiguous() && qkv.size(4) == D &&
+                  qkv.size(0) % T == 0,
+              "attn_bwd: needs contiguous bf16 [s, b, G, hpg+2, 128] with s % 128 == 0");
+  TORCH_CHECK(dO.is_contiguous() && o.is_contiguous() && dO.scalar_type() == at::kBFloat16);
+  const int64_t s = qkv.size(0), b = qkv.size(1), G = qkv.size(2), H = G * hpg;
+  auto dqkv = at::empty_like(qkv);
+  auto dq = at::zeros({s, b, H, D}, qkv.options().dtype(at::kFloat));
+  auto delta = at::empty({b, H, s}, qkv.options().dtype(at::kFloat));
+  auto st = cur_stream();
+  const int rows = (int)(s * b * H);
+  delta_kernel<<<(rows + 7) / 8, 256, 0, st>>>(reinterpret_cast<const __nv_bfloat16*>(dO.data_ptr()),
+                                               reinterpret_cast<const __nv_bfloat16*>(o.data_ptr()),
+                                               delta.data_ptr<float>(), (int)s, (int)b, (int)H);
+  CUtensorMap tq = fa::qkv_map(qkv);
+  CUtensorMap td = do_map(dO, s, b, H);
+  Params p;
+  p.lse = lse.data_ptr<float>();
+  p.delta = delta.data_ptr<float>();
+  p.dq_acc = dq.data_ptr<float>();
+  p.dqkv = reinterpret_cast<__nv_bfloat16*>(dqkv.data_ptr());
+  p.s = (int)s;
+  p.b = (int)b;
+  p.G = (int)G;
+  p.hpg = (int)hpg;
+  p.scale = (float)(1.0 / std::sqrt((double)D));
+  p.scale_log2 = (float)(1.4426950408889634 / std::sqrt((double)D));
+  p.causal = causal ? 1 : 0;
+  p.err = err_flag();
+  static bool attr = false;
+  if (!attr) {
+    EMB_CUDA_CHECK(cudaFuncSetAttribute(flash_bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
+    attr = true;
+  }
+  dim3 grid((unsigned)(s / T), (unsigned)(b * G));
+  flash_bwd_kernel<<<grid, 192, SMEM_BYTES, st>>>(tq, td, p);
+  const int64_t n = s * b * G * hpg * (D / 8);
+  dq_cast_kernel<<<(int)std::min<int64_t>((n + 255) / 256, (int64_t)num_sms() * 8), 256, 0, st>>>(
+      dq.data_ptr<float>(), reinterpret_cast<__nv_bfloat16*>(dqkv.data_ptr()), (int)s, (int)b, (int)G, (int)hpg);
+  EMB_LAUNCH_CHECK();
+  count_launch(3);
+  return dqkv;
+}
+
+int64_t attn_bwd_error_flag() {
+  int v = 0;
+  EMB_CUDA_CHECK(cudaMemcpy(&v, fab::err_flag(), sizeof(int), cudaMemcpyDeviceToHost));
+  return v;
+}
+
+}  // namespace emb

@@ -36,6 +36,9 @@ bool gemm_tc_supported(torch::Tensor a, torch::Tensor b, bool trans_a, bool tran
 std::vector<torch::Tensor> attn_fwd(torch::Tensor qkv, int64_t hpg, bool causal);
 bool attn_supported(torch::Tensor qkv);
 int64_t attn_error_flag();
+torch::Tensor attn_bwd(torch::Tensor dO, torch::Tensor qkv, torch::Tensor o, torch::Tensor lse, int64_t hpg,
+                       bool causal);
+int64_t attn_bwd_error_flag();
 int64_t gemm_error_flag();
 }  // namespace emb
 
@@ -71,6 +74,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("out") = py::none(), py::arg("accumulate") = false, py::arg("variant") = 0);
   m.def("attn_fwd", &attn_fwd, py::arg("qkv"), py::arg("hpg"), py::arg("causal") = true);
   m.def("attn_supported", &attn_supported);
+  m.def("attn_bwd", &attn_bwd, py::arg("dO"), py::arg("qkv"), py::arg("o"), py::arg("lse"), py::arg("hpg"),
+        py::arg("causal") = true);
+  m.def("attn_bwd_error_flag", &attn_bwd_error_flag);
   m.def("attn_error_flag", &attn_error_flag);
   m.def("gemm_error_flag", &gemm_error_flag);
   m.def("gemm_tc_supported", &gemm_tc_supported, py::arg("a"), py::arg("b"), py::arg("trans_a") = false,

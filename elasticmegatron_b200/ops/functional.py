@@ -348,7 +348,7 @@ def _sdpa_attention(qkv, hpg):
 
 
 def attention(qkv, hpg):
-    if qkv.is_cuda and not _has_native_attention():
+    if qkv.is_cuda and not (_has_native_attention() and ext().attn_supported(qkv)):
         return _sdpa_attention(qkv, hpg)
     return AttentionFn.apply(qkv, hpg)
 

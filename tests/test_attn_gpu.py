@@ -32,3 +32,38 @@ def test_flash_fwd(s, b, G, hpg, causal):
     o_ref, lse_ref = _ref(qkv, hpg, causal)
     torch.testing.assert_close(o.float(), o_ref, atol=2e-2, rtol=2e-2)
     torch.testing.assert_close(lse, lse_ref, atol=1e-3, rtol=1e-3)
+
+
+@pytest.mark.parametrize("s,b,G,hpg", [(128, 1, 1, 1), (256, 2, 2, 2), (384, 1, 1, 4)])
+def test_flash_bwd(s, b, G, hpg):
+    from elasticmegatron_b200.ops.native import ext
+
+    torch.manual_seed(0)
+    qkv = torch.randn(s, b, G, hpg + 2, 128, device="cuda").bfloat16()
+    dO = torch.randn(s, b, G * hpg * 128, device="cuda").bfloat16()
+    o, lse = ext().attn_fwd(qkv, hpg, True)
+    dqkv = ext().attn_bwd(dO, qkv, o, lse, hpg, True)
+    torch.cuda.synchronize()
+    assert ext().attn_bwd_error_flag() == 0
+    x = qkv.float().requires_grad_(True)
+    o_ref, _ = _ref(x, hpg, True)
+    (g,) = torch.autograd.grad(o_ref, x, dO.float())
+    scale = g.abs().max().item()
+    torch.testing.assert_close(dqkv.float(), g, atol=3e-2 * max(1.0, scale / 4), rtol=5e-2)
+
+
+def test_attention_autograd_native_path():
+    """The model's attention op runs the native kernels on CUDA for head dim 128."""
+    from elasticmegatron_b200.ops import functional as F_
+    from elasticmegatron_b200.ops.native import launch_count
+
+    torch.manual_seed(0)
+    qkv = torch.randn(256, 1, 2, 4, 128, device="cuda").bfloat16().requires_grad_(True)
+    n0 = launch_count()
+    y = F_.attention(qkv, 2)
+    y.float().pow(2).sum().backward()
+    torch.cuda.synchronize()
+    assert launch_count() - n0 >= 4
+    x = qkv.detach().float().requires_grad_(True)
+    o_ref, _ = _ref(x, 2, True)
+    torch.testing.assert_close(y.float(), o_ref, atol=2e-2, rtol=2e-2)
