@@ -39,11 +39,13 @@ def _strategies(world):
     return out
 
 
-def _fill(param, opt, seed, rank):
+def _fill(param, opt, rl, seed, rank):
+    """Params N(0, 0.02); master = the own shard of the params; moments uniform in [0, 1e-3)."""
     g = torch.Generator(device=param.device)
     g.manual_seed(seed * 131 + rank)
     param.normal_(0.0, 0.02, generator=g)
-    opt[0].copy_(param.float())
+    for a, e, o in rl.owned():
+        opt[0, o:o + (e - a)].copy_(param[a:e].float())
     opt[1:].uniform_(0.0, 1e-3, generator=g)
 
 
@@ -118,7 +120,7 @@ def main():
         sa = arenas(a) if rank < a.world_size else None
         sb = arenas(b) if rank < b.world_size else None
         if sa:
-            _fill(sa[2], sa[3], 1, rank)
+            _fill(sa[2], sa[3], sa[4], 1, rank)
         union = sorted(set(range(a.world_size)) | set(range(b.world_size)))
         group = ProcessGroupPool.get(union)
         times = []
