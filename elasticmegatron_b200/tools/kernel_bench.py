@@ -94,9 +94,37 @@ def bench_elementwise(iters):
     return out
 
 
+def bench_attention(iters, s=4096, b=1, G=32, hpg=1):
+    """Causal attention at the 7B shape: native forward / backward vs PyTorch SDPA (library)."""
+    from elasticmegatron_b200.ops.functional import _sdpa_attention
+    from elasticmegatron_b200.ops.native import ext
+
+    qkv = torch.randn(s, b, G, hpg + 2, 128, device="cuda").bfloat16()
+    H = G * hpg
+    flops_fwd = 4 * b * H * s * s * 128 / 2  # causal
+    o, lse = ext().attn_fwd(qkv, hpg, True)
+    dO = torch.randn_like(o)
+    ms_f = timeit(lambda: ext().attn_fwd(qkv, hpg, True), iters)
+    ms_b = timeit(lambda: ext().attn_bwd(dO, qkv, o, lse, hpg, True), iters)
+    x = qkv.clone().requires_grad_(True)
+
+    def sdpa_fb():
+        y = _sdpa_attention(x, hpg)
+        y.backward(dO)
+
+    ms_sf = timeit(lambda: _sdpa_attention(qkv, hpg), iters)
+    ms_sfb = timeit(sdpa_fb, iters)
+    pk, _, src = peaks()
+    return [{"op": "attn_fwd", "ms": ms_f, "tflops": flops_fwd / ms_f / 1e9, "frac": flops_fwd / ms_f / 1e9 / pk,
+             "sdpa_ms": ms_sf, "sdpa_tflops": flops_fwd / ms_sf / 1e9, "peak": src},
+            {"op": "attn_bwd", "ms": ms_b, "tflops": 2.5 * flops_fwd / ms_b / 1e9,
+             "frac": 2.5 * flops_fwd / ms_b / 1e9 / pk, "sdpa_fwd_bwd_ms": ms_sfb, "native_fwd_bwd_ms": ms_f + ms_b,
+             "peak": src}]
+
+
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("what", choices=["gemm", "elementwise", "all"])
+    ap.add_argument("what", choices=["gemm", "elementwise", "attention", "all"])
     ap.add_argument("--m", type=int, default=16384)
     ap.add_argument("--n", type=int, default=4096)
     ap.add_argument("--k", type=int, default=4096)
@@ -118,6 +146,8 @@ def main():
                     res.append(bench_gemm(mm, nn, kk, lay, a.iters, a.baseline and var == 2, var))
     if a.what in ("elementwise", "all"):
         res += bench_elementwise(a.iters)
+    if a.what in ("attention", "all"):
+        res += bench_attention(a.iters)
     for r in res:
         print(json.dumps(r))
 
