@@ -25,9 +25,13 @@ def _act_shape(ts) -> tuple:
     return (tokens, cfg.hidden_size)
 
 
-def train_step(ts, data_iter: Iterator, hetero_dp: bool = False, return_loss: bool = True) -> Dict:
+def train_step(ts, data_iter: Iterator, hetero_dp: Optional[bool] = None, return_loss: bool = True) -> Dict:
     ps, tc, cfg = ts.ps, ts.train_cfg, ts.cfg
     s = ts.strategy
+    if hetero_dp is None:
+        from .hetero_dp import hetero_dp_enabled
+
+        hetero_dp = hetero_dp_enabled()
     n_mb = num_microbatches(tc.global_batch_size, tc.micro_batch_size, s.data_parallel_size, ps.dp_rank, hetero_dp)
     dev = ts.device
     needs_data = ps.is_first_stage or ps.is_last_stage
@@ -39,8 +43,10 @@ def train_step(ts, data_iter: Iterator, hetero_dp: bool = False, return_loss: bo
         else:
             batches.append((ids.to(dev, non_blocking=True), lab.to(dev, non_blocking=True)))
     ts.ddp.zero_grad()
-    seq_tokens = cfg.seq_length * tc.micro_batch_size  # tokens of one micro-batch over all CP ranks
-    loss_scale = s.context_parallel_size / (seq_tokens * n_mb)
+    # Every rank scales its token-loss sum by DP*CP / (GBS * seq): after the optimizer's 1/(DP*CP) gradient
+    # average this is the gradient of the global mean token loss, also when DP ranks run different numbers
+    # of micro-batches (hetero-DP).
+    loss_scale = (s.data_parallel_size * s.context_parallel_size) / (tc.global_batch_size * cfg.seq_length)
     ctx = StepContext(ts.stage, ps, ts.ddp, n_mb, _act_shape(ts), ts.param_dtype, dev, loss_scale,
                       lambda i: batches[i])
     fb = get_forward_backward_func(s.pipeline_model_parallel_size)

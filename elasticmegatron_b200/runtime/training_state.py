@@ -34,6 +34,9 @@ class TrainingState:
     def __init__(self, strategy: ParallelStrategy, cfg: Optional[ModelConfig] = None,
                  train_cfg: Optional[TrainConfig] = None, device=None, is_meta_device: bool = False):
         args = get_args()
+        from .meta import in_meta_context
+
+        is_meta_device = is_meta_device or in_meta_context()
         self.cfg = cfg or args.model
         self.train_cfg = train_cfg or args.train
         self.strategy = strategy
@@ -122,7 +125,18 @@ class TrainingState:
         if not self.model_released:
             return
         self._alloc_model()
-        self.stage.rebind(self._param_views())
+        if self.is_meta_device:
+            # meta parameters cannot be re-pointed at device memory in place: build the stage and its
+            # gradient hooks afresh over the new arenas (the optimizer and scheduler objects survive)
+            self.ddp.remove_hooks()
+            self.stage = GPTStage(self.cfg, self.ps, self.layout.params, self._param_views(),
+                                  self.train_cfg.micro_batch_size)
+            self.stage._training_state = self
+            self.model = [self.stage]
+            self.ddp = DistributedDataParallel(self.layout, self.ps, self.stage.params_by_name, self.param_flat,
+                                               self.grad_flat, self.train_cfg.overlap_grad_reduce)
+        else:
+            self.stage.rebind(self._param_views())
         self.ddp.bind(self.param_flat, self.grad_flat)
         self.optimizer.bind(self.param_flat, self.grad_flat, self.opt_flat)
         self.model_released = False

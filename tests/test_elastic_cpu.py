@@ -177,3 +177,55 @@ def test_checkpoint_save_a_load_b_equals_live_reshard(tmp_path):
     st = torch.load(it / "mp_rank_00" / "model_optim_rng.pt", weights_only=False)
     assert "decoder.layers.0.self_attention.linear_qkv.weight" in st["model"]
     assert st["iteration"] == 2
+
+
+def _hetero(rank, world, strat_idx):
+    from elasticmegatron_b200.config import Args, ModelConfig, TrainConfig, set_args
+    from elasticmegatron_b200 import apply_hetero_dp
+    from elasticmegatron_b200.parallel.process_groups import create_all_groups
+    from elasticmegatron_b200.parallel.strategy import ParallelStrategy
+    from elasticmegatron_b200.runtime.data import DataloaderState
+    from elasticmegatron_b200.runtime.train import train_step
+    from elasticmegatron_b200.runtime.training_state import TrainingState
+
+    cfg = ModelConfig(num_layers=2, hidden_size=64, num_attention_heads=4, ffn_hidden_size=128, vocab_size=500,
+                      seq_length=32, params_dtype="fp32", max_tensor_parallel_size=2, make_vocab_size_divisible_by=8)
+    # 3 micro-batches of 2 per global batch: DP2 splits them 2 + 1
+    set_args(Args(model=cfg, train=TrainConfig(micro_batch_size=2, global_batch_size=6, lr=1e-3, train_iters=20)))
+    apply_hetero_dp(True)
+    S = [ParallelStrategy(world_size=2, tensor_model_parallel_size=1, pipeline_model_parallel_size=1),
+         ParallelStrategy(world_size=1, tensor_model_parallel_size=1, pipeline_model_parallel_size=1)]
+    create_all_groups(S)
+    s = S[strat_idx]
+    if rank >= s.world_size:
+        return None
+    ts = TrainingState(s)
+    ts.init_weights(0)
+    it = DataloaderState.build_iterators(ts, 0)[0]
+    return [train_step(ts, it)["loss"] for _ in range(3)]
+
+
+def test_hetero_dp_matches_single_rank():
+    dp2 = run_distributed(_hetero, 2, 0)
+    one = run_distributed(_hetero, 2, 1)
+    np.testing.assert_allclose(dp2[0], one[0], rtol=2e-6)
+
+
+def test_meta_device_context_and_exports():
+    import elasticmegatron_b200 as emb
+    from elasticmegatron_b200.config import Args, ModelConfig, set_args
+    from elasticmegatron_b200.parallel.strategy import ParallelStrategy
+    from elasticmegatron_b200.runtime.training_state import TrainingState
+
+    for n in ("ElasticMegatronManager", "apply_hetero_dp", "meta_device_context", "nccl_group_recreate"):
+        assert callable(getattr(emb, n))
+    set_args(Args(model=ModelConfig(num_layers=2, hidden_size=64, num_attention_heads=4, ffn_hidden_size=128,
+                                    vocab_size=500, params_dtype="fp32")))
+    s = ParallelStrategy(world_size=1, tensor_model_parallel_size=1, pipeline_model_parallel_size=1)
+    with emb.meta_device_context():
+        ts = TrainingState(s)
+    assert ts.is_meta_device and ts.param_arena is None and ts.opt_arena is None
+    assert next(iter(ts.stage.params_by_name.values())).device.type == "meta"
+    ts.rebuild()
+    assert ts.param_flat is not None and not ts.is_meta_device
+    assert next(iter(ts.stage.params_by_name.values())).device.type == "cpu"
