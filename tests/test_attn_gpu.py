@@ -57,12 +57,16 @@ def test_attention_autograd_native_path():
     from elasticmegatron_b200.ops import functional as F_
     from elasticmegatron_b200.ops.native import launch_count
 
+    import os
+
+    os.environ["EMB_NATIVE_ATTENTION"] = "1"
     torch.manual_seed(0)
     qkv = torch.randn(256, 1, 2, 4, 128, device="cuda").bfloat16().requires_grad_(True)
     n0 = launch_count()
     y = F_.attention(qkv, 2)
     y.float().pow(2).sum().backward()
     torch.cuda.synchronize()
+    os.environ.pop("EMB_NATIVE_ATTENTION")
     assert launch_count() - n0 >= 4
     x = qkv.detach().float().requires_grad_(True)
     o_ref, _ = _ref(x, 2, True)
