@@ -8,6 +8,7 @@ torch::Tensor arena_alloc(int64_t nbytes, int64_t device);
 torch::Tensor ipc_get_handle(torch::Tensor arena);
 int64_t ipc_open(torch::Tensor handle);
 void ipc_close_all();
+bool ipc_close(torch::Tensor handle);
 int64_t ipc_open_count();
 std::vector<torch::Tensor> rmsnorm_fwd(torch::Tensor x, torch::Tensor w, double eps);
 std::vector<torch::Tensor> rmsnorm_bwd(torch::Tensor dy, torch::Tensor x, torch::Tensor w, torch::Tensor rstd,
@@ -50,6 +51,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("ipc_get_handle", &ipc_get_handle);
   m.def("ipc_open", &ipc_open);
   m.def("ipc_close_all", &ipc_close_all);
+  m.def("ipc_close", &ipc_close);
   m.def("ipc_open_count", &ipc_open_count);
   m.def("rmsnorm_fwd", &rmsnorm_fwd);
   m.def("rmsnorm_bwd", &rmsnorm_bwd, py::arg("dy"), py::arg("x"), py::arg("w"), py::arg("rstd"),

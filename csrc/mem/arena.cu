@@ -60,6 +60,18 @@ int64_t ipc_open(at::Tensor handle) {
   return (int64_t)(uint64_t)p;
 }
 
+// Unmap one peer allocation previously mapped with ipc_open (no-op if it is not mapped).
+bool ipc_close(at::Tensor handle) {
+  TORCH_CHECK(handle.numel() == sizeof(cudaIpcMemHandle_t));
+  std::string key((const char*)handle.data_ptr(), sizeof(cudaIpcMemHandle_t));
+  std::lock_guard<std::mutex> g(g_mu);
+  auto it = g_open.find(key);
+  if (it == g_open.end()) return false;
+  cudaIpcCloseMemHandle((void*)it->second);
+  g_open.erase(it);
+  return true;
+}
+
 void ipc_close_all() {
   std::lock_guard<std::mutex> g(g_mu);
   for (auto& kv : g_open) cudaIpcCloseMemHandle((void*)kv.second);

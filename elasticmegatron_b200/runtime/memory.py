@@ -13,7 +13,6 @@ stay valid.
 """
 from __future__ import annotations
 
-from collections import defaultdict
 from typing import Dict, List, Optional
 
 import torch
@@ -53,44 +52,75 @@ class Arena:
 
 
 class ArenaPool:
-    def __init__(self, device: torch.device):
+    """Size-keyed cache of released arenas.
+
+    ``alloc`` reuses the smallest free arena that is at least the requested size and at most ``slack`` times
+    larger (best fit), so alternating between layouts whose arenas differ only by padding reuses memory and
+    peer mappings.  The free cache is bounded by ``max_cached_bytes`` (default: 40% of the device); older
+    entries beyond it are returned to the driver, and a failed allocation trims the whole cache and retries.
+    """
+
+    def __init__(self, device: torch.device, max_cached_bytes: Optional[int] = None, slack: float = 1.25):
         self.device = torch.device(device)
-        self._free: Dict[int, List[Arena]] = defaultdict(list)
+        self._free: List[Arena] = []
         self.allocated_bytes = 0
+        self.slack = slack
+        if max_cached_bytes is None:
+            total = 0
+            if self.device.type == "cuda":
+                total = torch.cuda.get_device_properties(self.device).total_memory
+            max_cached_bytes = int(0.4 * total) if total else (1 << 62)
+        self.max_cached_bytes = max_cached_bytes
 
     @staticmethod
     def _round(nbytes: int) -> int:
         g = 2 << 20
         return max(g, (nbytes + g - 1) // g * g)
 
+    def cached_bytes(self) -> int:
+        return sum(a.nbytes for a in self._free)
+
+    def _new(self, nbytes: int) -> Arena:
+        if self.device.type == "cuda":
+            from ..ops.native import ext
+
+            dev = self.device.index if self.device.index is not None else torch.cuda.current_device()
+            raw = ext().arena_alloc(nbytes, dev)
+            return Arena(raw, nbytes, True)
+        return Arena(torch.empty(nbytes, dtype=torch.uint8, device=self.device), nbytes, False)
+
     def alloc(self, nbytes: int, zero: bool = False) -> Arena:
         nbytes = self._round(nbytes)
-        lst = self._free.get(nbytes)
-        if lst:
-            a = lst.pop()
+        fits = [a for a in self._free if nbytes <= a.nbytes <= self.slack * nbytes]
+        if fits:
+            a = min(fits, key=lambda x: x.nbytes)
+            self._free.remove(a)
         else:
-            if self.device.type == "cuda":
-                from ..ops.native import ext
-
-                raw = ext().arena_alloc(nbytes, self.device.index if self.device.index is not None
-                                        else torch.cuda.current_device())
-                a = Arena(raw, nbytes, True)
-            else:
-                a = Arena(torch.empty(nbytes, dtype=torch.uint8, device=self.device), nbytes, False)
+            try:
+                a = self._new(nbytes)
+            except RuntimeError:
+                self.trim()
+                a = self._new(nbytes)
             self.allocated_bytes += nbytes
         if zero:
             a.raw.zero_()
         return a
 
     def free(self, a: Optional[Arena]) -> None:
-        if a is not None:
-            self._free[a.nbytes].append(a)
+        if a is None:
+            return
+        self._free.append(a)
+        while self.cached_bytes() > self.max_cached_bytes and self._free:
+            old = self._free.pop(0)
+            self.allocated_bytes -= old.nbytes
+            del old
 
     def trim(self) -> None:
-        """Drop cached free arenas (returns device memory)."""
-        for lst in self._free.values():
-            for a in lst:
-                self.allocated_bytes -= a.nbytes
+        """Return every cached free arena to the driver."""
+        if self.device.type == "cuda":
+            torch.cuda.synchronize(self.device)
+        for a in self._free:
+            self.allocated_bytes -= a.nbytes
         self._free.clear()
 
 

@@ -50,7 +50,7 @@ class NativeP2PEngine:
         assert mode in ("pull", "push")
         self.mode = mode
         self.task_bytes = task_bytes
-        self._handles: Dict[int, bytes] = {}
+        self._mapped: Dict[int, set] = {}
         self._cache: Dict[tuple, Tuple[torch.Tensor, int, int]] = {}
         self._flag = None
         self.bytes_moved = 0
@@ -60,17 +60,14 @@ class NativeP2PEngine:
 
     # ------------------------------------------------------------------ address exchange
     def _local_handle(self, t: Optional[torch.Tensor]):
-        if t is None:
-            return None
-        k = t.data_ptr()
-        h = self._handles.get(k)
-        if h is None:
-            h = _handle_of(t)
-            self._handles[k] = h
-        return h
+        # not cached by address: a pooled arena freed and re-allocated at the same address has a new handle
+        return _handle_of(t) if t is not None else None
 
     def _exchange(self, rank, sp, so, dp, do, union):
-        """All ranks' arena base addresses as seen from this process: {rank: (sp, so, dp, do)}."""
+        """All ranks' arena base addresses as seen from this process: {rank: (sp, so, dp, do)}.
+
+        Mappings of a peer's arenas that the peer no longer advertises are closed, so arenas a peer has
+        returned to the driver are not kept alive by this process."""
         mine = (self._local_handle(sp), self._local_handle(so), self._local_handle(dp), self._local_handle(do))
         objs = [None] * len(union)
         dist.all_gather_object(objs, (rank, mine), group=ProcessGroupPool.get(union, "gloo"))
@@ -79,9 +76,13 @@ class NativeP2PEngine:
         for r, hs in objs:
             if r == rank:
                 out[r] = tuple(t.data_ptr() if t is not None else 0 for t in local)
-            else:
-                out[r] = tuple(int(ext().ipc_open(torch.frombuffer(bytearray(h), dtype=torch.uint8))) if h else 0
-                               for h in hs)
+                continue
+            live = {h for h in hs if h}
+            for h in self._mapped.get(r, set()) - live:
+                ext().ipc_close(torch.frombuffer(bytearray(h), dtype=torch.uint8))
+            self._mapped[r] = live
+            out[r] = tuple(int(ext().ipc_open(torch.frombuffer(bytearray(h), dtype=torch.uint8))) if h else 0
+                           for h in hs)
         return out
 
     # ------------------------------------------------------------------ task building
