@@ -144,8 +144,12 @@ def read_latest(root: str) -> int:
         return int(f.read().strip())
 
 
-def load_checkpoint(ts, root: str, iteration: Optional[int] = None) -> Dict:
-    """Load params + optimizer state (+ scheduler) saved under any strategy into ``ts``'s layout."""
+def read_global_state(root: str, iteration: Optional[int] = None):
+    """Reassemble layout-free global tensors from a checkpoint saved under any strategy.
+
+    Returns ``(params, opt, meta)`` with ``params[vp.index]`` fp32 global tensors, ``opt[vp.index]`` the
+    ``[3, *shape]`` master / exp_avg / exp_avg_sq, and the metadata of the first rank file.
+    """
     args = get_args()
     cfg, tc = args.model, args.train
     if iteration is None:
@@ -186,8 +190,17 @@ def load_checkpoint(ts, root: str, iteration: Optional[int] = None) -> Dict:
                     o = pc.off(gr, pc.gc0)
                     g2[gr, pc.gc0:pc.gc1] = P[o:o + k]
                     o2[:, gr, pc.gc0:pc.gc1] = O[:, o:o + k]
+    meta["saved_strategy"] = saved
+    return g_param, g_opt, meta
+
+
+def load_checkpoint(ts, root: str, iteration: Optional[int] = None) -> Dict:
+    """Load params + optimizer state (+ scheduler) saved under any strategy into ``ts``'s layout."""
     from ..planner.materialize import scatter_to_rank
 
+    args = get_args()
+    cfg, tc = args.model, args.train
+    g_param, g_opt, meta = read_global_state(root, iteration)
     Pc = torch.zeros(ts.param_flat.shape, dtype=torch.float32)
     Oc = torch.zeros(ts.opt_flat.shape, dtype=torch.float32)
     scatter_to_rank(cfg, ts.strategy, ts.rank, g_param, Pc, Oc, g_opt, tc.overlap_grad_reduce, tc.ddp_bucket_size)
@@ -197,5 +210,52 @@ def load_checkpoint(ts, root: str, iteration: Optional[int] = None) -> Dict:
     ts.opt_param_scheduler.load_state_dict(meta["opt_param_scheduler"])
     args.iteration = meta["iteration"]
     args.consumed_train_samples = meta.get("consumed_train_samples", 0)
-    return {"iteration": meta["iteration"], "saved_strategy": saved,
+    return {"iteration": meta["iteration"], "saved_strategy": meta["saved_strategy"],
             "consumed_train_samples": args.consumed_train_samples}
+
+
+def convert_checkpoint(src_root: str, dst_root: str, dst_strategy, iteration: Optional[int] = None) -> None:
+    """Offline re-layout of a checkpoint to another strategy (one process, no process groups)."""
+    from ..planner.materialize import scatter_to_rank
+
+    args = get_args()
+    cfg, tc = args.model, args.train
+    g_param, g_opt, meta = read_global_state(src_root, iteration)
+    dst = ParallelStrategy.from_any(dst_strategy)
+    it = meta["iteration"]
+    for r in range(dst.world_size):
+        c = dst.coords(r)
+        rl = rank_layout(cfg, dst, r, tc.overlap_grad_reduce, tc.ddp_bucket_size)
+        if not (c["dp"] == 0 and c["cp"] == 0 and rl.instance == 0):
+            continue
+        P = torch.zeros(rl.param_numel)
+        Ofull = torch.zeros(3, rl.param_numel)
+        # parameters and the whole TP-local optimizer state (written as if one rank owned every shard)
+        O = torch.zeros(3, rl.opt_numel)
+        scatter_to_rank(cfg, dst, r, g_param, P, O, g_opt, tc.overlap_grad_reduce, tc.ddp_bucket_size)
+        from ..planner.plan import _StrategyView
+
+        view = _StrategyView(cfg, dst, tc.overlap_grad_reduce, tc.ddp_bucket_size)
+        for vp in virtual_params(cfg):
+            if r not in view.holders(vp):
+                continue
+            o2 = g_opt[vp.index].view(3, 1, -1) if len(vp.shape) == 1 else g_opt[vp.index]
+            for pc in view.param_pieces(vp, r):
+                k = pc.gc1 - pc.gc0
+                for gr in range(pc.gr0, pc.gr1):
+                    o = pc.off(gr, pc.gc0)
+                    Ofull[:, o:o + k] = o2[:, gr, pc.gc0:pc.gc1]
+        d = _dir_for(dst, r, dst_root, it)
+        os.makedirs(d, exist_ok=True)
+        names = _local_names(rl)
+        model = {n: P[off:off + int(np.prod(shp))].view(shp).to(cfg.torch_dtype).clone() for n, off, shp, _ in names}
+        optim = {n: Ofull[:, off:off + int(np.prod(shp))].reshape(3, *shp).clone() for n, off, shp, _ in names}
+        state = dict(meta)
+        state.pop("saved_strategy", None)
+        state["args"] = dict(meta["args"])
+        state["args"]["strategy"] = dst.to_dict()
+        state["model"] = model
+        torch.save(state, os.path.join(d, "model_optim_rng.pt"))
+        torch.save(optim, os.path.join(d, "distrib_optim.pt"))
+    with open(os.path.join(dst_root, "latest_checkpointed_iteration.txt"), "w") as f:
+        f.write(str(it))

@@ -157,6 +157,7 @@ def _ckpt(rank, world, root):
     ok = True
     for i in (1, 2):
         live = mgr.reshard(STRATS[i])
+        save_checkpoint(live, f"{root}/live_{i}", iteration=2, consumed_samples=16)
         fresh = TrainingState(S[i])
         info = load_checkpoint(fresh, root)
         ok &= torch.equal(live.param_flat, fresh.param_flat) and torch.equal(live.opt_flat, fresh.opt_flat)
@@ -177,6 +178,19 @@ def test_checkpoint_save_a_load_b_equals_live_reshard(tmp_path):
     st = torch.load(it / "mp_rank_00" / "model_optim_rng.pt", weights_only=False)
     assert "decoder.layers.0.self_attention.linear_qkv.weight" in st["model"]
     assert st["iteration"] == 2
+    # offline conversion DP2 -> TP2 / PP2 equals the checkpoint of the live resharded state
+    from elasticmegatron_b200.runtime.checkpoint import convert_checkpoint
+    from elasticmegatron_b200.tools.compare_ckpt import compare
+
+    _setup()
+    for i in (1, 2):
+        conv = tmp_path / f"conv_{i}"
+        convert_checkpoint(str(tmp_path), str(conv), STRATS[i])
+        assert compare(str(conv / "iter_0000002"), str(tmp_path / f"live_{i}" / "iter_0000002"), 0.0) == []
+        for sub in os.listdir(conv / "iter_0000002"):
+            a = torch.load(conv / "iter_0000002" / sub / "distrib_optim.pt")
+            b = torch.load(tmp_path / f"live_{i}" / "iter_0000002" / sub / "distrib_optim.pt")
+            assert a.keys() == b.keys() and all(torch.equal(a[k], b[k]) for k in a)
 
 
 def _hetero(rank, world, strat_idx):
