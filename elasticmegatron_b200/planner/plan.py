@@ -229,12 +229,19 @@ def _merge_rows(rows, cols, sst, dstd):
 
 
 def build_plan(src, dst, cfg: Optional[ModelConfig] = None, kinds: Iterable[int] = (KIND_OPT, KIND_PARAM),
-               overlap_grad_reduce: Optional[bool] = None, ddp_bucket_size: Optional[int] = None) -> ReshardPlan:
+               overlap_grad_reduce: Optional[bool] = None, ddp_bucket_size: Optional[int] = None,
+               allowed_src: Optional[Iterable[int]] = None) -> ReshardPlan:
+    """Plan the switch ``src -> dst``.
+
+    ``allowed_src`` restricts which source ranks may be read (failure recovery: only survivors); a piece of
+    state with no allowed holder raises ``RuntimeError`` (the state is lost without a Group-ZeRO replica).
+    """
     args = get_args()
     cfg = cfg or args.model
     if overlap_grad_reduce is None:
         overlap_grad_reduce = args.train.overlap_grad_reduce
         ddp_bucket_size = args.train.ddp_bucket_size
+    allowed = set(allowed_src) if allowed_src is not None else None
     sv = _StrategyView(cfg, src, overlap_grad_reduce, ddp_bucket_size)
     dv = _StrategyView(cfg, dst, overlap_grad_reduce, ddp_bucket_size)
     recs = []
@@ -258,7 +265,10 @@ def build_plan(src, dst, cfg: Optional[ModelConfig] = None, kinds: Iterable[int]
                     dp = dv.param_pieces(vp, d) if kind == KIND_PARAM else dv.opt_pieces(vp, d)
                     dcache[dkey] = dp
                 for members, spcs in src_pieces:
-                    srank = _choose(members, d, vp.index)
+                    cands = members if allowed is None else [m for m in members if m in allowed]
+                    if not cands:
+                        raise RuntimeError(f"no surviving source holds {vp.name} (kind {kind}) for rank {d}")
+                    srank = _choose(cands, d, vp.index)
                     for sp in spcs:
                         for dpp in dp:
                             box = _intersect(sp, dpp)

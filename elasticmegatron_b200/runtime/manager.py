@@ -203,6 +203,47 @@ class ElasticMegatronManager:
             save_checkpoint(dst, ckpt_dir or "after_reshard")
         return dst
 
+    def recover(self, new_parallel_strategy, failed_ranks, logger: Optional[logging.Logger] = None):
+        """Continue on ``new_parallel_strategy`` after ``failed_ranks`` died (detected by ``runtime/health.py``).
+
+        Only the destination ranks take part: they must all be alive, every collective runs on the
+        destination's own groups (a dead rank is never waited on), and the plan reads only destination ranks
+        that hold source state - typically the surviving Group-ZeRO replica.  Raises ``RuntimeError`` when some
+        state has no surviving holder.  Survivors outside the destination just stop (returns ``None``).
+        """
+        dst_s = ParallelStrategy.from_any(new_parallel_strategy)
+        failed = set(failed_ranks)
+        assert not (failed & set(dst_s.ranks)), "the recovery strategy must not contain failed ranks"
+        src_s = self.current
+        if self._rank not in dst_s.ranks:
+            self.current = dst_s
+            return None
+        src = self._states.get(src_s)
+        dst = self._get_or_build(dst_s, False)
+        plan = build_plan(src_s, dst_s, allowed_src=set(dst_s.ranks) - failed)
+        group = ProcessGroupPool.get(dst_s.ranks)
+        eng = self.engine
+        eng.execute(plan, self._rank, src.param_flat if src else None, src.opt_flat if src else None,
+                    dst.param_flat, dst.opt_flat, group)
+        if not getattr(eng, "moves_params", True):
+            dst.update_model_weight()
+        obj = [None]
+        if self._rank == 0 and src is not None:
+            obj = [{"opt": src.optimizer.state_dict(), "sched": src.opt_param_scheduler.state_dict()}]
+        if dist.is_initialized() and dst_s.world_size > 1:
+            dist.broadcast_object_list(obj, src=0, group=ProcessGroupPool.get(dst_s.ranks, "gloo"))
+        if obj[0] is not None:
+            dst.optimizer.load_state_dict(obj[0]["opt"])
+            dst.opt_param_scheduler.load_state_dict(obj[0]["sched"])
+        if src is not None and src is not dst:
+            src.release()
+        self.current = dst_s
+        set_world_group(ProcessGroupPool.get(dst_s.ranks))
+        dst.ddp.zero_grad()
+        if self._rank == 0 or logger is not None:
+            log_json("recover", logger, src=str(src_s), dst=str(dst_s), failed=sorted(failed))
+        return dst
+
     # ------------------------------------------------------------------ internals
     def _transfer(self, plan, src, dst, ugroup, same_layout: bool):
         eng = self.engine
