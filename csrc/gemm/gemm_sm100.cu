@@ -332,13 +332,15 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 //   tempty[b] - leader only; all 8 epilogue warps of the pair arrive (remote arrive from the peer).
 // TMA loads never use cluster multicast.
 namespace gk2 {
-constexpr int BM = 256, BN = 256, BK = 64, STAGES = 6;
+constexpr int BM = 256, BN = 256, BK = 64, STAGES = 5;
 constexpr int A_HALF = 128 * BK * 2;  // 16 KiB per CTA
 constexpr int B_HALF = 128 * BK * 2;  // 16 KiB per CTA
 constexpr int STAGE_BYTES = A_HALF + B_HALF;
 constexpr int TMEM_COLS = 512;
 constexpr int NUM_THREADS = 192;
-constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 256;
+constexpr int EPI_STRIDE = 144;  // 128-byte rows padded to 144 B: a warp's 16-byte writes hit 4-way banks
+constexpr int EPI_BYTES = 2 * 128 * EPI_STRIDE;  // double-buffered epilogue staging
+constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + EPI_BYTES + 1024 + 256;
 
 __device__ __forceinline__ uint32_t cluster_rank() {
   uint32_t r;
@@ -390,7 +392,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
   uint8_t* sB = smem + STAGES * A_HALF;
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
+  uint8_t* sEpi = smem + STAGES * STAGE_BYTES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES + EPI_BYTES);
   uint64_t* empty = full + STAGES;
   uint64_t* tfull = empty + STAGES;  // [2]
   uint64_t* tempty = tfull + 2;      // [2]
@@ -497,6 +500,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     const int quarter = warp & 3;
     const int row_in_half = quarter * 32 + lane;
     int local = 0;
+    uint32_t epi_n = 0;  // bulk groups issued by this thread (selects the staging buffer)
     for (int t = cluster_id; t < num_tiles; t += num_clusters, ++local) {
       const int buf = local & 1;
       const uint32_t tph = (local >> 1) & 1;
@@ -514,6 +518,46 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         const int col0 = n0 + c * 32;
         if (!row_ok || col0 >= p.N) continue;
         const int ncols = min(32, p.N - col0);
+        void* gdst = p.out_fp32 ? (void*)(reinterpret_cast<float*>(p.C) + (size_t)row * p.ldc + col0)
+                                : (void*)(reinterpret_cast<__nv_bfloat16*>(p.C) + (size_t)row * p.ldc + col0);
+        if (ncols == 32 && ((reinterpret_cast<uintptr_t>(gdst) & 15) == 0)) {
+          // stage the row chunk in shared memory and hand it to the bulk-copy engine: a plain store, or an
+          // fp32 add-reduction into C (the wgrad accumulate), without the read-modify-write round trip
+          uint8_t* srow = sEpi + (epi_n & 1) * (128 * EPI_STRIDE) + row_in_half * EPI_STRIDE;
+          asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+          uint32_t bytes;
+          if (p.out_fp32) {
+#pragma unroll
+            for (int v = 0; v < 8; ++v) {
+              *reinterpret_cast<float4*>(srow + v * 16) =
+                  make_float4(__uint_as_float(r[4 * v]), __uint_as_float(r[4 * v + 1]),
+                              __uint_as_float(r[4 * v + 2]), __uint_as_float(r[4 * v + 3]));
+            }
+            bytes = 128;
+          } else {
+#pragma unroll
+            for (int v = 0; v < 4; ++v) {
+              float f[8];
+#pragma unroll
+              for (int j = 0; j < 8; ++j) f[j] = __uint_as_float(r[8 * v + j]);
+              *reinterpret_cast<uint4*>(srow + v * 16) = pack8(f);
+            }
+            bytes = 64;
+          }
+          asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+          if (p.accumulate) {
+            asm volatile("cp.reduce.async.bulk.global.shared::cta.bulk_group.add.f32 [%0], [%1], %2;" ::"l"(gdst),
+                         "r"(smem_u32(srow)), "r"(bytes)
+                         : "memory");
+          } else {
+            asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(gdst),
+                         "r"(smem_u32(srow)), "r"(bytes)
+                         : "memory");
+          }
+          asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+          ++epi_n;
+          continue;
+        }
         if (p.out_fp32) {
           float* dst = reinterpret_cast<float*>(p.C) + (size_t)row * p.ldc + col0;
           if (ncols == 32 && ((reinterpret_cast<uintptr_t>(dst) & 15) == 0)) {
@@ -558,6 +602,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       __syncwarp();
       if (lane == 0) remote_arrive(mapa(smem_u32(&tempty[buf]), 0));
     }
+    asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
   }
 
   tc_fence_before();
