@@ -59,6 +59,7 @@ def main():
     ap.add_argument("--iters", type=int, default=3)
     ap.add_argument("--link-gbs", type=float, default=770.0)
     ap.add_argument("--out", default=None)
+    ap.add_argument("--mode", default="pull", choices=["pull", "push"], help="native engine: who runs each copy")
     args = ap.parse_args()
 
     import datetime
@@ -149,11 +150,11 @@ def main():
         return t.tolist(), int(m.sum()), roof
 
     for eng_name in args.engines.split(","):
-        eng = engines[eng_name]()
+        eng = engines[eng_name](mode=args.mode) if eng_name == "native" else engines[eng_name]()
         for a, b in pairs:
             ts, nbytes, roof = run_pair(eng_name, eng, a, b, args.iters)
             p50 = statistics.median(ts)
-            rec = {"engine": eng_name, "src": str(a), "dst": str(b), "p50_ms": p50, "all_ms": ts,
+            rec = {"engine": eng_name + (f"-{args.mode}" if eng_name == "native" else ""), "src": str(a), "dst": str(b), "p50_ms": p50, "all_ms": ts,
                    "bytes_moved": nbytes, "roofline_ms": roof, "roofline_frac": (roof / p50) if p50 else None}
             results.append(rec)
             if rank == 0:
