@@ -131,6 +131,13 @@ struct Params {
   int accumulate;  // C += (fp32 only)
   int a_mn, b_mn;  // operand majorness
   int* err;
+  // reduce-scatter epilogue (2-SM kernel only): when scatter != 0, output row `row` belongs to TP rank
+  // owner = row / rows_per_rank and is written (bf16) into that rank's staging buffer peer_out[owner] at slot
+  // `my_slot`: peer_out[owner] + (my_slot * rows_per_rank + row % rows_per_rank) * ldc + col.
+  int scatter;
+  int rows_per_rank;
+  int my_slot;
+  void* peer_out[8];
 };
 
 __global__ void __launch_bounds__(NUM_THREADS, 1)
@@ -518,6 +525,27 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         const int col0 = n0 + c * 32;
         if (!row_ok || col0 >= p.N) continue;
         const int ncols = min(32, p.N - col0);
+        if (p.scatter) {
+          // fused reduce-scatter: this partial row chunk goes straight to its owner's staging slot (peer
+          // memory over NVLink; plain stores are posted, so the math of the next tiles overlaps the transfer)
+          const int owner = row / p.rows_per_rank;
+          __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(p.peer_out[owner]) +
+                               ((size_t)p.my_slot * p.rows_per_rank + (row - owner * p.rows_per_rank)) * p.ldc + col0;
+          if (ncols == 32) {
+#pragma unroll
+            for (int v = 0; v < 4; ++v) {
+              float f[8];
+#pragma unroll
+              for (int j = 0; j < 8; ++j) f[j] = __uint_as_float(r[8 * v + j]);
+              reinterpret_cast<uint4*>(dst)[v] = pack8(f);
+            }
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              if (j < ncols) dst[j] = __float2bfloat16_rn(__uint_as_float(r[j]));
+          }
+          continue;
+        }
         void* gdst = p.out_fp32 ? (void*)(reinterpret_cast<float*>(p.C) + (size_t)row * p.ldc + col0)
                                 : (void*)(reinterpret_cast<__nv_bfloat16*>(p.C) + (size_t)row * p.ldc + col0);
         if (ncols == 32 && ((reinterpret_cast<uintptr_t>(gdst) & 15) == 0)) {
@@ -697,7 +725,7 @@ at::Tensor gemm_tc(at::Tensor a, at::Tensor b, bool trans_a, bool trans_b, c10::
   const bool a_mn = trans_a, b_mn = !trans_b;
   CUtensorMap tA = a_mn ? make_map(a.data_ptr(), K, M, a.stride(0), 64, 64) : make_map(a.data_ptr(), M, K, a.stride(0), 64, BM);
   CUtensorMap tB = b_mn ? make_map(b.data_ptr(), K, N, b.stride(0), 64, 64) : make_map(b.data_ptr(), N, K, b.stride(0), 64, BN);
-  Params p;
+  Params p{};
   p.C = C.data_ptr();
   p.M = (int)M;
   p.N = (int)N;
@@ -747,6 +775,90 @@ at::Tensor gemm_tc(at::Tensor a, at::Tensor b, bool trans_a, bool trans_b, c10::
   EMB_LAUNCH_CHECK();
   count_launch();
   return C;
+}
+
+// out_local[i, n] = sum_s stage[s, i, n] over the TP slots (bf16 in, fp32 sum, bf16 out)
+__global__ void rs_reduce_kernel(const __nv_bfloat16* __restrict__ stage, __nv_bfloat16* __restrict__ out,
+                                 int64_t slot_elems, int tp) {
+  const int64_t nv = slot_elems / 8;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < nv; i += (int64_t)gridDim.x * blockDim.x) {
+    float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    for (int sl = 0; sl < tp; ++sl) {
+      float f[8];
+      unpack8(reinterpret_cast<const uint4*>(stage + sl * slot_elems)[i], f);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) acc[k] += f[k];
+    }
+    reinterpret_cast<uint4*>(out)[i] = pack8(acc);
+  }
+}
+
+// Fused GEMM -> reduce-scatter over `tp` ranks: op(a) @ op(b) = [M, N] partial, M = tp * rows_per_rank; row
+// block `o` is written into rank o's staging buffer (peer pointers `peers`, int64 [tp]) at slot `my_slot`.
+// The caller orders it with barriers and then runs rs_reduce on its own staging buffer.
+void gemm_rs(at::Tensor a, at::Tensor b, bool trans_a, bool trans_b, at::Tensor peers, int64_t my_slot,
+             int64_t rows_per_rank) {
+  using namespace gk;
+  TORCH_CHECK(gemm_tc_supported(a, b, trans_a, trans_b, c10::nullopt, false), "gemm_rs: unsupported operands");
+  const int64_t M = trans_a ? a.size(1) : a.size(0);
+  const int64_t K = trans_a ? a.size(0) : a.size(1);
+  const int64_t N = trans_b ? b.size(0) : b.size(1);
+  const int64_t tp = peers.numel();
+  TORCH_CHECK(tp >= 1 && tp <= 8 && M == tp * rows_per_rank && N % 8 == 0,
+              "gemm_rs: M must equal tp * rows_per_rank, tp <= 8, N % 8 == 0");
+  auto pc = peers.to(at::kCPU).contiguous();
+  const bool a_mn = trans_a, b_mn = !trans_b;
+  CUtensorMap tA = a_mn ? make_map(a.data_ptr(), K, M, a.stride(0), 64, 64) : make_map(a.data_ptr(), M, K, a.stride(0), 64, 128);
+  CUtensorMap tB = b_mn ? make_map(b.data_ptr(), K, N, b.stride(0), 64, 64) : make_map(b.data_ptr(), N, K, b.stride(0), 64, 128);
+  Params p{};
+  p.C = nullptr;
+  p.M = (int)M;
+  p.N = (int)N;
+  p.K = (int)K;
+  p.ldc = (int)N;
+  p.a_mn = a_mn;
+  p.b_mn = b_mn;
+  p.err = err_flag();
+  p.scatter = 1;
+  p.rows_per_rank = (int)rows_per_rank;
+  p.my_slot = (int)my_slot;
+  for (int64_t i = 0; i < tp; ++i) p.peer_out[i] = reinterpret_cast<void*>(pc.data_ptr<int64_t>()[i]);
+  static bool attr2 = false;
+  if (!attr2) {
+    EMB_CUDA_CHECK(cudaFuncSetAttribute(gk2::gemm2_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        gk2::SMEM_BYTES));
+    attr2 = true;
+  }
+  const int64_t tiles2 = ((M + 255) / 256) * ((N + 255) / 256);
+  const int clusters = (int)std::min<int64_t>(tiles2, num_sms() / 2);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(2 * clusters, 1, 1);
+  cfg.blockDim = dim3(gk2::NUM_THREADS, 1, 1);
+  cfg.dynamicSmemBytes = gk2::SMEM_BYTES;
+  cfg.stream = cur_stream();
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  EMB_CUDA_CHECK(cudaLaunchKernelEx(&cfg, gk2::gemm2_kernel, tA, tB, p));
+  count_launch();
+}
+
+at::Tensor rs_reduce(at::Tensor stage, int64_t tp, int64_t rows, int64_t n) {
+  TORCH_CHECK(stage.is_cuda() && stage.scalar_type() == at::kBFloat16 && stage.numel() >= tp * rows * n);
+  TORCH_CHECK(n % 8 == 0);
+  auto out = at::empty({rows, n}, stage.options());
+  const int64_t slot = rows * n;
+  const int64_t nv = slot / 8;
+  const int grid = (int)std::max<int64_t>(1, std::min<int64_t>((nv + 255) / 256, (int64_t)num_sms() * 8));
+  rs_reduce_kernel<<<grid, 256, 0, cur_stream()>>>(reinterpret_cast<const __nv_bfloat16*>(stage.data_ptr()),
+                                                   reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), slot, (int)tp);
+  EMB_LAUNCH_CHECK();
+  count_launch();
+  return out;
 }
 
 int64_t gemm_error_flag() {

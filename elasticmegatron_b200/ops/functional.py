@@ -15,6 +15,7 @@ import torch
 import torch.distributed as dist
 
 from . import reference as ref
+from . import tp_fused
 from .native import use_native, ext
 
 
@@ -167,6 +168,8 @@ class LinearFn(torch.autograd.Function):
         if mode == "col_sp":
             xf = _all_gather_dim0(x2, group)
             y = gemm(xf, w, trans_b=True)
+        elif mode == "row_sp" and tp_fused.eligible(x2, w, False, True, group):
+            y = tp_fused.gemm_reduce_scatter(x2, w, False, True, group)
         else:
             y = gemm(x2, w, trans_b=True)
             if mode == "row_sp":
@@ -184,11 +187,14 @@ class LinearFn(torch.autograd.Function):
         if mode == "row_sp":
             dy2 = _all_gather_dim0(dy2, group)
         xf = _all_gather_dim0(x2, group) if mode == "col_sp" else x2
-        dx = gemm(dy2, w)  # [M,N] @ [N,K]
-        if mode == "col_sp":
-            dx = _reduce_scatter_dim0(dx, group)
-        elif mode == "col":
-            dx = _all_reduce(dx, group)
+        if mode == "col_sp" and tp_fused.eligible(dy2, w, False, False, group):
+            dx = tp_fused.gemm_reduce_scatter(dy2, w, False, False, group)
+        else:
+            dx = gemm(dy2, w)  # [M,N] @ [N,K]
+            if mode == "col_sp":
+                dx = _reduce_scatter_dim0(dx, group)
+            elif mode == "col":
+                dx = _all_reduce(dx, group)
         dw = _accumulate_wgrad(w, dy2, xf)
         return dx, dw, None, None
 
