@@ -59,7 +59,7 @@ def main():
     ap.add_argument("--iters", type=int, default=3)
     ap.add_argument("--link-gbs", type=float, default=770.0)
     ap.add_argument("--out", default=None)
-    ap.add_argument("--mode", default="pull", choices=["pull", "push"], help="native engine: who runs each copy")
+    ap.add_argument("--mode", default="push", choices=["pull", "push"], help="native engine: who runs each copy")
     args = ap.parse_args()
 
     import datetime

@@ -4,8 +4,10 @@ Every rank exports its state arenas (source and destination parameters / optimiz
 handles once; peers map them once (the mappings are cached for the life of the process and the arena pool
 reuses arenas, so repeated switches map nothing new).  For a switch each rank turns the plan's descriptors
 into 64-byte copy tasks with *device* addresses - its own arenas or a peer's mapping - and runs them all in one
-``reshard_copy`` launch.  In pull mode (default) a rank executes the copies whose destination it owns, reading
-peers over NVLink; in push mode it executes the copies whose source it owns, writing peers.
+``reshard_copy`` launch.  In push mode (default) a rank executes the copies whose source it owns, writing peers
+over NVLink; in pull mode it executes the copies whose destination it owns, reading peers.  Measured on B200
+(13B-shaped state, 2 GPUs) push reaches 0.65-0.74 of the NVLink roofline against 0.49-0.61 for pull: NVLink
+writes carry their data in the request, reads need a request/response round trip.
 
 Ordering: a 1-element NCCL all-reduce over the union group is issued on the compute stream before and after
 the launch.  The first guarantees every peer finished producing its source state (previous optimizer step)
@@ -46,7 +48,7 @@ def _handle_of(t: Optional[torch.Tensor]):
 class NativeP2PEngine:
     name = "native"
 
-    def __init__(self, mode: str = "pull", task_bytes: int = 1 << 20):
+    def __init__(self, mode: str = "push", task_bytes: int = 1 << 20):
         assert mode in ("pull", "push")
         self.mode = mode
         self.task_bytes = task_bytes
