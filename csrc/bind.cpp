@@ -44,6 +44,8 @@ int64_t gemm_error_flag();
 void gemm_rs(torch::Tensor a, torch::Tensor b, bool trans_a, bool trans_b, torch::Tensor peers, int64_t my_slot,
              int64_t rows_per_rank);
 torch::Tensor rs_reduce(torch::Tensor stage, int64_t tp, int64_t rows, int64_t n);
+torch::Tensor gemm_ag(torch::Tensor local, torch::Tensor b, bool trans_b, torch::Tensor peers, int64_t my_slot,
+                      int64_t rows_per_rank, torch::Tensor ready);
 }  // namespace emb
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -86,6 +88,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_error_flag", &gemm_error_flag);
   m.def("gemm_rs", &gemm_rs);
   m.def("rs_reduce", &rs_reduce);
+  m.def("gemm_ag", &gemm_ag);
   m.def("gemm_tc_supported", &gemm_tc_supported, py::arg("a"), py::arg("b"), py::arg("trans_a") = false,
         py::arg("trans_b") = false, py::arg("out") = py::none(), py::arg("accumulate") = false);
 }

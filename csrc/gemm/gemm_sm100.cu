@@ -138,6 +138,13 @@ struct Params {
   int rows_per_rank;
   int my_slot;
   void* peer_out[8];
+  // all-gather prologue (2-SM kernel, AG template only): A rows are gathered from TP peers into the local
+  // buffer ag_local [M, K] (K-major, chunk c = rows [c*rows_per_rank, (c+1)*rows_per_rank) from ag_src[c]);
+  // ready[c] counts finished pieces of chunk c, ready[ag_tp + c] hands out pieces.
+  const void* ag_src[8];
+  void* ag_local;
+  int* ready;
+  int ag_tp;
 };
 
 __global__ void __launch_bounds__(NUM_THREADS, 1)
@@ -345,6 +352,8 @@ constexpr int B_HALF = 128 * BK * 2;  // 16 KiB per CTA
 constexpr int STAGE_BYTES = A_HALF + B_HALF;
 constexpr int TMEM_COLS = 512;
 constexpr int NUM_THREADS = 192;
+constexpr int NUM_THREADS_AG = 256;  // + 2 copy warps for the all-gather prologue
+constexpr int AG_PIECES = 64;        // claimable pieces per gathered chunk
 constexpr int EPI_STRIDE = 144;  // 128-byte rows padded to 144 B: a warp's 16-byte writes hit 4-way banks
 constexpr int EPI_BYTES = 2 * 128 * EPI_STRIDE;  // double-buffered epilogue staging
 constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + EPI_BYTES + 1024 + 256;
@@ -392,7 +401,23 @@ __host__ __device__ constexpr uint32_t make_idesc2(bool a_mn, bool b_mn) {
          ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
 }
 
-__global__ void __launch_bounds__(NUM_THREADS, 1)
+// bounded acquire-wait until *ctr >= target (all-gather chunk readiness); false on timeout
+__device__ __forceinline__ bool wait_counter(const int* ctr, int target, int* err, int code) {
+  for (uint32_t i = 0; i < gk::WAIT_LIMIT; ++i) {
+    int v;
+    asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(ctr) : "memory");
+    if (v >= target) {
+      asm volatile("fence.proxy.async.global;" ::: "memory");  // the TMA reads that follow see the copies
+      return true;
+    }
+    __nanosleep(128);
+  }
+  atomicExch(err, code);
+  return false;
+}
+
+template <bool AG>
+__global__ void __launch_bounds__(AG ? NUM_THREADS_AG : NUM_THREADS, 1)
     gemm2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, gk::Params p) {
   using namespace gk;
   extern __shared__ uint8_t smem_raw[];
@@ -417,6 +442,15 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   const int tiles_n = (p.N + BN - 1) / BN;
   const int num_tiles = tiles_m * tiles_n;
   const int nk = (p.K + BK - 1) / BK;
+  // tile -> (m block, n block).  With the all-gather prologue, n varies fastest and m blocks start at this
+  // rank's own chunk, so the first tiles never wait for a peer's rows.
+  const int my_chunk = AG ? p.my_slot : 0;
+  const int mt_per_chunk = AG ? p.rows_per_rank / BM : 1;
+  auto tile_m = [&](int t) -> int {
+    if (!AG) return t % tiles_m;
+    return (t / tiles_n + my_chunk * mt_per_chunk) % tiles_m;
+  };
+  auto tile_n = [&](int t) -> int { return AG ? t % tiles_n : t / tiles_m; };
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -447,8 +481,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       int it = 0;
       bool ok = true;
       for (int t = cluster_id; t < num_tiles && ok; t += num_clusters) {
-        const int m0 = (t % tiles_m) * BM + 128 * rank;
-        const int n0 = (t / tiles_m) * BN + 128 * rank;
+        const int m0 = tile_m(t) * BM + 128 * rank;
+        const int n0 = tile_n(t) * BN + 128 * rank;
+        if (AG) {
+          const int c = m0 / p.rows_per_rank;
+          if (c != my_chunk && !wait_counter(&p.ready[c], AG_PIECES, p.err, 15)) { ok = false; *abort_flag = 1; break; }
+        }
         for (int kb = 0; kb < nk; ++kb, ++it) {
           const int s = it % STAGES;
           const uint32_t ph = (it / STAGES) & 1;
@@ -503,6 +541,42 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         if (ok) commit_pair(&tfull[buf]);
       }
     }
+  } else if (AG && warp >= 6) {
+    // ------------------------------------------------------------------ all-gather copy warps
+    // Each peer chunk is cut into AG_PIECES pieces that any CTA's copy warps claim with an atomic counter
+    // (so the resident CTAs finish all copies even if others are not yet scheduled); a claimed piece is
+    // pulled from the peer's buffer over NVLink with 16-byte loads and counted into ready[c].
+    __shared__ int claimed;
+    const int ct = threadIdx.x - 192;  // 0..63
+    const size_t row_bytes = (size_t)p.K * 2;
+    const int rows_per_piece = (p.rows_per_rank + AG_PIECES - 1) / AG_PIECES;
+    for (int i = 1; i < p.ag_tp; ++i) {
+      const int c = (my_chunk + i) % p.ag_tp;
+      while (true) {
+        if (ct == 0) claimed = atomicAdd(&p.ready[p.ag_tp + c], 1);
+        asm volatile("bar.sync 2, 64;" ::: "memory");
+        const int piece = claimed;
+        asm volatile("bar.sync 2, 64;" ::: "memory");
+        if (piece >= AG_PIECES) break;
+        const int r0 = piece * rows_per_piece, r1 = min(p.rows_per_rank, r0 + rows_per_piece);
+        if (r0 < r1) {
+          const size_t off = ((size_t)c * p.rows_per_rank + r0) * row_bytes;
+          const uint4* src = reinterpret_cast<const uint4*>(reinterpret_cast<const uint8_t*>(p.ag_src[c]) + off);
+          uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(p.ag_local) + off);
+          const size_t nv = (size_t)(r1 - r0) * row_bytes / 16;
+          size_t v = ct;
+          for (; v + 64 * 3 < nv; v += 64 * 4) {
+            uint4 x0 = src[v], x1 = src[v + 64], x2 = src[v + 128], x3 = src[v + 192];
+            dst[v] = x0; dst[v + 64] = x1; dst[v + 128] = x2; dst[v + 192] = x3;
+          }
+          for (; v < nv; v += 64) dst[v] = src[v];
+        }
+        asm volatile("fence.proxy.async.global;" ::: "memory");
+        __threadfence();
+        asm volatile("bar.sync 2, 64;" ::: "memory");
+        if (ct == 0) atomicAdd(&p.ready[c], 1);
+      }
+    }
   } else {
     const int quarter = warp & 3;
     const int row_in_half = quarter * 32 + lane;
@@ -513,8 +587,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       const uint32_t tph = (local >> 1) & 1;
       if (!mbar_wait(&tfull[buf], tph, p.err, 14) || *abort_flag) { *abort_flag = 1; break; }
       tc_fence_after();
-      const int row = (t % tiles_m) * BM + 128 * rank + row_in_half;
-      const int n0 = (t / tiles_m) * BN;
+      const int row = tile_m(t) * BM + 128 * rank + row_in_half;
+      const int n0 = tile_n(t) * BN;
       const bool row_ok = row < p.M;
 #pragma unroll 1
       for (int c = 0; c < BN / 32; ++c) {
@@ -744,7 +818,7 @@ at::Tensor gemm_tc(at::Tensor a, at::Tensor b, bool trans_a, bool trans_b, c10::
     CUtensorMap tB2 = b_mn ? tB : make_map(b.data_ptr(), N, K, b.stride(0), 64, 128);
     static bool attr2 = false;
     if (!attr2) {
-      EMB_CUDA_CHECK(cudaFuncSetAttribute(gk2::gemm2_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+      EMB_CUDA_CHECK(cudaFuncSetAttribute(gk2::gemm2_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                           gk2::SMEM_BYTES));
       attr2 = true;
     }
@@ -761,7 +835,7 @@ at::Tensor gemm_tc(at::Tensor a, at::Tensor b, bool trans_a, bool trans_b, c10::
     attr[0].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    EMB_CUDA_CHECK(cudaLaunchKernelEx(&cfg, gk2::gemm2_kernel, tA2, tB2, p));
+    EMB_CUDA_CHECK(cudaLaunchKernelEx(&cfg, gk2::gemm2_kernel<false>, tA2, tB2, p));
   } else {
     static bool attr_set = false;
     if (!attr_set) {
@@ -825,7 +899,7 @@ void gemm_rs(at::Tensor a, at::Tensor b, bool trans_a, bool trans_b, at::Tensor 
   for (int64_t i = 0; i < tp; ++i) p.peer_out[i] = reinterpret_cast<void*>(pc.data_ptr<int64_t>()[i]);
   static bool attr2 = false;
   if (!attr2) {
-    EMB_CUDA_CHECK(cudaFuncSetAttribute(gk2::gemm2_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    EMB_CUDA_CHECK(cudaFuncSetAttribute(gk2::gemm2_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                         gk2::SMEM_BYTES));
     attr2 = true;
   }
@@ -843,8 +917,67 @@ void gemm_rs(at::Tensor a, at::Tensor b, bool trans_a, bool trans_b, at::Tensor 
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  EMB_CUDA_CHECK(cudaLaunchKernelEx(&cfg, gk2::gemm2_kernel, tA, tB, p));
+  EMB_CUDA_CHECK(cudaLaunchKernelEx(&cfg, gk2::gemm2_kernel<false>, tA, tB, p));
   count_launch();
+}
+
+// Fused all-gather -> GEMM: C[M, N] = A_full @ op(b) where A_full [M, K] = concat over tp ranks of their
+// [rows_per_rank, K] shards.  `local` is this rank's gather buffer (its own chunk already in place); `peers`
+// (int64 [tp]) are the peers' gather buffers (CUDA-IPC mapped) holding their own chunks at the same offsets;
+// `ready` is an int32 [2 * tp] zero-filled array (completed and claimed pieces per chunk).  The kernel pulls the missing chunks while it computes.
+at::Tensor gemm_ag(at::Tensor local, at::Tensor b, bool trans_b, at::Tensor peers, int64_t my_slot,
+                   int64_t rows_per_rank, at::Tensor ready) {
+  using namespace gk;
+  TORCH_CHECK(gemm_tc_supported(local, b, false, trans_b, c10::nullopt, false), "gemm_ag: unsupported operands");
+  const int64_t M = local.size(0), K = local.size(1);
+  const int64_t N = trans_b ? b.size(0) : b.size(1);
+  const int64_t tp = peers.numel();
+  TORCH_CHECK(tp >= 1 && tp <= 8 && M == tp * rows_per_rank && rows_per_rank % 256 == 0 && (K * 2) % 16 == 0,
+              "gemm_ag: rows per rank must be a multiple of 256, tp <= 8");
+  TORCH_CHECK(ready.is_cuda() && ready.scalar_type() == at::kInt && ready.numel() >= 2 * tp);
+  auto pc = peers.to(at::kCPU).contiguous();
+  const bool b_mn = !trans_b;
+  CUtensorMap tA = make_map(local.data_ptr(), M, K, local.stride(0), 64, 128);
+  CUtensorMap tB = b_mn ? make_map(b.data_ptr(), K, N, b.stride(0), 64, 64) : make_map(b.data_ptr(), N, K, b.stride(0), 64, 128);
+  auto C = at::empty({M, N}, local.options());
+  Params p{};
+  p.C = C.data_ptr();
+  p.M = (int)M;
+  p.N = (int)N;
+  p.K = (int)K;
+  p.ldc = (int)N;
+  p.a_mn = 0;
+  p.b_mn = b_mn;
+  p.err = err_flag();
+  p.rows_per_rank = (int)rows_per_rank;
+  p.my_slot = (int)my_slot;
+  p.ag_local = local.data_ptr();
+  p.ready = ready.data_ptr<int>();
+  p.ag_tp = (int)tp;
+  for (int64_t i = 0; i < tp; ++i) p.ag_src[i] = reinterpret_cast<const void*>(pc.data_ptr<int64_t>()[i]);
+  static bool attr = false;
+  if (!attr) {
+    EMB_CUDA_CHECK(cudaFuncSetAttribute(gk2::gemm2_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        gk2::SMEM_BYTES));
+    attr = true;
+  }
+  const int64_t tiles2 = ((M + 255) / 256) * ((N + 255) / 256);
+  const int clusters = (int)std::min<int64_t>(tiles2, num_sms() / 2);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(2 * clusters, 1, 1);
+  cfg.blockDim = dim3(gk2::NUM_THREADS_AG, 1, 1);
+  cfg.dynamicSmemBytes = gk2::SMEM_BYTES;
+  cfg.stream = cur_stream();
+  cudaLaunchAttribute attr2[1];
+  attr2[0].id = cudaLaunchAttributeClusterDimension;
+  attr2[0].val.clusterDim.x = 2;
+  attr2[0].val.clusterDim.y = 1;
+  attr2[0].val.clusterDim.z = 1;
+  cfg.attrs = attr2;
+  cfg.numAttrs = 1;
+  EMB_CUDA_CHECK(cudaLaunchKernelEx(&cfg, gk2::gemm2_kernel<true>, tA, tB, p));
+  count_launch();
+  return C;
 }
 
 at::Tensor rs_reduce(at::Tensor stage, int64_t tp, int64_t rows, int64_t n) {

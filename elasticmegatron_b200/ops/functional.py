@@ -165,7 +165,9 @@ class LinearFn(torch.autograd.Function):
         ctx.mode, ctx.group = mode, group
         assert x.dim() == 2, "activations are [tokens, features]"
         x2 = x
-        if mode == "col_sp":
+        if mode == "col_sp" and tp_fused.ag_eligible(x2, w, True, group):
+            y, _ = tp_fused.all_gather_gemm(x2, w, True, group)
+        elif mode == "col_sp":
             xf = _all_gather_dim0(x2, group)
             y = gemm(xf, w, trans_b=True)
         elif mode == "row_sp" and tp_fused.eligible(x2, w, False, True, group):
@@ -184,6 +186,11 @@ class LinearFn(torch.autograd.Function):
         x2, w = ctx.saved_tensors
         mode, group = ctx.mode, ctx.group
         dy2 = dy.reshape(-1, dy.shape[-1]).contiguous()
+        if mode == "row_sp" and tp_fused.ag_eligible(dy2, w, False, group):
+            # fused all-gather of dy with the dgrad GEMM; the gathered dy feeds the wgrad right after
+            dx, dyf = tp_fused.all_gather_gemm(dy2, w, False, group)
+            dw = _accumulate_wgrad(w, dyf, x2)
+            return dx, dw, None, None
         if mode == "row_sp":
             dy2 = _all_gather_dim0(dy2, group)
         xf = _all_gather_dim0(x2, group) if mode == "col_sp" else x2

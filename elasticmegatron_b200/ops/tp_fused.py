@@ -94,3 +94,39 @@ def gemm_reduce_scatter(a: torch.Tensor, b: torch.Tensor, trans_a: bool, trans_b
     ext().gemm_rs(a, b, trans_a, trans_b, buf.peers, buf.idx, rows)
     dist.all_reduce(buf.flag, group=group)  # every partial tile has landed in its owner's staging
     return ext().rs_reduce(buf.view(torch.bfloat16, tp * rows * N), tp, rows, N)
+
+
+_READY: Dict[Tuple[int, int], torch.Tensor] = {}
+
+
+def ag_eligible(shard: torch.Tensor, b: torch.Tensor, trans_b: bool, group) -> bool:
+    if not (shard.is_cuda and enabled() and group is not None):
+        return False
+    tp = dist.get_world_size(group)
+    return (1 < tp <= 8 and shard.dim() == 2 and shard.shape[0] % 256 == 0 and shard.shape[1] % 8 == 0
+            and ext().gemm_tc_supported(shard, b, False, trans_b))
+
+
+def all_gather_gemm(shard: torch.Tensor, b: torch.Tensor, trans_b: bool, group):
+    """(all_gather(shard) @ op(b), gathered) over ``group``; ``gathered`` [tp * rows, K] stays valid until the
+    next fused call on this group.
+
+    The rank's own shard is placed in its symmetric buffer; one GEMM launch pulls the peers' shards over NVLink
+    while it computes (copy warps inside the GEMM, chunk readiness counters, tiles of the local shard first).
+    """
+    tp = dist.get_world_size(group)
+    R, K = shard.shape
+    M = tp * R
+    buf = _buffer(group, M * K * 2, shard.device)
+    local = buf.view(torch.bfloat16, M * K).view(M, K)
+    dist.all_reduce(buf.flag, group=group)  # peers finished with my buffer (previous fused call)
+    local[buf.idx * R:(buf.idx + 1) * R].copy_(shard)
+    dist.all_reduce(buf.flag, group=group)  # every rank's shard is in place
+    key = (id(group), shard.device.index)
+    ready = _READY.get(key)
+    if ready is None:
+        ready = torch.zeros(2 * tp, dtype=torch.int32, device=shard.device)
+        _READY[key] = ready
+    ready.zero_()
+    y = ext().gemm_ag(local, b, trans_b, buf.peers, buf.idx, R, ready)
+    return y, local

@@ -28,6 +28,39 @@ def _rs_case(rank, world):
     return bool(ok)
 
 
+def _ag_case(rank, world):
+    import torch.distributed as dist
+
+    from elasticmegatron_b200.ops import tp_fused
+    from elasticmegatron_b200.ops.native import ext
+
+    g = dist.group.WORLD
+    ok = True
+    for trans_b, (R, N, K) in ((True, (512, 768, 512)), (False, (256, 1024, 256)), (True, (2048, 6144, 4096))):
+        torch.manual_seed(rank)
+        shard = torch.randn(R, K, device="cuda").bfloat16()
+        torch.manual_seed(99)
+        b = torch.randn(*((N, K) if trans_b else (K, N)), device="cuda").bfloat16()
+        full = torch.empty(world * R, K, device="cuda", dtype=torch.bfloat16)
+        dist.all_gather_into_tensor(full, shard, group=g)
+        ref = ext().gemm_tc(full, b, False, trans_b)
+        for _ in range(2):  # twice: the symmetric buffer and ready counters are reused
+            got, gathered = tp_fused.all_gather_gemm(shard, b, trans_b, g)
+            torch.cuda.synchronize()
+            ok &= torch.equal(gathered, full)
+            ok &= torch.allclose(got.float(), ref.float(), atol=1e-2, rtol=1e-2)
+    ok &= ext().gemm_error_flag() == 0
+    return bool(ok)
+
+
+def test_fused_all_gather_gemm():
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    from dist_utils import run_distributed
+
+    assert all(run_distributed(_ag_case, 2, backend="nccl"))
+
+
 def _tp_train(rank, world, fused):
     os.environ["EMB_FUSED_TP"] = "1" if fused else "0"
     from elasticmegatron_b200.config import Args, ModelConfig, TrainConfig, set_args
