@@ -46,6 +46,9 @@ void gemm_rs(torch::Tensor a, torch::Tensor b, bool trans_a, bool trans_b, torch
 torch::Tensor rs_reduce(torch::Tensor stage, int64_t tp, int64_t rows, int64_t n);
 torch::Tensor gemm_ag(torch::Tensor local, torch::Tensor b, bool trans_b, torch::Tensor peers, int64_t my_slot,
                       int64_t rows_per_rank, torch::Tensor ready);
+void sym_barrier(torch::Tensor sig_ptrs, int64_t me, int64_t epoch, int64_t timeout_ms);
+int64_t comm_error_flag();
+void comm_clear_error();
 }  // namespace emb
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -89,6 +92,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_rs", &gemm_rs);
   m.def("rs_reduce", &rs_reduce);
   m.def("gemm_ag", &gemm_ag);
+  m.def("sym_barrier", &sym_barrier, py::arg("sig_ptrs"), py::arg("me"), py::arg("epoch"),
+        py::arg("timeout_ms") = 60000);
+  m.def("comm_error_flag", &comm_error_flag);
+  m.def("comm_clear_error", &comm_clear_error);
   m.def("gemm_tc_supported", &gemm_tc_supported, py::arg("a"), py::arg("b"), py::arg("trans_a") = false,
         py::arg("trans_b") = false, py::arg("out") = py::none(), py::arg("accumulate") = false);
 }

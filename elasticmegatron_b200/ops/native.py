@@ -66,3 +66,16 @@ def reset_launch_count() -> None:
 def so_path() -> str:
     e = ext()
     return os.path.abspath(e.__file__)
+
+
+def check_device_errors() -> None:
+    """Raise if a bounded device-side wait of this package's kernels gave up (GEMM pipeline barriers, attention
+    pipelines, symmetric-memory barriers).  Each read is a 4-byte device->host copy, so call it where the host
+    already synchronises (after reading the loss)."""
+    if _EXT is None or not torch.cuda.is_available():
+        return
+    flags = {"gemm": _EXT.gemm_error_flag(), "comm": _EXT.comm_error_flag(),
+             "attn_fwd": _EXT.attn_error_flag(), "attn_bwd": _EXT.attn_bwd_error_flag()}
+    bad = {k: hex(v) for k, v in flags.items() if v}
+    if bad:
+        raise RuntimeError(f"device-side wait timed out (kernel error flags {bad}); results of this step are invalid")

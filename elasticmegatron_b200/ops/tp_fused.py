@@ -6,9 +6,13 @@ straight into the owning TP rank's staging buffer (peer stores through CUDA-IPC 
 transfer overlaps the math of the remaining tiles; each rank then sums its TP slots with one small kernel.
 
 Staging buffers are "symmetric": one ``cudaMalloc`` arena per rank of the TP group, mapped into every peer
-once (``SymmetricBuffer``), grown on demand.  Ordering uses two stream-ordered 1-element NCCL all-reduces
-per call (no device spin-waits): before the GEMM (every rank finished reading its staging from the previous
-call) and after it (every partial tile has landed).
+once (``SymmetricBuffer``), grown on demand.  Each arena holds a signal array and two staging halves used on
+alternate calls.  Every call has ONE ordering point, a stream-ordered barrier over the signal arrays
+(``sym_barrier``: peer stores of an epoch + bounded acquire spins; no NCCL): after the GEMM for
+reduce-scatter (every partial tile has landed), before it for all-gather (every shard is in place).  The
+barrier of call i also orders every access of call i-1 against call i+1, so with two halves no
+"peers finished reading" barrier is needed: call i+1 touches the other half, and call i+2 - which reuses this
+half - starts only after barrier i+1, which no rank passes before finishing call i.
 
 Disabled with ``EMB_FUSED_TP=0`` (then the plain GEMM + NCCL path runs).
 """
@@ -23,14 +27,22 @@ import torch.distributed as dist
 from .native import ext
 
 
+_SIG_BYTES = 4096  # signal array (uint32 per rank) at the head of every arena; keeps the halves 4 KiB aligned
+_TIMEOUT_MS = int(os.environ.get("EMB_FUSED_TP_TIMEOUT_MS", "60000"))
+
+
 class SymmetricBuffer:
-    def __init__(self, group, nbytes: int, device: torch.device):
+    def __init__(self, group, half_bytes: int, device: torch.device):
         self.group = group
         ranks = dist.get_process_group_ranks(group)
         self.n = len(ranks)
         self.idx = ranks.index(dist.get_rank())
-        self.nbytes = nbytes
-        self.arena = ext().arena_alloc(nbytes, device.index)
+        half_bytes = (half_bytes + 4095) // 4096 * 4096
+        self.half = half_bytes
+        self.nbytes = _SIG_BYTES + 2 * half_bytes
+        self.arena = ext().arena_alloc(self.nbytes, device.index)
+        self.arena[:_SIG_BYTES].zero_()
+        torch.cuda.synchronize(device)  # signals are zero on every rank before any peer can map them
         h = bytes(ext().ipc_get_handle(self.arena).numpy().tobytes())
         handles = [None] * self.n
         dist.all_gather_object(handles, h, group=group)
@@ -41,11 +53,25 @@ class SymmetricBuffer:
                 ptrs.append(self.arena.data_ptr())
             else:
                 ptrs.append(int(ext().ipc_open(torch.frombuffer(bytearray(hh), dtype=torch.uint8))))
-        self.peers = torch.tensor(ptrs, dtype=torch.int64)
+        self.sig = torch.tensor(ptrs, dtype=torch.int64)
+        self.peers = [torch.tensor([p + _SIG_BYTES + h * half_bytes for p in ptrs], dtype=torch.int64)
+                      for h in (0, 1)]
         self.flag = torch.zeros(1, dtype=torch.float32, device=device)
+        self.epoch = 0
+        self.calls = 0
 
-    def view(self, dtype, numel: int) -> torch.Tensor:
-        return self.arena[: numel * torch.finfo(dtype).bits // 8].view(dtype)
+    def next_half(self) -> int:
+        h = self.calls & 1
+        self.calls += 1
+        return h
+
+    def barrier(self) -> None:
+        self.epoch += 1
+        ext().sym_barrier(self.sig, self.idx, self.epoch, _TIMEOUT_MS)
+
+    def view(self, half: int, dtype, numel: int) -> torch.Tensor:
+        off = _SIG_BYTES + half * self.half
+        return self.arena[off: off + numel * torch.finfo(dtype).bits // 8].view(dtype)
 
     def close(self):
         for i, hh in enumerate(self.handles):
@@ -59,9 +85,10 @@ _BUFS: Dict[Tuple[int, int], SymmetricBuffer] = {}
 def _buffer(group, nbytes: int, device) -> SymmetricBuffer:
     key = (id(group), device.index)
     b = _BUFS.get(key)
-    if b is None or b.nbytes < nbytes:
+    if b is None or b.half < nbytes:
         if b is not None:
-            # every rank of the group grows at the same call (same shapes), so the swap stays collective
+            # every rank of the group grows at the same call (same shapes), so the swap stays collective;
+            # nobody may still read or write the old arenas when they are unmapped and freed
             dist.all_reduce(b.flag, group=group)
             torch.cuda.synchronize(device)
             b.close()
@@ -90,10 +117,10 @@ def gemm_reduce_scatter(a: torch.Tensor, b: torch.Tensor, trans_a: bool, trans_b
     N = b.shape[0] if trans_b else b.shape[1]
     rows = M // tp
     buf = _buffer(group, tp * rows * N * 2, a.device)
-    dist.all_reduce(buf.flag, group=group)  # peers finished reading their staging from the previous call
-    ext().gemm_rs(a, b, trans_a, trans_b, buf.peers, buf.idx, rows)
-    dist.all_reduce(buf.flag, group=group)  # every partial tile has landed in its owner's staging
-    return ext().rs_reduce(buf.view(torch.bfloat16, tp * rows * N), tp, rows, N)
+    h = buf.next_half()
+    ext().gemm_rs(a, b, trans_a, trans_b, buf.peers[h], buf.idx, rows)
+    buf.barrier()  # every partial tile has landed in its owner's staging
+    return ext().rs_reduce(buf.view(h, torch.bfloat16, tp * rows * N), tp, rows, N)
 
 
 _READY: Dict[Tuple[int, int], torch.Tensor] = {}
@@ -109,7 +136,7 @@ def ag_eligible(shard: torch.Tensor, b: torch.Tensor, trans_b: bool, group) -> b
 
 def all_gather_gemm(shard: torch.Tensor, b: torch.Tensor, trans_b: bool, group):
     """(all_gather(shard) @ op(b), gathered) over ``group``; ``gathered`` [tp * rows, K] stays valid until the
-    next fused call on this group.
+    second-next fused call on this group (it lives in one staging half).
 
     The rank's own shard is placed in its symmetric buffer; one GEMM launch pulls the peers' shards over NVLink
     while it computes (copy warps inside the GEMM, chunk readiness counters, tiles of the local shard first).
@@ -118,15 +145,15 @@ def all_gather_gemm(shard: torch.Tensor, b: torch.Tensor, trans_b: bool, group):
     R, K = shard.shape
     M = tp * R
     buf = _buffer(group, M * K * 2, shard.device)
-    local = buf.view(torch.bfloat16, M * K).view(M, K)
-    dist.all_reduce(buf.flag, group=group)  # peers finished with my buffer (previous fused call)
+    h = buf.next_half()
+    local = buf.view(h, torch.bfloat16, M * K).view(M, K)
     local[buf.idx * R:(buf.idx + 1) * R].copy_(shard)
-    dist.all_reduce(buf.flag, group=group)  # every rank's shard is in place
+    buf.barrier()  # every rank's shard is in place
     key = (id(group), shard.device.index)
     ready = _READY.get(key)
     if ready is None:
         ready = torch.zeros(2 * tp, dtype=torch.int32, device=shard.device)
         _READY[key] = ready
     ready.zero_()
-    y = ext().gemm_ag(local, b, trans_b, buf.peers, buf.idx, R, ready)
+    y = ext().gemm_ag(local, b, trans_b, buf.peers[h], buf.idx, R, ready)
     return y, local

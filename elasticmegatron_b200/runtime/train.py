@@ -72,4 +72,9 @@ def reduce_loss(ts, loss_sums: List[torch.Tensor]) -> float:
     g = ps.group("world")
     if g is not None and dist.get_world_size(g) > 1:
         dist.all_reduce(t, group=g)
-    return float(t.item()) / (tc.global_batch_size * cfg.seq_length)
+    loss = float(t.item()) / (tc.global_batch_size * cfg.seq_length)
+    if t.is_cuda:
+        from ..ops.native import check_device_errors
+
+        check_device_errors()
+    return loss

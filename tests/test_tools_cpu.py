@@ -1,0 +1,36 @@
+"""Command-line tools on CPU: checkpoint convert (+ compare) round trip and the loss-curve reader."""
+import os
+
+
+def test_convert_round_trip_matches(tmp_path):
+    from test_elastic_cpu import _setup
+
+    from elasticmegatron_b200.parallel.strategy import ParallelStrategy
+    from elasticmegatron_b200.runtime.checkpoint import save_checkpoint
+    from elasticmegatron_b200.runtime.training_state import TrainingState
+    from elasticmegatron_b200.tools.convert_ckpt import main
+
+    _setup()
+    ts = TrainingState(ParallelStrategy(world_size=1, tensor_model_parallel_size=1, pipeline_model_parallel_size=1))
+    ts.init_weights(0)
+    a, b, c = (str(tmp_path / x) for x in "abc")
+    save_checkpoint(ts, a, iteration=3)
+    assert main([a, b, "--world-size", "2", "--tp", "2"]) == 0
+    assert sorted(os.listdir(os.path.join(b, "iter_0000003"))) == ["mp_rank_00", "mp_rank_01"]
+    # TP2 -> TP1 again, compared with the original: identical tensors
+    assert main([b, c, "--world-size", "1", "--compare", a]) == 0
+
+
+def test_loss_curve_reads_three_formats(tmp_path):
+    from elasticmegatron_b200.tools.loss_curve import read_log
+
+    p1 = tmp_path / "megatron.log"
+    p1.write_text(" iteration        1/     100 | lm loss: 1.050000E+01 | elapsed time per iteration (ms): 812.5\n"
+                  " iteration        2/     100 | lm loss: 1.040000E+01 | elapsed time per iteration (ms): 800.0\n")
+    p2 = tmp_path / "json.log"
+    p2.write_text('{"event": "iteration", "iteration": 1, "loss": 10.5, "ms": 10}\nnoise\n')
+    p3 = tmp_path / "plain.txt"
+    p3.write_text("10.5\n10.4\n")
+    assert read_log(str(p1)) == {1: (10.5, 812.5), 2: (10.4, 800.0)}
+    assert read_log(str(p2)) == {1: (10.5, 10.0)}
+    assert {k: v[0] for k, v in read_log(str(p3)).items()} == {1: 10.5, 2: 10.4}

@@ -25,6 +25,7 @@ def _rs_case(rank, world):
         got = tp_fused.gemm_reduce_scatter(a, b, False, trans_b, g)
         torch.cuda.synchronize()
         ok &= torch.allclose(got.float(), ref.float(), atol=0.05 * (K ** 0.5), rtol=2e-2)
+    ok &= ext().comm_error_flag() == 0
     return bool(ok)
 
 
@@ -49,7 +50,7 @@ def _ag_case(rank, world):
             torch.cuda.synchronize()
             ok &= torch.equal(gathered, full)
             ok &= torch.allclose(got.float(), ref.float(), atol=1e-2, rtol=1e-2)
-    ok &= ext().gemm_error_flag() == 0
+    ok &= ext().gemm_error_flag() == 0 and ext().comm_error_flag() == 0
     return bool(ok)
 
 
@@ -97,3 +98,24 @@ def test_tp2_training_fused_matches_nccl_path():
     a = run_distributed(_tp_train, 2, True, backend="nccl")[0]
     b = run_distributed(_tp_train, 2, False, backend="nccl")[0]
     torch.testing.assert_close(torch.tensor(a), torch.tensor(b), atol=2e-2, rtol=2e-3)
+
+
+def test_sym_barrier_bounded_wait():
+    """One GPU: a barrier whose 'peer' slot nobody writes gives up after its limit and reports the peer."""
+    from elasticmegatron_b200.ops.native import ext
+
+    own = torch.zeros(1024, dtype=torch.int32, device="cuda")
+    fake_peer = torch.zeros(1024, dtype=torch.int32, device="cuda")
+    sig = torch.tensor([own.data_ptr(), fake_peer.data_ptr()], dtype=torch.int64)
+    ext().comm_clear_error()
+    own[1] = 3  # the peer already reached epoch 3: epochs 1..3 pass at once
+    for e in (1, 2, 3):
+        ext().sym_barrier(sig, 0, e, 1000)
+    torch.cuda.synchronize()
+    assert ext().comm_error_flag() == 0
+    assert int(fake_peer[0]) == 3  # our arrivals were stored into the peer's slot 0
+    ext().sym_barrier(sig, 0, 4, 100)  # nobody stores epoch 4 into our slot 1
+    torch.cuda.synchronize()
+    assert ext().comm_error_flag() == 0x5001
+    ext().comm_clear_error()
+    assert ext().comm_error_flag() == 0
