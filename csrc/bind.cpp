@@ -45,7 +45,18 @@ void gemm_rs(torch::Tensor a, torch::Tensor b, bool trans_a, bool trans_b, torch
              int64_t rows_per_rank);
 torch::Tensor rs_reduce(torch::Tensor stage, int64_t tp, int64_t rows, int64_t n);
 torch::Tensor gemm_ag(torch::Tensor local, torch::Tensor b, bool trans_b, torch::Tensor peers, int64_t my_slot,
-                      int64_t rows_per_rank, torch::Tensor ready);
+                      int64_t rows_per_rank, torch::Tensor claim, torch::Tensor shard, torch::Tensor flags,
+                      int64_t epoch, int64_t units_max);
+torch::Tensor gemm_grouped(torch::Tensor a, torch::Tensor w, bool trans_b, torch::Tensor tile_group);
+void gemm_grouped_wgrad(torch::Tensor dy, torch::Tensor x, torch::Tensor seg, torch::Tensor out, bool accumulate);
+std::vector<torch::Tensor> moe_router_fwd(torch::Tensor logits, int64_t k);
+torch::Tensor moe_router_bwd(torch::Tensor logits, torch::Tensor top_idx, torch::Tensor probs, torch::Tensor dprobs,
+                             torch::Tensor g_aux);
+std::vector<torch::Tensor> moe_layout(torch::Tensor gid, torch::Tensor counts, int64_t rows_cap);
+torch::Tensor moe_scatter(torch::Tensor src, int64_t k_div, torch::Tensor pos, c10::optional<torch::Tensor> w,
+                          torch::Tensor seg, torch::Tensor counts, int64_t rows_cap);
+torch::Tensor moe_gather(torch::Tensor src, torch::Tensor pos, c10::optional<torch::Tensor> w, int64_t n_out, int64_t k);
+torch::Tensor moe_row_dot(torch::Tensor a, int64_t k, torch::Tensor b, torch::Tensor pos);
 void sym_barrier(torch::Tensor sig_ptrs, int64_t me, int64_t epoch, int64_t timeout_ms);
 int64_t comm_error_flag();
 void comm_clear_error();
@@ -95,6 +106,15 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("sym_barrier", &sym_barrier, py::arg("sig_ptrs"), py::arg("me"), py::arg("epoch"),
         py::arg("timeout_ms") = 60000);
   m.def("comm_error_flag", &comm_error_flag);
+  m.def("gemm_grouped", &gemm_grouped);
+  m.def("gemm_grouped_wgrad", &gemm_grouped_wgrad);
+  m.def("moe_router_fwd", &moe_router_fwd);
+  m.def("moe_router_bwd", &moe_router_bwd);
+  m.def("moe_layout", &moe_layout);
+  m.def("moe_scatter", &moe_scatter, py::arg("src"), py::arg("k_div"), py::arg("pos"), py::arg("w"), py::arg("seg"),
+        py::arg("counts"), py::arg("rows_cap"));
+  m.def("moe_gather", &moe_gather, py::arg("src"), py::arg("pos"), py::arg("w"), py::arg("n_out"), py::arg("k"));
+  m.def("moe_row_dot", &moe_row_dot);
   m.def("comm_clear_error", &comm_clear_error);
   m.def("gemm_tc_supported", &gemm_tc_supported, py::arg("a"), py::arg("b"), py::arg("trans_a") = false,
         py::arg("trans_b") = false, py::arg("out") = py::none(), py::arg("accumulate") = false);

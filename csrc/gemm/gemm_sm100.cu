@@ -131,6 +131,15 @@ struct Params {
   int accumulate;  // C += (fp32 only)
   int a_mn, b_mn;  // operand majorness
   int* err;
+  // grouped GEMM (1-SM kernel; MoE experts).  group_mode 1: A rows come in per-group segments padded to BM,
+  // group_info[m tile] = group of that tile (-1: skip); B holds every group's matrix stacked along its row
+  // coordinate, group g's rows start at g * group_b_stride.  group_mode 2 (weight gradient): group g reduces
+  // over rows [group_info[g], group_info[g + 1]) of A and B (multiples of BK) into C + g * group_c_stride.
+  int group_mode;
+  const int* group_info;
+  int groups;
+  int group_b_stride;
+  long long group_c_stride;
   // reduce-scatter epilogue (2-SM kernel only): when scatter != 0, output row `row` belongs to TP rank
   // owner = row / rows_per_rank and is written (bf16) into that rank's staging buffer peer_out[owner] at slot
   // `my_slot`: peer_out[owner] + (my_slot * rows_per_rank + row % rows_per_rank) * ldc + col.
@@ -138,14 +147,54 @@ struct Params {
   int rows_per_rank;
   int my_slot;
   void* peer_out[8];
-  // all-gather prologue (2-SM kernel, AG template only): A rows are gathered from TP peers into the local
-  // buffer ag_local [M, K] (K-major, chunk c = rows [c*rows_per_rank, (c+1)*rows_per_rank) from ag_src[c]);
-  // ready[c] counts finished pieces of chunk c, ready[ag_tp + c] hands out pieces.
-  const void* ag_src[8];
+  // all-gather prologue (2-SM kernel, AG template only), push mode.  A = ag_local [M, K] (K-major), chunk c =
+  // rows [c*rows_per_rank, (c+1)*rows_per_rank) coming from TP rank c.  This rank's own chunk is already in
+  // place; its copy warps store this rank's shard (ag_shard, [rows_per_rank, K] contiguous) into every peer's
+  // buffer (ag_dst[peer], same layout) in units of AG_UNIT_ROWS rows and after each unit set the peer's flag
+  // ag_flags[peer][my_slot * ag_units_max + unit] = ag_epoch (release, system scope).  The producer of a tile
+  // whose rows come from chunk c waits for the flags of those rows in its own array ag_flags[my_slot].
+  // ready[0] hands out units (zeroed by the host before the launch).
+  void* ag_dst[8];
+  uint32_t* ag_flags[8];
+  const void* ag_shard;
   void* ag_local;
   int* ready;
   int ag_tp;
+  int ag_units_max;
+  uint32_t ag_epoch;
 };
+
+struct TileInfo {
+  int m0, n0, kb0, kb1, b_off;
+  long long c_off;
+};
+
+// Output tile t of the persistent schedule (m fastest); false when the tile has no work (grouped modes).
+__device__ __forceinline__ bool tile_info(const Params& p, int t, int tiles_m, int tiles_n, int nk, TileInfo& ti) {
+  if (p.group_mode == 2) {
+    const int per = tiles_m * tiles_n;
+    const int g = t / per, r = t - g * per;
+    ti.m0 = (r % tiles_m) * BM;
+    ti.n0 = (r / tiles_m) * BN;
+    ti.kb0 = p.group_info[g] / BK;
+    ti.kb1 = p.group_info[g + 1] / BK;
+    ti.b_off = 0;
+    ti.c_off = (long long)g * p.group_c_stride;
+    return ti.kb1 > ti.kb0;
+  }
+  ti.m0 = (t % tiles_m) * BM;
+  ti.n0 = (t / tiles_m) * BN;
+  ti.kb0 = 0;
+  ti.kb1 = nk;
+  ti.b_off = 0;
+  ti.c_off = 0;
+  if (p.group_mode == 1) {
+    const int g = p.group_info[t % tiles_m];
+    if (g < 0) return false;
+    ti.b_off = g * p.group_b_stride;
+  }
+  return true;
+}
 
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, Params p) {
@@ -164,7 +213,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   const int lane = threadIdx.x & 31;
   const int tiles_m = (p.M + BM - 1) / BM;
   const int tiles_n = (p.N + BN - 1) / BN;
-  const int num_tiles = tiles_m * tiles_n;
+  const int num_tiles = tiles_m * tiles_n * (p.group_mode == 2 ? p.groups : 1);
   const int nk = (p.K + BK - 1) / BK;
 
   if (threadIdx.x == 0) {
@@ -197,9 +246,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       int it = 0;
       bool ok = true;
       for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
-        const int m0 = (t % tiles_m) * BM;
-        const int n0 = (t / tiles_m) * BN;
-        for (int kb = 0; kb < nk; ++kb, ++it) {
+        TileInfo ti;
+        if (!tile_info(p, t, tiles_m, tiles_n, nk, ti)) continue;
+        const int m0 = ti.m0, n0 = ti.n0;
+        for (int kb = ti.kb0; kb < ti.kb1; ++kb, ++it) {
           const int s = it % STAGES;
           const uint32_t ph = (it / STAGES) & 1;
           if (!mbar_wait(&empty[s], ph ^ 1, p.err, 1) || *abort_flag) { ok = false; *abort_flag = 1; break; }
@@ -214,10 +264,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             tma_load_2d(a_dst + 8192, &tmA, &full[s], m0 + 64, k0);
           }
           if (!p.b_mn) {
-            tma_load_2d(b_dst, &tmB, &full[s], k0, n0);
+            tma_load_2d(b_dst, &tmB, &full[s], k0, n0 + ti.b_off);
           } else {
 #pragma unroll
-            for (int j = 0; j < 4; ++j) tma_load_2d(b_dst + j * 8192, &tmB, &full[s], n0 + 64 * j, k0);
+            for (int j = 0; j < 4; ++j) tma_load_2d(b_dst + j * 8192, &tmB, &full[s], n0 + 64 * j, k0 + ti.b_off);
           }
         }
       }
@@ -231,13 +281,16 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       const uint32_t b_lbo = p.b_mn ? 8192 : 16, b_sbo = 1024, b_step = p.b_mn ? 2048 : 32;
       int it = 0, local = 0;
       bool ok = true;
-      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x, ++local) {
+      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+        TileInfo ti;
+        if (!tile_info(p, t, tiles_m, tiles_n, nk, ti)) continue;
         const int buf = local & 1;
         const uint32_t tph = (local >> 1) & 1;
+        ++local;
         if (!mbar_wait(&tempty[buf], tph ^ 1, p.err, 2) || *abort_flag) { ok = false; *abort_flag = 1; break; }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + buf * BN;
-        for (int kb = 0; kb < nk; ++kb, ++it) {
+        for (int kb = ti.kb0; kb < ti.kb1; ++kb, ++it) {
           const int s = it % STAGES;
           const uint32_t ph = (it / STAGES) & 1;
           if (!mbar_wait(&full[s], ph, p.err, 3) || *abort_flag) { ok = false; *abort_flag = 1; break; }
@@ -248,7 +301,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           for (int k = 0; k < BK / 16; ++k) {
             const uint64_t ad = smem_desc(a_addr + k * a_step, a_lbo, a_sbo);
             const uint64_t bd = smem_desc(b_addr + k * b_step, b_lbo, b_sbo);
-            mma_bf16(d_tmem, ad, bd, idesc, (kb | k) != 0);
+            mma_bf16(d_tmem, ad, bd, idesc, ((kb - ti.kb0) | k) != 0);
           }
           mma_commit(&empty[s]);  // frees the smem stage once these MMAs have read it
         }
@@ -260,13 +313,16 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     const int quarter = warp & 3;  // TMEM lane quarter this warp may access
     const int row_in_tile = quarter * 32 + lane;
     int local = 0;
-    for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++local) {
+    for (int t = blockIdx.x; t < num_tiles; t += gridDim.x) {
+      TileInfo ti;
+      if (!tile_info(p, t, tiles_m, tiles_n, nk, ti)) continue;
       const int buf = local & 1;
       const uint32_t tph = (local >> 1) & 1;
+      ++local;
       if (!mbar_wait(&tfull[buf], tph, p.err, 4) || *abort_flag) { *abort_flag = 1; break; }
       tc_fence_after();
-      const int m0 = (t % tiles_m) * BM;
-      const int n0 = (t / tiles_m) * BN;
+      const int m0 = ti.m0;
+      const int n0 = ti.n0;
       const int row = m0 + row_in_tile;
       const bool row_ok = row < p.M;
 #pragma unroll 1
@@ -279,7 +335,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         if (!row_ok || col0 >= p.N) continue;
         const int ncols = min(32, p.N - col0);
         if (p.out_fp32) {
-          float* dst = reinterpret_cast<float*>(p.C) + (size_t)row * p.ldc + col0;
+          float* dst = reinterpret_cast<float*>(p.C) + ti.c_off + (size_t)row * p.ldc + col0;
           if (ncols == 32 && ((reinterpret_cast<uintptr_t>(dst) & 15) == 0)) {
 #pragma unroll
             for (int v = 0; v < 8; ++v) {
@@ -302,7 +358,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             }
           }
         } else {
-          __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(p.C) + (size_t)row * p.ldc + col0;
+          __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(p.C) + ti.c_off + (size_t)row * p.ldc + col0;
           if (ncols == 32 && ((reinterpret_cast<uintptr_t>(dst) & 15) == 0)) {
 #pragma unroll
             for (int v = 0; v < 4; ++v) {
@@ -353,7 +409,7 @@ constexpr int STAGE_BYTES = A_HALF + B_HALF;
 constexpr int TMEM_COLS = 512;
 constexpr int NUM_THREADS = 192;
 constexpr int NUM_THREADS_AG = 256;  // + 2 copy warps for the all-gather prologue
-constexpr int AG_PIECES = 64;        // claimable pieces per gathered chunk
+constexpr int AG_UNIT_ROWS = 32;     // rows per pushed unit (one readiness flag each)
 constexpr int EPI_STRIDE = 144;  // 128-byte rows padded to 144 B: a warp's 16-byte writes hit 4-way banks
 constexpr int EPI_BYTES = 2 * 128 * EPI_STRIDE;  // double-buffered epilogue staging
 constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + EPI_BYTES + 1024 + 256;
@@ -401,16 +457,16 @@ __host__ __device__ constexpr uint32_t make_idesc2(bool a_mn, bool b_mn) {
          ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
 }
 
-// bounded acquire-wait until *ctr >= target (all-gather chunk readiness); false on timeout
-__device__ __forceinline__ bool wait_counter(const int* ctr, int target, int* err, int code) {
+// bounded acquire-wait until the flag written by a peer GPU reaches `epoch` (wrap-safe); false on timeout
+__device__ __forceinline__ bool wait_epoch(const uint32_t* flag, uint32_t epoch, int* err, int code) {
   for (uint32_t i = 0; i < gk::WAIT_LIMIT; ++i) {
-    int v;
-    asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(ctr) : "memory");
-    if (v >= target) {
-      asm volatile("fence.proxy.async.global;" ::: "memory");  // the TMA reads that follow see the copies
+    uint32_t v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(flag) : "memory");
+    if ((int32_t)(v - epoch) >= 0) {
+      asm volatile("fence.proxy.async.global;" ::: "memory");  // the TMA reads that follow see the pushed rows
       return true;
     }
-    __nanosleep(128);
+    __nanosleep(64);
   }
   atomicExch(err, code);
   return false;
@@ -485,7 +541,13 @@ __global__ void __launch_bounds__(AG ? NUM_THREADS_AG : NUM_THREADS, 1)
         const int n0 = tile_n(t) * BN + 128 * rank;
         if (AG) {
           const int c = m0 / p.rows_per_rank;
-          if (c != my_chunk && !wait_counter(&p.ready[c], AG_PIECES, p.err, 15)) { ok = false; *abort_flag = 1; break; }
+          if (c != my_chunk) {
+            const int u0 = (m0 - c * p.rows_per_rank) / AG_UNIT_ROWS;
+            const uint32_t* f = p.ag_flags[my_chunk] + c * p.ag_units_max;
+            bool got = true;
+            for (int u = u0; u < u0 + 128 / AG_UNIT_ROWS && got; ++u) got = wait_epoch(f + u, p.ag_epoch, p.err, 15);
+            if (!got) { ok = false; *abort_flag = 1; break; }
+          }
         }
         for (int kb = 0; kb < nk; ++kb, ++it) {
           const int s = it % STAGES;
@@ -542,39 +604,44 @@ __global__ void __launch_bounds__(AG ? NUM_THREADS_AG : NUM_THREADS, 1)
       }
     }
   } else if (AG && warp >= 6) {
-    // ------------------------------------------------------------------ all-gather copy warps
-    // Each peer chunk is cut into AG_PIECES pieces that any CTA's copy warps claim with an atomic counter
-    // (so the resident CTAs finish all copies even if others are not yet scheduled); a claimed piece is
-    // pulled from the peer's buffer over NVLink with 16-byte loads and counted into ready[c].
+    // ------------------------------------------------------------------ all-gather push warps
+    // Units (peer d, AG_UNIT_ROWS rows of this rank's shard) are claimed through one atomic counter by the
+    // copy warps of every CTA (so resident CTAs finish all pushes even if others are not yet scheduled).
+    // Peers are served in the order in which they consume this rank's chunk (rank me-1 first).  A unit is
+    // read from local HBM and stored into the peer's buffer over NVLink (posted writes), then the peer's flag
+    // for the unit is released at system scope.
     __shared__ int claimed;
     const int ct = threadIdx.x - 192;  // 0..63
     const size_t row_bytes = (size_t)p.K * 2;
-    const int rows_per_piece = (p.rows_per_rank + AG_PIECES - 1) / AG_PIECES;
-    for (int i = 1; i < p.ag_tp; ++i) {
-      const int c = (my_chunk + i) % p.ag_tp;
-      while (true) {
-        if (ct == 0) claimed = atomicAdd(&p.ready[p.ag_tp + c], 1);
-        asm volatile("bar.sync 2, 64;" ::: "memory");
-        const int piece = claimed;
-        asm volatile("bar.sync 2, 64;" ::: "memory");
-        if (piece >= AG_PIECES) break;
-        const int r0 = piece * rows_per_piece, r1 = min(p.rows_per_rank, r0 + rows_per_piece);
-        if (r0 < r1) {
-          const size_t off = ((size_t)c * p.rows_per_rank + r0) * row_bytes;
-          const uint4* src = reinterpret_cast<const uint4*>(reinterpret_cast<const uint8_t*>(p.ag_src[c]) + off);
-          uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(p.ag_local) + off);
-          const size_t nv = (size_t)(r1 - r0) * row_bytes / 16;
-          size_t v = ct;
-          for (; v + 64 * 3 < nv; v += 64 * 4) {
-            uint4 x0 = src[v], x1 = src[v + 64], x2 = src[v + 128], x3 = src[v + 192];
-            dst[v] = x0; dst[v + 64] = x1; dst[v + 128] = x2; dst[v + 192] = x3;
-          }
-          for (; v < nv; v += 64) dst[v] = src[v];
-        }
-        asm volatile("fence.proxy.async.global;" ::: "memory");
-        __threadfence();
-        asm volatile("bar.sync 2, 64;" ::: "memory");
-        if (ct == 0) atomicAdd(&p.ready[c], 1);
+    const int units = p.rows_per_rank / AG_UNIT_ROWS;
+    const int total = (p.ag_tp - 1) * units;
+    const size_t nv = (size_t)AG_UNIT_ROWS * row_bytes / 16;
+    while (true) {
+      if (ct == 0) claimed = atomicAdd(p.ready, 1);
+      asm volatile("bar.sync 2, 64;" ::: "memory");
+      const int u = claimed;
+      asm volatile("bar.sync 2, 64;" ::: "memory");
+      if (u >= total) break;
+      const int d = u / units, j = u % units;
+      const int dest = (my_chunk - 1 - d + 2 * p.ag_tp) % p.ag_tp;
+      const size_t src_off = (size_t)j * AG_UNIT_ROWS * row_bytes;
+      const size_t dst_off = ((size_t)my_chunk * p.rows_per_rank + (size_t)j * AG_UNIT_ROWS) * row_bytes;
+      const uint4* src = reinterpret_cast<const uint4*>(reinterpret_cast<const uint8_t*>(p.ag_shard) + src_off);
+      uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(p.ag_dst[dest]) + dst_off);
+      size_t v = ct;
+      for (; v + 64 * 7 < nv; v += 64 * 8) {
+        uint4 x[8];
+#pragma unroll
+        for (int q = 0; q < 8; ++q) x[q] = src[v + 64 * q];
+#pragma unroll
+        for (int q = 0; q < 8; ++q) dst[v + 64 * q] = x[q];
+      }
+      for (; v < nv; v += 64) dst[v] = src[v];
+      __threadfence_system();
+      asm volatile("bar.sync 2, 64;" ::: "memory");
+      if (ct == 0) {
+        uint32_t* f = p.ag_flags[dest] + my_chunk * p.ag_units_max + j;
+        asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(f), "r"(p.ag_epoch) : "memory");
       }
     }
   } else {
@@ -851,6 +918,92 @@ at::Tensor gemm_tc(at::Tensor a, at::Tensor b, bool trans_a, bool trans_b, c10::
   return C;
 }
 
+// Grouped GEMM over per-group row segments (MoE experts), 1-SM tcgen05 kernel.
+//   y [R, N] = a [R, K] @ op(w[g]) for every 128-row tile whose tile_group entry is g >= 0 (other tiles are
+//   skipped and their rows of y left unwritten).  w: [G, N, K] (trans_b) or [G, K, N] (!trans_b; K % 64 == 0 so
+//   that a k-block never reaches into the next group's rows).
+at::Tensor gemm_grouped(at::Tensor a, at::Tensor w, bool trans_b, at::Tensor tile_group) {
+  using namespace gk;
+  TORCH_CHECK(a.is_cuda() && a.scalar_type() == at::kBFloat16 && w.scalar_type() == at::kBFloat16 && a.dim() == 2 &&
+              w.dim() == 3 && a.is_contiguous() && w.is_contiguous(), "gemm_grouped: bf16 a [R, K], w [G, ., .]");
+  TORCH_CHECK(tile_group.is_cuda() && tile_group.scalar_type() == at::kInt);
+  const int64_t R = a.size(0), K = a.size(1), G = w.size(0);
+  const int64_t N = trans_b ? w.size(1) : w.size(2);
+  TORCH_CHECK((trans_b ? w.size(2) : w.size(1)) == K, "gemm_grouped: inner dimensions differ");
+  TORCH_CHECK(R % BM == 0 && tile_group.numel() >= R / BM, "gemm_grouped: rows must be whole 128-row tiles");
+  TORCH_CHECK(K % 8 == 0 && N % 8 == 0 && (trans_b || K % BK == 0), "gemm_grouped: unsupported sizes");
+  auto C = at::empty({R, N}, a.options());
+  if (R == 0 || N == 0) return C;
+  CUtensorMap tA = make_map(a.data_ptr(), R, K, K, 64, BM);
+  CUtensorMap tB = trans_b ? make_map(w.data_ptr(), G * N, K, K, 64, BN) : make_map(w.data_ptr(), G * K, N, N, 64, 64);
+  Params p{};
+  p.C = C.data_ptr();
+  p.M = (int)R;
+  p.N = (int)N;
+  p.K = (int)K;
+  p.ldc = (int)N;
+  p.a_mn = 0;
+  p.b_mn = !trans_b;
+  p.err = err_flag();
+  p.group_mode = 1;
+  p.group_info = tile_group.data_ptr<int>();
+  p.groups = (int)G;
+  p.group_b_stride = (int)(trans_b ? N : K);
+  static bool attr_set = false;
+  if (!attr_set) {
+    EMB_CUDA_CHECK(cudaFuncSetAttribute(gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
+    attr_set = true;
+  }
+  const int tiles = (int)((R / BM) * ((N + BN - 1) / BN));
+  gemm_kernel<<<std::min(tiles, num_sms()), NUM_THREADS, SMEM_BYTES, cur_stream()>>>(tA, tB, p);
+  EMB_LAUNCH_CHECK();
+  count_launch();
+  return C;
+}
+
+// Grouped weight gradient: out[g] (+)= dy[seg[g]:seg[g+1]]^T @ x[seg[g]:seg[g+1]] for g < G, with dy [R, M],
+// x [R, N] bf16, seg int32 [G + 1] (device, multiples of 64), out fp32 [G, M, N].
+void gemm_grouped_wgrad(at::Tensor dy, at::Tensor x, at::Tensor seg, at::Tensor out, bool accumulate) {
+  using namespace gk;
+  TORCH_CHECK(dy.is_cuda() && dy.scalar_type() == at::kBFloat16 && x.scalar_type() == at::kBFloat16 &&
+              dy.is_contiguous() && x.is_contiguous() && dy.size(0) == x.size(0), "gemm_grouped_wgrad: operands");
+  TORCH_CHECK(out.scalar_type() == at::kFloat && out.dim() == 3 && out.is_contiguous() && seg.scalar_type() == at::kInt);
+  const int64_t R = dy.size(0), M = dy.size(1), N = x.size(1), G = out.size(0);
+  TORCH_CHECK(out.size(1) == M && out.size(2) == N && seg.numel() == G + 1, "gemm_grouped_wgrad: shapes");
+  TORCH_CHECK(M % 8 == 0 && N % 8 == 0, "gemm_grouped_wgrad: sizes must be multiples of 8");
+  if (R == 0 || G == 0) {
+    if (!accumulate) out.zero_();
+    return;
+  }
+  if (!accumulate) out.zero_();  // groups without rows are skipped by the kernel
+  CUtensorMap tA = make_map(dy.data_ptr(), R, M, M, 64, 64);
+  CUtensorMap tB = make_map(x.data_ptr(), R, N, N, 64, 64);
+  Params p{};
+  p.C = out.data_ptr();
+  p.M = (int)M;
+  p.N = (int)N;
+  p.K = (int)R;
+  p.ldc = (int)N;
+  p.out_fp32 = 1;
+  p.accumulate = 1;
+  p.a_mn = 1;
+  p.b_mn = 1;
+  p.err = err_flag();
+  p.group_mode = 2;
+  p.group_info = seg.data_ptr<int>();
+  p.groups = (int)G;
+  p.group_c_stride = (long long)M * N;
+  static bool attr_set = false;
+  if (!attr_set) {
+    EMB_CUDA_CHECK(cudaFuncSetAttribute(gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
+    attr_set = true;
+  }
+  const int64_t tiles = G * ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
+  gemm_kernel<<<(int)std::min<int64_t>(tiles, num_sms()), NUM_THREADS, SMEM_BYTES, cur_stream()>>>(tA, tB, p);
+  EMB_LAUNCH_CHECK();
+  count_launch();
+}
+
 // out_local[i, n] = sum_s stage[s, i, n] over the TP slots (bf16 in, fp32 sum, bf16 out)
 __global__ void rs_reduce_kernel(const __nv_bfloat16* __restrict__ stage, __nv_bfloat16* __restrict__ out,
                                  int64_t slot_elems, int tp) {
@@ -923,10 +1076,12 @@ void gemm_rs(at::Tensor a, at::Tensor b, bool trans_a, bool trans_b, at::Tensor 
 
 // Fused all-gather -> GEMM: C[M, N] = A_full @ op(b) where A_full [M, K] = concat over tp ranks of their
 // [rows_per_rank, K] shards.  `local` is this rank's gather buffer (its own chunk already in place); `peers`
-// (int64 [tp]) are the peers' gather buffers (CUDA-IPC mapped) holding their own chunks at the same offsets;
-// `ready` is an int32 [2 * tp] zero-filled array (completed and claimed pieces per chunk).  The kernel pulls the missing chunks while it computes.
+// (int64 [tp]) are the peers' gather buffers (CUDA-IPC mapped, same layout) into which this kernel pushes
+// `shard`; `flags` (int64 [tp]) are the ranks' readiness-flag arrays (units_max uint32 per chunk), set to
+// `epoch` when a unit lands; `claim` is an int32 counter zeroed before the launch.
 at::Tensor gemm_ag(at::Tensor local, at::Tensor b, bool trans_b, at::Tensor peers, int64_t my_slot,
-                   int64_t rows_per_rank, at::Tensor ready) {
+                   int64_t rows_per_rank, at::Tensor claim, at::Tensor shard, at::Tensor flags, int64_t epoch,
+                   int64_t units_max) {
   using namespace gk;
   TORCH_CHECK(gemm_tc_supported(local, b, false, trans_b, c10::nullopt, false), "gemm_ag: unsupported operands");
   const int64_t M = local.size(0), K = local.size(1);
@@ -934,8 +1089,13 @@ at::Tensor gemm_ag(at::Tensor local, at::Tensor b, bool trans_b, at::Tensor peer
   const int64_t tp = peers.numel();
   TORCH_CHECK(tp >= 1 && tp <= 8 && M == tp * rows_per_rank && rows_per_rank % 256 == 0 && (K * 2) % 16 == 0,
               "gemm_ag: rows per rank must be a multiple of 256, tp <= 8");
-  TORCH_CHECK(ready.is_cuda() && ready.scalar_type() == at::kInt && ready.numel() >= 2 * tp);
+  TORCH_CHECK(flags.numel() == tp && rows_per_rank / gk2::AG_UNIT_ROWS <= units_max, "gemm_ag: flag array too small");
+  TORCH_CHECK(claim.is_cuda() && claim.scalar_type() == at::kInt && claim.numel() >= 1);
+  TORCH_CHECK(shard.is_cuda() && shard.is_contiguous() && shard.scalar_type() == at::kBFloat16 &&
+                  shard.size(0) == rows_per_rank && shard.size(1) == K,
+              "gemm_ag: shard must be a contiguous bf16 [rows_per_rank, K] tensor");
   auto pc = peers.to(at::kCPU).contiguous();
+  auto fc = flags.to(at::kCPU).contiguous();
   const bool b_mn = !trans_b;
   CUtensorMap tA = make_map(local.data_ptr(), M, K, local.stride(0), 64, 128);
   CUtensorMap tB = b_mn ? make_map(b.data_ptr(), K, N, b.stride(0), 64, 64) : make_map(b.data_ptr(), N, K, b.stride(0), 64, 128);
@@ -952,9 +1112,17 @@ at::Tensor gemm_ag(at::Tensor local, at::Tensor b, bool trans_b, at::Tensor peer
   p.rows_per_rank = (int)rows_per_rank;
   p.my_slot = (int)my_slot;
   p.ag_local = local.data_ptr();
-  p.ready = ready.data_ptr<int>();
+  p.ag_shard = shard.data_ptr();
+  p.ready = claim.data_ptr<int>();
   p.ag_tp = (int)tp;
-  for (int64_t i = 0; i < tp; ++i) p.ag_src[i] = reinterpret_cast<const void*>(pc.data_ptr<int64_t>()[i]);
+  p.ag_units_max = (int)units_max;
+  p.ag_epoch = (uint32_t)epoch;
+  for (int64_t i = 0; i < tp; ++i) {
+    p.ag_dst[i] = reinterpret_cast<void*>(pc.data_ptr<int64_t>()[i]);
+    p.ag_flags[i] = reinterpret_cast<uint32_t*>(fc.data_ptr<int64_t>()[i]);
+    TORCH_CHECK((reinterpret_cast<uintptr_t>(p.ag_dst[i]) & 15) == 0 && (reinterpret_cast<uintptr_t>(p.ag_flags[i]) & 3) == 0,
+                "gemm_ag: misaligned peer buffer");
+  }
   static bool attr = false;
   if (!attr) {
     EMB_CUDA_CHECK(cudaFuncSetAttribute(gk2::gemm2_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,

@@ -6,13 +6,20 @@ straight into the owning TP rank's staging buffer (peer stores through CUDA-IPC 
 transfer overlaps the math of the remaining tiles; each rank then sums its TP slots with one small kernel.
 
 Staging buffers are "symmetric": one ``cudaMalloc`` arena per rank of the TP group, mapped into every peer
-once (``SymmetricBuffer``), grown on demand.  Each arena holds a signal array and two staging halves used on
-alternate calls.  Every call has ONE ordering point, a stream-ordered barrier over the signal arrays
-(``sym_barrier``: peer stores of an epoch + bounded acquire spins; no NCCL): after the GEMM for
-reduce-scatter (every partial tile has landed), before it for all-gather (every shard is in place).  The
-barrier of call i also orders every access of call i-1 against call i+1, so with two halves no
-"peers finished reading" barrier is needed: call i+1 touches the other half, and call i+2 - which reuses this
-half - starts only after barrier i+1, which no rank passes before finishing call i.
+once (``SymmetricBuffer``), grown on demand.  Each arena holds signal / flag arrays and two staging halves used
+on alternate calls (call i uses half i % 2).
+
+``all_gather_gemm`` pushes: the GEMM's copy warps store this rank's shard into every peer's half over NVLink
+in 32-row units and release a per-unit flag (= the call's epoch) in the peer's flag array; a tile waits only
+for the units of its own rows.  It needs no barrier.  ``gemm_reduce_scatter`` has one stream-ordered barrier
+over the signal arrays after its GEMM (``sym_barrier``: peer stores of an epoch + bounded acquire spins; no
+NCCL): every partial tile has landed before the local reduction.
+
+Why two halves suffice without a "peers finished reading" barrier: a rank starts call i only after its call
+i-1 finished, and call i-1 finished only after every peer took part in it (the reduce-scatter barrier, or the
+peers' pushes that its all-gather GEMM waited for, which the peers issue from inside their own call-(i-1)
+kernel).  So every peer has finished call i-2 - the last user of half i % 2 - before any rank writes that
+half in call i.
 
 Disabled with ``EMB_FUSED_TP=0`` (then the plain GEMM + NCCL path runs).
 """
@@ -27,7 +34,12 @@ import torch.distributed as dist
 from .native import ext
 
 
-_SIG_BYTES = 4096  # signal array (uint32 per rank) at the head of every arena; keeps the halves 4 KiB aligned
+# Head of every arena: barrier signals (uint32 per rank) in the first 4 KiB, then the all-gather readiness flags
+# (uint32 per (source chunk, unit of 32 rows)); the staging halves follow, 4 KiB aligned.
+_SIG_BYTES = 64 << 10
+_FLAG_OFF = 4096
+_AG_UNIT_ROWS = 32
+_AG_UNITS_MAX = (_SIG_BYTES - _FLAG_OFF) // 4 // 8
 _TIMEOUT_MS = int(os.environ.get("EMB_FUSED_TP_TIMEOUT_MS", "60000"))
 
 
@@ -54,6 +66,7 @@ class SymmetricBuffer:
             else:
                 ptrs.append(int(ext().ipc_open(torch.frombuffer(bytearray(hh), dtype=torch.uint8))))
         self.sig = torch.tensor(ptrs, dtype=torch.int64)
+        self.flags = torch.tensor([p + _FLAG_OFF for p in ptrs], dtype=torch.int64)
         self.peers = [torch.tensor([p + _SIG_BYTES + h * half_bytes for p in ptrs], dtype=torch.int64)
                       for h in (0, 1)]
         self.flag = torch.zeros(1, dtype=torch.float32, device=device)
@@ -131,6 +144,7 @@ def ag_eligible(shard: torch.Tensor, b: torch.Tensor, trans_b: bool, group) -> b
         return False
     tp = dist.get_world_size(group)
     return (1 < tp <= 8 and shard.dim() == 2 and shard.shape[0] % 256 == 0 and shard.shape[1] % 8 == 0
+            and shard.shape[0] // _AG_UNIT_ROWS <= _AG_UNITS_MAX and shard.is_contiguous()
             and ext().gemm_tc_supported(shard, b, False, trans_b))
 
 
@@ -138,8 +152,9 @@ def all_gather_gemm(shard: torch.Tensor, b: torch.Tensor, trans_b: bool, group):
     """(all_gather(shard) @ op(b), gathered) over ``group``; ``gathered`` [tp * rows, K] stays valid until the
     second-next fused call on this group (it lives in one staging half).
 
-    The rank's own shard is placed in its symmetric buffer; one GEMM launch pulls the peers' shards over NVLink
-    while it computes (copy warps inside the GEMM, chunk readiness counters, tiles of the local shard first).
+    The rank's own shard is placed in its own buffer; one GEMM launch pushes it into the peers' buffers over
+    NVLink while it computes (copy warps inside the GEMM, per-unit readiness flags, tiles of the local shard
+    first).
     """
     tp = dist.get_world_size(group)
     R, K = shard.shape
@@ -148,12 +163,12 @@ def all_gather_gemm(shard: torch.Tensor, b: torch.Tensor, trans_b: bool, group):
     h = buf.next_half()
     local = buf.view(h, torch.bfloat16, M * K).view(M, K)
     local[buf.idx * R:(buf.idx + 1) * R].copy_(shard)
-    buf.barrier()  # every rank's shard is in place
     key = (id(group), shard.device.index)
-    ready = _READY.get(key)
-    if ready is None:
-        ready = torch.zeros(2 * tp, dtype=torch.int32, device=shard.device)
-        _READY[key] = ready
-    ready.zero_()
-    y = ext().gemm_ag(local, b, trans_b, buf.peers[h], buf.idx, R, ready)
+    claim = _READY.get(key)
+    if claim is None:
+        claim = torch.zeros(1, dtype=torch.int32, device=shard.device)
+        _READY[key] = claim
+    claim.zero_()
+    y = ext().gemm_ag(local, b, trans_b, buf.peers[h], buf.idx, R, claim, shard, buf.flags, buf.calls,
+                      _AG_UNITS_MAX)
     return y, local

@@ -128,7 +128,32 @@ class ParallelStrategy:
     def from_any(cls, s) -> "ParallelStrategy":
         if isinstance(s, ParallelStrategy):
             return s
+        if isinstance(s, str):
+            return cls.parse(s)
         return cls(**s)
+
+    _SPEC_KEYS = {"ws": "world_size", "tp": "tensor_model_parallel_size", "pp": "pipeline_model_parallel_size",
+                  "cp": "context_parallel_size", "ep": "expert_model_parallel_size",
+                  "etp": "expert_tensor_parallel_size", "inst": "num_distributed_optimizer_instances"}
+
+    @classmethod
+    def parse(cls, spec: str) -> "ParallelStrategy":
+        """Inverse of ``str()``: ``"ws8-tp2-pp1"``, ``"ws4-tp2-sp"``, ``"ws8-ep4"`` ... (missing sizes default
+        to 1; ``dp`` is derived and ignored if given; ``sp`` / ``nosp`` force sequence parallelism)."""
+        kw: Dict = {"tensor_model_parallel_size": 1, "pipeline_model_parallel_size": 1}
+        for tok in spec.strip().split("-"):
+            if tok in ("sp", "nosp"):
+                kw["sequence_parallel"] = tok == "sp"
+                continue
+            key = tok.rstrip("0123456789")
+            if key == "dp":
+                continue
+            if key not in cls._SPEC_KEYS or key == tok:
+                raise ValueError(f"bad strategy token {tok!r} in {spec!r}")
+            kw[cls._SPEC_KEYS[key]] = int(tok[len(key):])
+        if "world_size" not in kw:
+            raise ValueError(f"strategy {spec!r} needs a ws<N> token")
+        return cls(**kw)
 
     # ------------------------------------------------------------------ coordinates
     def coords(self, rank: Optional[int] = None) -> Dict[str, int]:
