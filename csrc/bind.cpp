@@ -52,7 +52,7 @@ void gemm_grouped_wgrad(torch::Tensor dy, torch::Tensor x, torch::Tensor seg, to
 std::vector<torch::Tensor> moe_router_fwd(torch::Tensor logits, int64_t k);
 torch::Tensor moe_router_bwd(torch::Tensor logits, torch::Tensor top_idx, torch::Tensor probs, torch::Tensor dprobs,
                              torch::Tensor g_aux);
-std::vector<torch::Tensor> moe_layout(torch::Tensor gid, torch::Tensor counts, int64_t rows_cap);
+std::vector<torch::Tensor> moe_layout(torch::Tensor gid, torch::Tensor counts, int64_t rows_cap, int64_t align);
 torch::Tensor moe_scatter(torch::Tensor src, int64_t k_div, torch::Tensor pos, c10::optional<torch::Tensor> w,
                           torch::Tensor seg, torch::Tensor counts, int64_t rows_cap);
 torch::Tensor moe_gather(torch::Tensor src, torch::Tensor pos, c10::optional<torch::Tensor> w, int64_t n_out, int64_t k);
@@ -110,7 +110,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_grouped_wgrad", &gemm_grouped_wgrad);
   m.def("moe_router_fwd", &moe_router_fwd);
   m.def("moe_router_bwd", &moe_router_bwd);
-  m.def("moe_layout", &moe_layout);
+  m.def("moe_layout", &moe_layout, py::arg("gid"), py::arg("counts"), py::arg("rows_cap"), py::arg("align") = 128);
   m.def("moe_scatter", &moe_scatter, py::arg("src"), py::arg("k_div"), py::arg("pos"), py::arg("w"), py::arg("seg"),
         py::arg("counts"), py::arg("rows_cap"));
   m.def("moe_gather", &moe_gather, py::arg("src"), py::arg("pos"), py::arg("w"), py::arg("n_out"), py::arg("k"));

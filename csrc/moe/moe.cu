@@ -141,15 +141,15 @@ __global__ void router_bwd_kernel(const float* __restrict__ logits, const int* _
   }
 }
 
-// seg[g] (g = 0..G) and tile_group[i] from the group counts; one block
-__global__ void segments_kernel(const int* __restrict__ counts, int G, int n_tiles, int* __restrict__ seg,
+// seg[g] (g = 0..G) and tile_group[i] from the group counts (segments rounded up to `align` rows); one block
+__global__ void segments_kernel(const int* __restrict__ counts, int G, int align, int n_tiles, int* __restrict__ seg,
                                 int* __restrict__ tile_group) {
   __shared__ int s_seg[1025];
   if (threadIdx.x == 0) {
     int o = 0;
     for (int g = 0; g < G; ++g) {
       s_seg[g] = o;
-      o += (counts[g] + SEG_ALIGN - 1) / SEG_ALIGN * SEG_ALIGN;
+      o += (counts[g] + align - 1) / align * align;
     }
     s_seg[G] = o;
   }
@@ -300,18 +300,22 @@ at::Tensor moe_router_bwd(at::Tensor logits, at::Tensor top_idx, at::Tensor prob
   return d;
 }
 
-// Group layout for R rows with group ids gid [R] (int32) and per-group counts [G]; rows_cap = allocated rows
-// (>= sum of padded counts).  Returns {pos [R], seg [G + 1], tile_group [rows_cap / 128]}.
-std::vector<at::Tensor> moe_layout(at::Tensor gid, at::Tensor counts, int64_t rows_cap) {
+// Group layout for R rows with group ids gid [R] (int32) and per-group counts [G]; segments are rounded up to
+// `align` rows (128 for the grouped GEMM, 1 for a dense send buffer); rows_cap = allocated rows (>= the sum of
+// rounded counts).  Returns {pos [R], seg [G + 1], tile_group [rows_cap / 128]} (tile_group empty unless
+// align == 128).
+std::vector<at::Tensor> moe_layout(at::Tensor gid, at::Tensor counts, int64_t rows_cap, int64_t align) {
   TORCH_CHECK(gid.is_cuda() && gid.scalar_type() == at::kInt && counts.scalar_type() == at::kInt);
-  TORCH_CHECK(rows_cap % SEG_ALIGN == 0);
+  TORCH_CHECK(align == 1 || align == SEG_ALIGN, "moe_layout: align must be 1 or 128");
+  TORCH_CHECK(align == 1 || rows_cap % SEG_ALIGN == 0);
   const int64_t R = gid.numel(), G = counts.numel();
   TORCH_CHECK(G >= 1 && G <= 1024);
   auto oi = gid.options();
   auto pos = at::empty({R}, oi);
   auto seg = at::empty({G + 1}, oi);
-  auto tg = at::empty({rows_cap / SEG_ALIGN}, oi);
-  segments_kernel<<<1, 256, 0, cur_stream()>>>(counts.data_ptr<int>(), (int)G, (int)(rows_cap / SEG_ALIGN),
+  const int64_t n_tiles = align == SEG_ALIGN ? rows_cap / SEG_ALIGN : 0;
+  auto tg = at::empty({n_tiles}, oi);
+  segments_kernel<<<1, 256, 0, cur_stream()>>>(counts.data_ptr<int>(), (int)G, (int)align, (int)n_tiles,
                                                seg.data_ptr<int>(), tg.data_ptr<int>());
   EMB_LAUNCH_CHECK();
   if (R > 0) {

@@ -8,6 +8,7 @@ load balancing).  Experts use ETP = 1: each EP rank holds ``E / EP`` whole exper
 """
 from __future__ import annotations
 
+import os
 from typing import List
 
 import torch
@@ -74,6 +75,112 @@ class GroupedLinearFn(torch.autograd.Function):
         return dx, dw.to(w.dtype), None
 
 
+# ------------------------------------------------------------------------------------------ native (CUDA) path
+# Router, token layout and expert MLP on the extension's kernels (csrc/moe/moe.cu, grouped tcgen05 GEMM in
+# csrc/gemm): no per-expert Python loop and, without expert parallelism, no host synchronisation.
+
+def _ext():
+    from ..ops.native import ext
+
+    return ext()
+
+
+class _RouterFn(torch.autograd.Function):
+    """(probs [T, k], score_sum [E], top_idx, counts) from fp32 logits; differentiable in probs and score_sum."""
+
+    @staticmethod
+    def forward(ctx, logits, k: int):
+        top, probs, counts, part = _ext().moe_router_fwd(logits.contiguous(), k)
+        ctx.save_for_backward(logits, top, probs)
+        ctx.mark_non_differentiable(top, counts)
+        return probs, part.sum(0), top, counts
+
+    @staticmethod
+    def backward(ctx, dprobs, dscore, _top, _counts):
+        logits, top, probs = ctx.saved_tensors
+        dprobs = torch.zeros_like(probs) if dprobs is None else dprobs.float().contiguous()
+        dscore = torch.zeros(logits.shape[1], device=logits.device) if dscore is None else dscore.float().contiguous()
+        return _ext().moe_router_bwd(logits, top, probs, dprobs, dscore), None
+
+
+class _ScatterFn(torch.autograd.Function):
+    """Rows of ``src`` (row r // k_div for assignment r) into the grouped layout ``lay``."""
+
+    @staticmethod
+    def forward(ctx, src, lay, k_div: int):
+        ctx.lay, ctx.k_div, ctx.n = lay, k_div, src.shape[0]
+        return _ext().moe_scatter(src.contiguous(), k_div, lay["pos"], None, lay["seg"], lay["counts"], lay["cap"])
+
+    @staticmethod
+    def backward(ctx, d):
+        lay = ctx.lay
+        return _ext().moe_gather(d.contiguous(), lay["pos"], None, ctx.n, ctx.k_div), None, None
+
+
+class _GatherFn(torch.autograd.Function):
+    """out[i] = sum_j w[i, j] * y[pos[i * k + j]] (w optional); the inverse movement of ``_ScatterFn``."""
+
+    @staticmethod
+    def forward(ctx, y, w, lay, n_out: int, k: int):
+        ctx.lay, ctx.n_out, ctx.k = lay, n_out, k
+        wf = w.reshape(-1).float().contiguous() if w is not None else None
+        ctx.has_w = w is not None
+        # y is only needed for the gradient of the weights
+        ctx.save_for_backward(y if ctx.has_w else torch.empty(0, device=y.device),
+                              wf if ctx.has_w else torch.empty(0, device=y.device))
+        return _ext().moe_gather(y.contiguous(), lay["pos"], wf, n_out, k)
+
+    @staticmethod
+    def backward(ctx, dout):
+        y, wf = ctx.saved_tensors
+        lay = ctx.lay
+        dout = dout.contiguous()
+        dy = _ext().moe_scatter(dout, ctx.k, lay["pos"], wf if ctx.has_w else None, lay["seg"], lay["counts"],
+                                lay["cap"])
+        dw = _ext().moe_row_dot(dout, ctx.k, y.contiguous(), lay["pos"]).view(ctx.n_out, ctx.k) if ctx.has_w else None
+        return dy, dw, None, None, None
+
+
+class _GroupedLinearNativeFn(torch.autograd.Function):
+    """y = x @ W[g]^T per 128-row tile of group g (one grouped tcgen05 launch); W [G, out, in]."""
+
+    @staticmethod
+    def forward(ctx, x, w, lay):
+        ctx.lay = lay
+        ctx.save_for_backward(x, w)
+        return _ext().gemm_grouped(x.contiguous(), w.contiguous(), True, lay["tiles"])
+
+    @staticmethod
+    def backward(ctx, dy):
+        x, w = ctx.saved_tensors
+        lay = ctx.lay
+        dy = dy.contiguous()
+        dx = _ext().gemm_grouped(dy, w.contiguous(), False, lay["tiles"])
+        mg = getattr(w, "main_grad", None)
+        if mg is not None:
+            _ext().gemm_grouped_wgrad(dy, x, lay["seg"], mg.view(w.shape), True)
+            hook = getattr(w, "_grad_ready", None)
+            if hook is not None:
+                hook()
+            return dx, None, None
+        dw = torch.empty(w.shape, dtype=torch.float32, device=w.device)
+        _ext().gemm_grouped_wgrad(dy, x, lay["seg"], dw, False)
+        return dx, dw.to(w.dtype), None
+
+
+def _layout(gid: torch.Tensor, counts: torch.Tensor, n_rows: int, align: int) -> dict:
+    G = counts.numel()
+    cap = n_rows + (G * (align - 1) if align > 1 else 0)
+    cap = (cap + 127) // 128 * 128 if align > 1 else max(cap, 1)
+    pos, seg, tiles = _ext().moe_layout(gid.to(torch.int32).contiguous(), counts.to(torch.int32).contiguous(), cap,
+                                        align)
+    return {"pos": pos, "seg": seg, "tiles": tiles, "counts": counts.to(torch.int32).contiguous(), "cap": cap}
+
+
+def native_moe_enabled() -> bool:
+    return os.environ.get("EMB_NATIVE_MOE", "1") != "0"
+
+
 class MoELayer:
     def __init__(self, cfg, pstate, w_router, w_fc1, w_fc2):
         self.cfg, self.ps = cfg, pstate
@@ -87,6 +194,63 @@ class MoELayer:
         self.sp_group = pstate.group("tp") if (s.tensor_model_parallel_size > 1 and s.sequence_parallel) else None
 
     def __call__(self, h: torch.Tensor):
+        f2 = self.w1.shape[1]
+        if (h.is_cuda and native_moe_enabled() and self.E <= 256 and self.k <= 8 and h.shape[1] % 64 == 0
+                and f2 % 64 == 0):
+            return self._native_forward(h)
+        return self._torch_forward(h)
+
+    def _aux(self, score_sum: torch.Tensor, counts: torch.Tensor, T: int) -> torch.Tensor:
+        E, k = self.E, self.k
+        T_full, counts_full = T, counts
+        if self.sp_group is not None:
+            counts_full = counts.clone()
+            dist.all_reduce(counts_full, group=self.sp_group)
+            T_full = T * dist.get_world_size(self.sp_group)
+        return (E * self.cfg.moe_aux_loss_coeff / (T_full * T_full * k)) * (score_sum * counts_full.to(score_sum.dtype)).sum()
+
+    def _native_forward(self, h: torch.Tensor):
+        """Router kernel -> expert-grouped layout -> grouped fc1 / SwiGLU / fc2 -> weighted combine.
+
+        Without expert parallelism nothing synchronises with the host: the layout is sized for the worst case
+        (every segment padded to 128 rows) and the grouped GEMM skips tiles past the last segment.  With EP the
+        token counts are exchanged and the rows move with NCCL all-to-all (host-known split sizes)."""
+        T = h.shape[0]
+        E, k, E_loc, ep = self.E, self.k, self.E_loc, self.ep
+        logits = F_.linear(h, self.wr).float()
+        probs, score_sum, top, counts = _RouterFn.apply(logits, k)
+        aux = self._aux(score_sum, counts.to(torch.int64), T)
+        gid = top.reshape(-1)
+        if ep == 1:
+            lay = _layout(gid, counts, T * k, 128)
+            xe = _ScatterFn.apply(h, lay, k)
+            ye = self._experts(xe, lay)
+            return _GatherFn.apply(ye, probs, lay, T, k), aux
+        # expert parallelism: dense send buffer grouped by global expert (= by destination rank, local expert)
+        send_lay = _layout(gid, counts, T * k, 1)
+        x_send = _ScatterFn.apply(h, send_lay, k)
+        cnt = counts.view(ep, E_loc)
+        recv = torch.empty_like(cnt)
+        dist.all_to_all_single(recv, cnt.contiguous(), group=self.ep_group)
+        send_splits = cnt.sum(1).tolist()
+        recv_splits = recv.sum(1).tolist()
+        x_recv = all_to_all(x_send, send_splits, recv_splits, self.ep_group)
+        n_recv = int(sum(recv_splits))
+        gid_recv = torch.repeat_interleave(torch.arange(E_loc, device=h.device, dtype=torch.int32).repeat(ep),
+                                           recv.reshape(-1).to(torch.int64), output_size=n_recv)
+        lay = _layout(gid_recv, recv.sum(0), n_recv, 128)
+        xe = _ScatterFn.apply(x_recv, lay, 1)
+        ye = self._experts(xe, lay)
+        y_recv = _GatherFn.apply(ye, None, lay, n_recv, 1)
+        y_send = all_to_all(y_recv, recv_splits, send_splits, self.ep_group)
+        return _GatherFn.apply(y_send, probs, send_lay, T, k), aux
+
+    def _experts(self, xe: torch.Tensor, lay: dict) -> torch.Tensor:
+        a = _GroupedLinearNativeFn.apply(xe, self.w1, lay)
+        a = F_.swiglu(a)
+        return _GroupedLinearNativeFn.apply(a, self.w2, lay)
+
+    def _torch_forward(self, h: torch.Tensor):
         T = h.shape[0]
         E, k, E_loc, ep = self.E, self.k, self.E_loc, self.ep
         logits = F_.linear(h, self.wr).float()
