@@ -34,7 +34,7 @@ from ..parallel.process_groups import (ProcessGroupPool, create_all_groups, glob
 from ..parallel.strategy import ParallelStrategy, union_ranks
 from ..planner.plan import KIND_OPT, KIND_PARAM, build_plan
 from ..utils.logging import log_json
-from ..utils.timers import DeviceTimer, HostTimer, max_over_ranks
+from ..utils.timers import DeviceTimer, HostTimer, max_over_ranks, nvtx_range
 from .data import DataloaderState
 from .training_state import TrainingState
 
@@ -52,9 +52,14 @@ class ElasticMegatronManager:
         TrainingState.setup_model_and_optimizer_func = setup_model_and_optimizer_func
         DataloaderState.register(train_valid_test_datasets_provider)
 
-    def __init__(self, parallel_strategy_list: List[Union[Dict, ParallelStrategy]], model=None, optimizer=None,
-                 opt_param_scheduler=None, training_state: Optional[TrainingState] = None,
-                 engine: Optional[str] = None, warmup: bool = True):
+    def __init__(self, parallel_strategy_list: List[Union[Dict, ParallelStrategy, str]], model=None, optimizer=None,
+                 opt_param_scheduler=None, send_fn: Optional[Callable] = None, recv_fn: Optional[Callable] = None,
+                 broadcast_fn: Optional[Callable] = None, use_p2p_to_collective: Optional[bool] = None,
+                 training_state: Optional[TrainingState] = None, engine: Optional[str] = None, warmup: bool = True):
+        """``send_fn`` / ``recv_fn`` / ``broadcast_fn`` / ``use_p2p_to_collective`` keep the reference's
+        injectable communicator (elastic_manager.py:41-58): when any is given, switches run the reference's
+        transfer schedule through those functions; otherwise ``engine`` picks the transfer engine
+        ("native" peer-memory kernel on GPUs by default, "torch" batched P2P, "reference")."""
         self._rank = dist.get_rank() if dist.is_initialized() else 0
         self.strategies = [ParallelStrategy.from_any(s) for s in parallel_strategy_list]
         assert len(set(self.strategies)) == len(self.strategies), "duplicate strategies"
@@ -68,8 +73,15 @@ class ElasticMegatronManager:
             assert training_state.strategy == self.strategies[0], "strategy 0 must match the live model"
             self._states[self.current] = training_state
         self._plans: Dict[tuple, object] = {}
-        self.engine_name = engine or ("native" if torch.cuda.is_available() else "torch")
-        self.engine = self._make_engine(self.engine_name)
+        custom = any(x is not None for x in (send_fn, recv_fn, broadcast_fn, use_p2p_to_collective))
+        if custom:
+            from ..transfer.reference_engine import ReferenceAlgorithmEngine
+
+            self.engine_name = "reference"
+            self.engine = ReferenceAlgorithmEngine(send_fn, recv_fn, broadcast_fn, bool(use_p2p_to_collective))
+        else:
+            self.engine_name = engine or ("native" if torch.cuda.is_available() else "torch")
+            self.engine = self._make_engine(self.engine_name)
         self.last_switch: Dict = {}
         set_world_group(ProcessGroupPool.get(self.current.ranks))
 
@@ -166,22 +178,26 @@ class ElasticMegatronManager:
             return None
         ugroup = ProcessGroupPool.get(union)
         same_layout = src_s.layout_key() == dst_s.layout_key()
-        with HostTimer(sync=False) as t_build:
+        with HostTimer(sync=False) as t_build, nvtx_range("reshard/build"):
             dst = self._get_or_build(dst_s, is_meta_device)
         if src is not None and src.model_released:
             src.rebuild()
-        plan = self.plan(src_s, dst_s)
-        kinds_moved = None
+        with nvtx_range("reshard/plan"):
+            plan = self.plan(src_s, dst_s)
         if is_meta_device:
             # meta mode: no data moves; only pre-build state / connections (reference "fake transfer")
             ms, nbytes = 0.0, 0
             if hasattr(self.engine, "warmup"):
-                self.engine.warmup(plan, self._rank, src, dst, ugroup)
+                with nvtx_range("reshard/warmup"):
+                    self.engine.warmup(plan, self._rank, src, dst, ugroup)
         else:
-            ms, nbytes = self._transfer(plan, src, dst, ugroup, same_layout)
-        self._transfer_lr(src, dst, union)
+            with nvtx_range("reshard/transfer"):
+                ms, nbytes = self._transfer(plan, src, dst, ugroup, same_layout)
+        with nvtx_range("reshard/lr"):
+            self._transfer_lr(src, dst, union)
         if src is not None and src is not dst:
-            src.release()
+            with nvtx_range("reshard/release"):
+                src.release()
         self.current = dst_s
         set_world_group(ProcessGroupPool.get(dst_s.ranks))
         if dst is not None and not is_meta_device:

@@ -39,8 +39,15 @@ class ReferenceAlgorithmEngine:
     name = "reference_algorithm"
     moves_params = False
 
-    def __init__(self):
+    def __init__(self, send_fn=None, recv_fn=None, broadcast_fn=None, use_p2p_to_collective: bool = False):
+        """``send_fn(t, dst)`` / ``recv_fn(t, src)`` / ``broadcast_fn(t, src, group)`` replace the NCCL calls
+        (the reference's injectable communicator, elastic_manager.py:41-51); with ``use_p2p_to_collective`` a
+        point-to-point exchange is a broadcast on the 2-rank group {src, dst} (p2p_to_collective.py:41-96)."""
         self.bytes_sent = 0
+        self.send_fn = send_fn or (lambda t, dst: dist.send(t, dst))
+        self.recv_fn = recv_fn or (lambda t, src: dist.recv(t, src))
+        self.broadcast_fn = broadcast_fn or (lambda t, src, group: dist.broadcast(t, src=src, group=group))
+        self.use_p2p_to_collective = use_p2p_to_collective
 
     def reset_counters(self):
         self.bytes_sent = 0
@@ -113,13 +120,26 @@ class ReferenceAlgorithmEngine:
         return out
 
     def _p2p(self, t: torch.Tensor, src: int, dst: int, rank: int):
-        if src == dst:
+        if src == dst or rank not in (src, dst):
+            return
+        if self.use_p2p_to_collective:
+            from ..parallel.process_groups import ProcessGroupPool
+
+            buf = t.contiguous()
+            self.broadcast_fn(buf, src, ProcessGroupPool.get(sorted((src, dst))))
+            if rank == dst and buf.data_ptr() != t.data_ptr():
+                t.copy_(buf)
+            if rank == src:
+                self.bytes_sent += t.numel() * t.element_size()
             return
         if rank == src:
-            dist.send(t.contiguous(), dst)
+            self.send_fn(t.contiguous(), dst)
             self.bytes_sent += t.numel() * t.element_size()
-        elif rank == dst:
-            dist.recv(t, src)
+        else:
+            buf = t if t.is_contiguous() else torch.empty_like(t, memory_format=torch.contiguous_format)
+            self.recv_fn(buf, src)
+            if buf is not t:
+                t.copy_(buf)
 
     def _gather_piece(self, view, vp, r, aligned, rank, opt, full, dev):
         for f0, f1, o in self._owned_ranges(view, vp, r):

@@ -74,3 +74,22 @@ def max_over_ranks(values: Sequence[float], group=None) -> list:
     t = torch.tensor(list(values), dtype=torch.float64 if dev.type == "cpu" else torch.float32, device=dev)
     dist.all_reduce(t, op=dist.ReduceOp.MAX, group=group)
     return t.tolist()
+
+
+class nvtx_range:
+    """NVTX range around a phase (plan, build, transfer, lr, release) so Nsight-style timelines show the
+    switch structure; a no-op without CUDA."""
+
+    def __init__(self, name: str):
+        self.name = name
+        self.on = torch.cuda.is_available()
+
+    def __enter__(self):
+        if self.on:
+            torch.cuda.nvtx.range_push(self.name)
+        return self
+
+    def __exit__(self, *exc):
+        if self.on:
+            torch.cuda.nvtx.range_pop()
+        return False

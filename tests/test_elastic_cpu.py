@@ -119,12 +119,32 @@ def _engine_losses(rank, world, engine):
     create_all_groups(S)
     ts = TrainingState(S[0])
     ts.init_weights(0)
-    mgr = ElasticMegatronManager(STRATS, training_state=ts, engine=engine)
+    calls = {"send": 0, "bcast": 0}
+    if engine == "injected":
+        import torch.distributed as dist
+
+        def send_fn(t, dst):
+            calls["send"] += 1
+            dist.send(t, dst)
+
+        mgr = ElasticMegatronManager(STRATS, training_state=ts, send_fn=send_fn)
+    elif engine == "p2p_as_collective":
+        import torch.distributed as dist
+
+        def bcast(t, src, group):
+            calls["bcast"] += 1
+            dist.broadcast(t, src=src, group=group)
+
+        mgr = ElasticMegatronManager(STRATS, training_state=ts, broadcast_fn=bcast, use_p2p_to_collective=True)
+    else:
+        mgr = ElasticMegatronManager(STRATS, training_state=ts, engine=engine)
     train_step(ts, mgr.build_iterators(0)[0])
     losses = []
     for i in (1, 2, 0):
         ts = mgr.reshard(STRATS[i])
         losses.append(train_step(ts, mgr.build_iterators(8)[0])["loss"])
+    if engine in ("injected", "p2p_as_collective"):
+        assert mgr.engine_name == "reference" and calls["send" if engine == "injected" else "bcast"] > 0
     return losses
 
 
@@ -132,6 +152,14 @@ def test_reference_algorithm_engine_matches_direct():
     a = run_distributed(_engine_losses, 2, "torch")
     b = run_distributed(_engine_losses, 2, "reference")
     np.testing.assert_allclose(a[0], b[0], rtol=1e-6)
+
+
+def test_injected_communicator_and_p2p_as_collective():
+    a = run_distributed(_engine_losses, 2, "torch")
+    b = run_distributed(_engine_losses, 2, "injected")
+    c = run_distributed(_engine_losses, 2, "p2p_as_collective")
+    np.testing.assert_allclose(a[0], b[0], rtol=1e-6)
+    np.testing.assert_allclose(a[0], c[0], rtol=1e-6)
 
 
 def _ckpt(rank, world, root):
