@@ -666,29 +666,24 @@ __global__ void __launch_bounds__(AG ? NUM_THREADS_AG : NUM_THREADS, 1)
         const int col0 = n0 + c * 32;
         if (!row_ok || col0 >= p.N) continue;
         const int ncols = min(32, p.N - col0);
+        void* gdst;
         if (p.scatter) {
-          // fused reduce-scatter: this partial row chunk goes straight to its owner's staging slot (peer
-          // memory over NVLink; plain stores are posted, so the math of the next tiles overlaps the transfer)
+          // fused reduce-scatter: this partial row chunk goes straight to its owner's staging slot (peer memory
+          // over NVLink), handed to the bulk-copy engine below so the epilogue warps move on to the next chunk
           const int owner = row / p.rows_per_rank;
           __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(p.peer_out[owner]) +
                                ((size_t)p.my_slot * p.rows_per_rank + (row - owner * p.rows_per_rank)) * p.ldc + col0;
-          if (ncols == 32) {
-#pragma unroll
-            for (int v = 0; v < 4; ++v) {
-              float f[8];
-#pragma unroll
-              for (int j = 0; j < 8; ++j) f[j] = __uint_as_float(r[8 * v + j]);
-              reinterpret_cast<uint4*>(dst)[v] = pack8(f);
-            }
-          } else {
+          if (ncols != 32 || (reinterpret_cast<uintptr_t>(dst) & 15) != 0) {
 #pragma unroll
             for (int j = 0; j < 32; ++j)
               if (j < ncols) dst[j] = __float2bfloat16_rn(__uint_as_float(r[j]));
+            continue;
           }
-          continue;
+          gdst = dst;
+        } else {
+          gdst = p.out_fp32 ? (void*)(reinterpret_cast<float*>(p.C) + (size_t)row * p.ldc + col0)
+                            : (void*)(reinterpret_cast<__nv_bfloat16*>(p.C) + (size_t)row * p.ldc + col0);
         }
-        void* gdst = p.out_fp32 ? (void*)(reinterpret_cast<float*>(p.C) + (size_t)row * p.ldc + col0)
-                                : (void*)(reinterpret_cast<__nv_bfloat16*>(p.C) + (size_t)row * p.ldc + col0);
         if (ncols == 32 && ((reinterpret_cast<uintptr_t>(gdst) & 15) == 0)) {
           // stage the row chunk in shared memory and hand it to the bulk-copy engine: a plain store, or an
           // fp32 add-reduction into C (the wgrad accumulate), without the read-modify-write round trip

@@ -1,7 +1,8 @@
 """K1 reshard copy kernel: byte-exact against the planner's CPU oracle.
 
-``test_k1_emulated_ranks`` runs on one GPU: all ranks' arenas of both layouts live on the device and each
-destination rank's task table is executed as in pull mode.  ``test_native_engine_two_gpus`` runs the real
+``test_k1_emulated_ranks`` runs on one GPU: all ranks' arenas of both layouts live on the device and every
+rank's task table is executed, once as in pull mode (tables of the destination ranks) and once as in push mode
+(tables of the source ranks).  ``test_native_engine_two_gpus`` runs the real
 engine (CUDA IPC + NCCL barriers) in two processes and needs two GPUs.
 """
 import itertools
@@ -49,8 +50,8 @@ def test_k1_emulated_ranks():
     S = [ParallelStrategy(world_size=8, tensor_model_parallel_size=tp, pipeline_model_parallel_size=pp)
          for tp, pp in ((1, 1), (2, 2), (4, 1), (1, 4))]
     S.append(ParallelStrategy(world_size=4, tensor_model_parallel_size=2, pipeline_model_parallel_size=1))
-    eng = NativeP2PEngine(task_bytes=4096)  # small tasks: exercise the splitter
-    for a, b in itertools.permutations(S, 2):
+    for mode, (a, b) in itertools.product(("pull", "push"), itertools.permutations(S, 2)):
+        eng = NativeP2PEngine(mode=mode, task_bytes=4096)  # small tasks: exercise the splitter
         plan = build_plan(a, b, cfg)
         sP, sO = _state(cfg, a, g, og)
         eP, eO = _state(cfg, b, g, og)
@@ -59,7 +60,7 @@ def test_k1_emulated_ranks():
         addrs = {r: (sP[r].data_ptr() if r in sP else 0, sO[r].data_ptr() if r in sO else 0,
                      tP[r].data_ptr() if r in tP else 0, tO[r].data_ptr() if r in tO else 0)
                  for r in range(max(a.world_size, b.world_size))}
-        for r in range(b.world_size):
+        for r in range(b.world_size if mode == "pull" else a.world_size):
             t = eng._tasks(plan, r, addrs, 2)
             if len(t):
                 buf = torch.from_numpy(t.view(np.uint8).copy()).cuda()
@@ -68,10 +69,10 @@ def test_k1_emulated_ranks():
         for r in range(b.world_size):
             # padding is never written by the plan: compare only what the oracle defines (non-nan after copy)
             mP, mO = ~torch.isnan(tP[r].float()), ~torch.isnan(tO[r])
-            assert torch.equal(tP[r][mP], eP[r][mP]) and torch.equal(tO[r][mO], eO[r][mO]), (a, b, r)
+            assert torch.equal(tP[r][mP], eP[r][mP]) and torch.equal(tO[r][mO], eO[r][mO]), (mode, a, b, r)
             # every non-padding element was written
             nzP = eP[r] != 0
-            assert bool(mP[nzP].all()), (a, b, r)
+            assert bool(mP[nzP].all()), (mode, a, b, r)
 
 
 def _two_gpu(rank, world):
