@@ -96,10 +96,13 @@ class NativeP2PEngine:
             return np.zeros(0, dtype=TASK_DTYPE)
         is_opt = d["kind"] == KIND_OPT
         el = np.where(is_opt, 4, el_param).astype(np.uint64)
-        src_base = np.array([addrs[int(r)][1] if o else addrs[int(r)][0] for r, o in zip(d["src_rank"], is_opt)],
-                            dtype=np.uint64)
-        dst_base = np.array([addrs[int(r)][3] if o else addrs[int(r)][2] for r, o in zip(d["dst_rank"], is_opt)],
-                            dtype=np.uint64)
+        nr = max(max(addrs) + 1, int(d["src_rank"].max()) + 1, int(d["dst_rank"].max()) + 1)
+        tab = np.zeros((nr, 4), dtype=np.uint64)  # per rank: src param, src opt, dst param, dst opt
+        for r, a4 in addrs.items():
+            tab[r] = a4
+        sr, dr = d["src_rank"].astype(np.int64), d["dst_rank"].astype(np.int64)
+        src_base = np.where(is_opt, tab[sr, 1], tab[sr, 0])
+        dst_base = np.where(is_opt, tab[dr, 3], tab[dr, 2])
         t = np.zeros(len(d), dtype=_TMP_DTYPE)
         t["src"] = src_base + d["src_off"].astype(np.uint64) * el
         t["dst"] = dst_base + d["dst_off"].astype(np.uint64) * el
@@ -123,31 +126,37 @@ class NativeP2PEngine:
         return t[np.argsort(-size.astype(np.int64), kind="stable")]
 
     def _split(self, t: np.ndarray) -> np.ndarray:
-        out = []
-        cap = self.task_bytes
-        for r in t:
-            rows, rb, planes = int(r["rows"]), int(r["row_bytes"]), int(r["planes"])
-            total = rows * rb * planes
-            if total <= cap:
-                out.append(r)
-                continue
-            if rows > 1:
-                per = max(1, cap // max(1, rb * planes))
-                for r0 in range(0, rows, per):
-                    x = r.copy()
-                    x["rows"] = min(per, rows - r0)
-                    x["src"] = r["src"] + np.uint64(r0) * r["src_stride"]
-                    x["dst"] = r["dst"] + np.uint64(r0) * r["dst_stride"]
-                    out.append(x)
-            else:
-                per = max(16, (cap // planes) // 16 * 16)
-                for c0 in range(0, rb, per):
-                    x = r.copy()
-                    x["row_bytes"] = min(per, rb - c0)
-                    x["src"] = r["src"] + np.uint64(c0)
-                    x["dst"] = r["dst"] + np.uint64(c0)
-                    out.append(x)
-        return np.array(out, dtype=_TMP_DTYPE) if out else np.zeros(0, dtype=_TMP_DTYPE)
+        """Cut tasks larger than ``task_bytes``: multi-row tasks by rows, single-row tasks by 16-byte-aligned
+        column ranges (vectorised; the planner emits tens of thousands of descriptors for a 13B model)."""
+        if len(t) == 0:
+            return t
+        cap = np.uint64(self.task_bytes)
+        rows, rb, planes = t["rows"], t["row_bytes"], t["planes"]
+        total = rows * rb * planes
+        big = total > cap
+        by_rows = big & (rows > 1)
+        by_cols = big & (rows <= 1)
+        one = np.uint64(1)
+        per_rows = np.maximum(one, cap // np.maximum(one, rb * planes))
+        per_cols = np.maximum(np.uint64(16), (cap // np.maximum(one, planes)) // np.uint64(16) * np.uint64(16))
+        n = np.ones(len(t), dtype=np.uint64)
+        n[by_rows] = (rows[by_rows] + per_rows[by_rows] - one) // per_rows[by_rows]
+        n[by_cols] = (rb[by_cols] + per_cols[by_cols] - one) // per_cols[by_cols]
+        idx = np.repeat(np.arange(len(t)), n.astype(np.int64))
+        out = t[idx].copy()
+        first = np.concatenate([[0], np.cumsum(n.astype(np.int64))[:-1]])
+        j = (np.arange(len(idx)) - np.repeat(first, n.astype(np.int64))).astype(np.uint64)
+        br, bc = by_rows[idx], by_cols[idx]
+        pr, pc = per_rows[idx], per_cols[idx]
+        r0 = j * pr
+        out["rows"][br] = np.minimum(pr[br], t["rows"][idx][br] - r0[br])
+        out["src"][br] += r0[br] * out["src_stride"][br]
+        out["dst"][br] += r0[br] * out["dst_stride"][br]
+        c0 = j * pc
+        out["row_bytes"][bc] = np.minimum(pc[bc], t["row_bytes"][idx][bc] - c0[bc])
+        out["src"][bc] += c0[bc]
+        out["dst"][bc] += c0[bc]
+        return out
 
     # ------------------------------------------------------------------ execution
     def _barrier(self, group, device):
