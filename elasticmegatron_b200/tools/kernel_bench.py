@@ -2,6 +2,12 @@
 
     python -m elasticmegatron_b200.tools.kernel_bench gemm --m 16384 --n 4096 --k 4096 --layout fprop
     python -m elasticmegatron_b200.tools.kernel_bench all
+    python -m elasticmegatron_b200.tools.kernel_bench fused --m 4096 --n 4096 --k 4096
+
+``fused`` runs the fused tensor-parallel kernels on ONE GPU with a 2-rank group emulated in local memory
+(the "peer" staging / gather buffers are ordinary local allocations and the all-gather readiness flags of the
+other rank's chunk are set before the launch), so the kernels can be profiled with single-GPU tools; the
+NVLink side of the real kernels is measured by ``tp_bench``.
 
 Each case runs a warm-up, then ``--iters`` timed launches bracketed by ``cuda.synchronize``, on inputs larger
 than L2 where the op is memory-bound.  Fractions are reported against the measured peaks in
@@ -122,9 +128,91 @@ def bench_attention(iters, s=4096, b=1, G=32, hpg=1):
              "peak": src}]
 
 
+def bench_fused(m, n, k, iters):
+    """gemm_rs / gemm_ag on one GPU, tp = 2 emulated with local buffers (see the module docstring)."""
+    from elasticmegatron_b200.ops.native import ext
+
+    pk, _, src = peaks()
+    dev = "cuda"
+    tp, R = 2, m // 2
+    a = torch.randn(m, k, device=dev).bfloat16()
+    w = torch.randn(n, k, device=dev).bfloat16()
+    st = [torch.empty(tp * R * n, device=dev, dtype=torch.bfloat16) for _ in range(tp)]
+    peers = torch.tensor([t.data_ptr() for t in st], dtype=torch.int64)
+    rs = lambda: ext().gemm_rs(a, w, False, True, peers, 0, R)
+    ms_rs = timeit(rs, iters)
+    ms_red = timeit(lambda: ext().rs_reduce(st[0], tp, R, n), iters)
+    # all-gather: own chunk 0 in place, chunk 1 pre-filled, its unit flags already at the epoch
+    units_max = 1920
+    local = torch.randn(m, k, device=dev).bfloat16()
+    shard = local[:R].contiguous()
+    other = torch.empty(m, k, device=dev, dtype=torch.bfloat16)
+    flags = [torch.zeros(tp * units_max, dtype=torch.int32, device=dev) for _ in range(tp)]
+    epoch = 7
+    flags[0][units_max:units_max + R // 32] = epoch
+    fptr = torch.tensor([f.data_ptr() for f in flags], dtype=torch.int64)
+    bptr = torch.tensor([local.data_ptr(), other.data_ptr()], dtype=torch.int64)
+    claim = torch.zeros(1, dtype=torch.int32, device=dev)
+
+    def ag():
+        claim.zero_()
+        return ext().gemm_ag(local, w, True, bptr, 0, R, claim, shard, fptr, epoch, units_max)
+
+    y = ag()
+    torch.cuda.synchronize()
+    ok = torch.equal(other[:R], shard) and ext().gemm_error_flag() == 0
+    ref = (local.float() @ w.float().t())
+    err = float((y.float() - ref).abs().max() / ref.abs().max())
+    ms_ag = timeit(ag, iters)
+    ms_g = timeit(lambda: ext().gemm_tc(a, w, False, True), iters)
+    fl = 2.0 * m * n * k
+    return [{"op": "gemm_rs(emulated tp2)", "m": m, "n": n, "k": k, "ms": ms_rs, "tflops": fl / ms_rs / 1e9,
+             "frac": fl / ms_rs / 1e9 / pk, "rs_reduce_ms": ms_red, "gemm_ms": ms_g, "peak": src},
+            {"op": "gemm_ag(emulated tp2)", "m": m, "n": n, "k": k, "ms": ms_ag, "tflops": fl / ms_ag / 1e9,
+             "frac": fl / ms_ag / 1e9 / pk, "gemm_ms": ms_g, "push_ok": bool(ok), "max_rel_err": err, "peak": src}]
+
+
+def bench_reshard_local(iters, model="llama2-7b", layers=2):
+    """K1 on ONE GPU: every rank's arenas of an 8-rank TP1*DP8 -> TP4*DP2 switch live on this device and all
+    destination ranks' task tables run in one launch (a local strided copy: bytes read + written over the
+    measured HBM copy bandwidth is its roofline)."""
+    import numpy as np
+
+    from elasticmegatron_b200.config import Args, TrainConfig, preset, set_args
+    from elasticmegatron_b200.ops.native import ext
+    from elasticmegatron_b200.parallel.strategy import ParallelStrategy
+    from elasticmegatron_b200.planner.layout import rank_layout
+    from elasticmegatron_b200.planner.plan import build_plan
+    from elasticmegatron_b200.transfer.native_engine import NativeP2PEngine
+
+    _, hbm, src = peaks()
+    cfg = preset(model, num_layers=layers, max_tensor_parallel_size=8)
+    set_args(Args(model=cfg, train=TrainConfig(overlap_grad_reduce=True)))
+    a = ParallelStrategy(world_size=8, tensor_model_parallel_size=1, pipeline_model_parallel_size=1)
+    b = ParallelStrategy(world_size=8, tensor_model_parallel_size=4, pipeline_model_parallel_size=1)
+    plan = build_plan(a, b, cfg, overlap_grad_reduce=True, ddp_bucket_size=None)
+    bufs, addrs = [], {}
+    for r in range(8):
+        la, lb = rank_layout(cfg, a, r, True, None), rank_layout(cfg, b, r, True, None)
+        t = [torch.randn(la.param_numel, device="cuda").bfloat16(), torch.rand(3, la.opt_numel, device="cuda"),
+             torch.empty(lb.param_numel, device="cuda", dtype=torch.bfloat16),
+             torch.empty(3, lb.opt_numel, device="cuda")]
+        bufs.append(t)
+        addrs[r] = tuple(x.data_ptr() for x in t)
+    eng = NativeP2PEngine(mode="pull")
+    tasks = np.concatenate([eng._tasks(plan, r, addrs, 2) for r in range(8)])
+    tasks = tasks[np.argsort(-(tasks["rows"].astype(np.int64) * tasks["row_bytes"] * tasks["planes"]), kind="stable")]
+    nbytes = int((tasks["rows"].astype(np.int64) * tasks["row_bytes"] * tasks["planes"]).sum())
+    buf = torch.from_numpy(tasks.view(np.uint8).copy()).cuda()
+    ms = timeit(lambda: ext().reshard_copy(buf, len(tasks), 0), iters)
+    gbs = 2 * nbytes / ms / 1e6
+    return [{"op": "reshard_copy(local, 8 ranks emulated)", "model": model, "layers": layers, "tasks": len(tasks),
+             "bytes": nbytes, "ms": ms, "rw_gbs": gbs, "frac": gbs / hbm, "peak": src}]
+
+
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("what", choices=["gemm", "elementwise", "attention", "all"])
+    ap.add_argument("what", choices=["gemm", "elementwise", "attention", "fused", "reshard", "all"])
     ap.add_argument("--m", type=int, default=16384)
     ap.add_argument("--n", type=int, default=4096)
     ap.add_argument("--k", type=int, default=4096)
@@ -136,6 +224,10 @@ def main():
     res = []
     if a.what == "gemm":
         res.append(bench_gemm(a.m, a.n, a.k, a.layout, a.iters, a.baseline, a.variant))
+    if a.what == "fused":
+        res += bench_fused(a.m, a.n, a.k, a.iters)
+    if a.what == "reshard":
+        res += bench_reshard_local(a.iters)
     if a.what == "all":
         # the Llama-2 7B training GEMMs at 4096 tokens per micro-batch
         for (m, n, k) in ((4096, 12288, 4096), (4096, 4096, 4096), (4096, 22016, 4096), (4096, 4096, 11008),
