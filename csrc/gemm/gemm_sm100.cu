@@ -131,6 +131,7 @@ struct Params {
   int accumulate;  // C += (fp32 only)
   int a_mn, b_mn;  // operand majorness
   int* err;
+  int split_tail;  // 2-SM kernel: run the last partial wave as 256 x 128 half tiles when they fit in one wave
   // grouped GEMM (1-SM kernel; MoE experts).  group_mode 1: A rows come in per-group segments padded to BM,
   // group_info[m tile] = group of that tile (-1: skip); B holds every group's matrix stacked along its row
   // coordinate, group g's rows start at g * group_b_stride.  group_mode 2 (weight gradient): group g reduces
@@ -452,9 +453,9 @@ __device__ __forceinline__ void commit_pair(uint64_t* bar) {
       "h"((uint16_t)0x3)
       : "memory");
 }
-__host__ __device__ constexpr uint32_t make_idesc2(bool a_mn, bool b_mn) {
+__host__ __device__ constexpr uint32_t make_idesc2(bool a_mn, bool b_mn, int n = BN) {
   return (1u << 4) | (1u << 7) | (1u << 10) | ((a_mn ? 1u : 0u) << 15) | ((b_mn ? 1u : 0u) << 16) |
-         ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+         ((uint32_t)(n >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
 }
 
 // bounded acquire-wait until the flag written by a peer GPU reaches `epoch` (wrap-safe); false on timeout
@@ -507,6 +508,16 @@ __global__ void __launch_bounds__(AG ? NUM_THREADS_AG : NUM_THREADS, 1)
     return (t / tiles_n + my_chunk * mt_per_chunk) % tiles_m;
   };
   auto tile_n = [&](int t) -> int { return AG ? t % tiles_n : t / tiles_m; };
+  // Tail split (not with the all-gather prologue): when the tiles of the last, partial wave could run as twice
+  // as many 256 x 128 halves in one wave, they do - the last wave then takes half as long (4096 x 4096
+  // outputs: 256 tiles on 74 clusters = 3 full waves + 34 tiles -> 3.5 wave-times instead of 4).  Work unit u
+  // maps to tile unit_tile(u); unit_half(u) is -1 for a whole tile, else which 128-column half.
+  const int tail = AG ? 0 : num_tiles % num_clusters;
+  const bool split_tail = !AG && p.split_tail && tail > 0 && 2 * tail <= num_clusters;
+  const int full_tiles = split_tail ? num_tiles - tail : num_tiles;
+  const int num_units = split_tail ? full_tiles + 2 * tail : num_tiles;
+  auto unit_tile = [&](int u) -> int { return u < full_tiles ? u : full_tiles + ((u - full_tiles) >> 1); };
+  auto unit_half = [&](int u) -> int { return u < full_tiles ? -1 : ((u - full_tiles) & 1); };
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -536,9 +547,12 @@ __global__ void __launch_bounds__(AG ? NUM_THREADS_AG : NUM_THREADS, 1)
     if (lane == 0) {
       int it = 0;
       bool ok = true;
-      for (int t = cluster_id; t < num_tiles && ok; t += num_clusters) {
+      for (int u = cluster_id; u < num_units && ok; u += num_clusters) {
+        const int t = unit_tile(u), hf = unit_half(u);
         const int m0 = tile_m(t) * BM + 128 * rank;
-        const int n0 = tile_n(t) * BN + 128 * rank;
+        // each CTA supplies half of the tile's B columns: 128 of a whole tile, 64 of a half tile (the loaded box
+        // stays 128 rows; the MMA reads its first 64)
+        const int n0 = tile_n(t) * BN + (hf > 0 ? 128 : 0) + (hf >= 0 ? 64 : 128) * rank;
         if (AG) {
           const int c = m0 / p.rows_per_rank;
           if (c != my_chunk) {
@@ -575,12 +589,14 @@ __global__ void __launch_bounds__(AG ? NUM_THREADS_AG : NUM_THREADS, 1)
     }
   } else if (warp == 1) {
     if (leader && lane == 0) {
-      const uint32_t idesc = make_idesc2(p.a_mn, p.b_mn);
+      const uint32_t idesc_full = make_idesc2(p.a_mn, p.b_mn);
+      const uint32_t idesc_half = make_idesc2(p.a_mn, p.b_mn, BN / 2);
       const uint32_t a_lbo = p.a_mn ? 8192 : 16, a_step = p.a_mn ? 2048 : 32;
       const uint32_t b_lbo = p.b_mn ? 8192 : 16, b_step = p.b_mn ? 2048 : 32;
       int it = 0, local = 0;
       bool ok = true;
-      for (int t = cluster_id; t < num_tiles && ok; t += num_clusters, ++local) {
+      for (int u = cluster_id; u < num_units && ok; u += num_clusters, ++local) {
+        const uint32_t idesc = unit_half(u) >= 0 ? idesc_half : idesc_full;
         const int buf = local & 1;
         const uint32_t tph = (local >> 1) & 1;
         if (!mbar_wait(&tempty[buf], tph ^ 1, p.err, 12) || *abort_flag) { ok = false; *abort_flag = 1; break; }
@@ -649,16 +665,18 @@ __global__ void __launch_bounds__(AG ? NUM_THREADS_AG : NUM_THREADS, 1)
     const int row_in_half = quarter * 32 + lane;
     int local = 0;
     uint32_t epi_n = 0;  // bulk groups issued by this thread (selects the staging buffer)
-    for (int t = cluster_id; t < num_tiles; t += num_clusters, ++local) {
+    for (int u = cluster_id; u < num_units; u += num_clusters, ++local) {
+      const int t = unit_tile(u), hf = unit_half(u);
       const int buf = local & 1;
       const uint32_t tph = (local >> 1) & 1;
       if (!mbar_wait(&tfull[buf], tph, p.err, 14) || *abort_flag) { *abort_flag = 1; break; }
       tc_fence_after();
       const int row = tile_m(t) * BM + 128 * rank + row_in_half;
-      const int n0 = tile_n(t) * BN;
+      const int n0 = tile_n(t) * BN + (hf > 0 ? BN / 2 : 0);
+      const int n_chunks = (hf >= 0 ? BN / 2 : BN) / 32;
       const bool row_ok = row < p.M;
 #pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
+      for (int c = 0; c < n_chunks; ++c) {
         uint32_t r[32];
         const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + buf * BN + c * 32;
         TMEM_LD_32(taddr, r);
@@ -873,7 +891,9 @@ at::Tensor gemm_tc(at::Tensor a, at::Tensor b, bool trans_a, bool trans_b, c10::
   p.b_mn = b_mn;
   p.err = err_flag();
   const int64_t tiles2 = ((M + 255) / 256) * ((N + 255) / 256);
-  const bool pair = variant == 2 || (variant <= 0 && tiles2 >= num_sms() / 2);
+  // variant: 0 auto, 1 one-SM tiles, 2 two-SM tiles, 3 two-SM tiles without the tail split (for comparison)
+  const bool pair = variant == 2 || variant == 3 || (variant <= 0 && tiles2 >= num_sms() / 2);
+  p.split_tail = variant == 3 ? 0 : 1;
   if (pair) {
     // 2-SM clusters: each CTA loads a 128-row half of the A tile and of the B tile
     CUtensorMap tA2 = a_mn ? tA : make_map(a.data_ptr(), M, K, a.stride(0), 64, 128);
@@ -1042,6 +1062,7 @@ void gemm_rs(at::Tensor a, at::Tensor b, bool trans_a, bool trans_b, at::Tensor 
   p.b_mn = b_mn;
   p.err = err_flag();
   p.scatter = 1;
+  p.split_tail = 1;
   p.rows_per_rank = (int)rows_per_rank;
   p.my_slot = (int)my_slot;
   for (int64_t i = 0; i < tp; ++i) p.peer_out[i] = reinterpret_cast<void*>(pc.data_ptr<int64_t>()[i]);

@@ -219,8 +219,12 @@ def main():
     ap.add_argument("--layout", default="fprop")
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--baseline", action="store_true")
-    ap.add_argument("--variant", type=int, default=0, help="0 both, 1 one-SM tiles, 2 two-SM cluster tiles")
+    ap.add_argument("--variant", type=int, default=0,
+                    help="0 = variants 1 and 2; 1 one-SM tiles, 2 two-SM cluster tiles, 3 two-SM tiles without the "
+                         "tail split")
+    ap.add_argument("--variants", default=None, help="comma list of GEMM variants for 'all' (overrides --variant)")
     a = ap.parse_args()
+    variants = [int(v) for v in a.variants.split(",")] if a.variants else ((1, 2) if a.variant == 0 else (a.variant,))
     res = []
     if a.what == "gemm":
         res.append(bench_gemm(a.m, a.n, a.k, a.layout, a.iters, a.baseline, a.variant))
@@ -234,8 +238,8 @@ def main():
                           (4096, 32000, 4096)):
             for lay in ("fprop", "dgrad", "wgrad"):
                 mm, nn, kk = (m, n, k) if lay == "fprop" else ((m, k, n) if lay == "dgrad" else (n, k, m))
-                for var in ((1, 2) if a.variant == 0 else (a.variant,)):
-                    res.append(bench_gemm(mm, nn, kk, lay, a.iters, a.baseline and var == 2, var))
+                for j, var in enumerate(variants):
+                    res.append(bench_gemm(mm, nn, kk, lay, a.iters, a.baseline and j == len(variants) - 1, var))
     if a.what in ("elementwise", "all"):
         res += bench_elementwise(a.iters)
     if a.what in ("attention", "all"):

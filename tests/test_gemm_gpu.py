@@ -12,10 +12,11 @@ def _ext():
 
 
 SHAPES = [(128, 256, 64), (256, 512, 128), (296, 520, 200), (1024, 4096, 4096), (4096, 1024, 512), (8, 8, 8),
+          (4096, 4096, 256), (2560, 2304, 128), (2600, 2200, 136),
           (136, 264, 72)]
 
 
-@pytest.mark.parametrize("variant", [1, 2])
+@pytest.mark.parametrize("variant", [1, 2, 3])
 @pytest.mark.parametrize("M,N,K", SHAPES)
 @pytest.mark.parametrize("layout", ["fprop", "dgrad", "wgrad"])
 def test_gemm_layouts(M, N, K, layout, variant):
