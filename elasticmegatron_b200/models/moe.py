@@ -214,7 +214,9 @@ class MoELayer:
 
         Without expert parallelism nothing synchronises with the host: the layout is sized for the worst case
         (every segment padded to 128 rows) and the grouped GEMM skips tiles past the last segment.  With EP the
-        token counts are exchanged and the rows move with NCCL all-to-all (host-known split sizes)."""
+        token counts are exchanged (one small all-gather read on the host) and the rows move over NVLink peer
+        memory straight into the owners' grouped layout (``ops/ep_comm.py``; ``EMB_EP_PEER=0``: NCCL
+        all-to-all)."""
         T = h.shape[0]
         E, k, E_loc, ep = self.E, self.k, self.E_loc, self.ep
         logits = F_.linear(h, self.wr).float()
@@ -226,7 +228,15 @@ class MoELayer:
             xe = _ScatterFn.apply(h, lay, k)
             ye = self._experts(xe, lay)
             return _GatherFn.apply(ye, probs, lay, T, k), aux
-        # expert parallelism: dense send buffer grouped by global expert (= by destination rank, local expert)
+        from ..ops import ep_comm
+
+        if ep_comm.enabled():
+            # expert parallelism over NVLink peer memory: rows go straight into the owners' grouped layout
+            plan = ep_comm.EPPlan(self.ep_group, top, counts, E_loc, h.shape[1])
+            xe = ep_comm.dispatch(h, plan)
+            ye = self._experts(xe, plan.layout())
+            return ep_comm.combine(ye, probs, plan), aux
+        # NCCL path: dense send buffer grouped by global expert (= by destination rank, local expert)
         send_lay = _layout(gid, counts, T * k, 1)
         x_send = _ScatterFn.apply(h, send_lay, k)
         cnt = counts.view(ep, E_loc)

@@ -84,7 +84,7 @@ class SymmetricBuffer:
 
     def view(self, half: int, dtype, numel: int) -> torch.Tensor:
         off = _SIG_BYTES + half * self.half
-        return self.arena[off: off + numel * torch.finfo(dtype).bits // 8].view(dtype)
+        return self.arena[off: off + numel * torch.empty((), dtype=dtype).element_size()].view(dtype)
 
     def close(self):
         for i, hh in enumerate(self.handles):
@@ -95,8 +95,9 @@ class SymmetricBuffer:
 _BUFS: Dict[Tuple[int, int], SymmetricBuffer] = {}
 
 
-def _buffer(group, nbytes: int, device) -> SymmetricBuffer:
-    key = (id(group), device.index)
+def _buffer(group, nbytes: int, device, tag: str = "", min_bytes: int = 64 << 20) -> SymmetricBuffer:
+    """The group's symmetric buffer named ``tag``, grown (collectively) to at least ``nbytes`` per half."""
+    key = (id(group), device.index, tag)
     b = _BUFS.get(key)
     if b is None or b.half < nbytes:
         if b is not None:
@@ -105,7 +106,7 @@ def _buffer(group, nbytes: int, device) -> SymmetricBuffer:
             dist.all_reduce(b.flag, group=group)
             torch.cuda.synchronize(device)
             b.close()
-        b = SymmetricBuffer(group, max(nbytes, 64 << 20), device)
+        b = SymmetricBuffer(group, max(nbytes, min_bytes), device)
         _BUFS[key] = b
     return b
 

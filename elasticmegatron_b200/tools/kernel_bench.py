@@ -57,11 +57,19 @@ def bench_gemm(m, n, k, layout, iters, baseline, variant=0):
         a, b = torch.randn(m, k, device=dev).bfloat16(), torch.randn(k, n, device=dev).bfloat16()
         fn = lambda: ext().gemm_tc(a, b, False, False, variant=variant)
         ref = lambda: torch.matmul(a, b)
+    elif layout == "tn":  # A MN-major, B K-major: a [K, M], b [N, K]
+        a, b = torch.randn(k, m, device=dev).bfloat16(), torch.randn(n, k, device=dev).bfloat16()
+        fn = lambda: ext().gemm_tc(a, b, True, True, variant=variant)
+        ref = lambda: torch.matmul(a.t(), b.t())
+    elif layout == "wgrad_bf16":  # both MN-major, bf16 output (no accumulate)
+        a, b = torch.randn(k, m, device=dev).bfloat16(), torch.randn(k, n, device=dev).bfloat16()
+        fn = lambda: ext().gemm_tc(a, b, True, False, variant=variant)
+        ref = lambda: torch.matmul(a.t(), b)
     else:
         a, b = torch.randn(k, m, device=dev).bfloat16(), torch.randn(k, n, device=dev).bfloat16()
         c = torch.zeros(m, n, device=dev)
         fn = lambda: ext().gemm_tc(a, b, True, False, c, True, variant=variant)
-        ref = lambda: c.addmm_(a.t().float(), b.float()) if False else torch.matmul(a.t(), b)
+        ref = lambda: torch.matmul(a.t(), b)
     ms = timeit(fn, iters)
     tf = 2 * m * n * k / ms / 1e9
     pk, _, src = peaks()
@@ -216,7 +224,7 @@ def main():
     ap.add_argument("--m", type=int, default=16384)
     ap.add_argument("--n", type=int, default=4096)
     ap.add_argument("--k", type=int, default=4096)
-    ap.add_argument("--layout", default="fprop")
+    ap.add_argument("--layout", default="fprop", help="fprop | dgrad | wgrad | tn | wgrad_bf16, or a comma list")
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--baseline", action="store_true")
     ap.add_argument("--variant", type=int, default=0,
@@ -227,7 +235,8 @@ def main():
     variants = [int(v) for v in a.variants.split(",")] if a.variants else ((1, 2) if a.variant == 0 else (a.variant,))
     res = []
     if a.what == "gemm":
-        res.append(bench_gemm(a.m, a.n, a.k, a.layout, a.iters, a.baseline, a.variant))
+        for lay in a.layout.split(","):
+            res.append(bench_gemm(a.m, a.n, a.k, lay, a.iters, a.baseline, a.variant))
     if a.what == "fused":
         res += bench_fused(a.m, a.n, a.k, a.iters)
     if a.what == "reshard":

@@ -143,8 +143,9 @@ def test_native_moe_training_matches_torch_path():
         assert abs(ga - gb) <= 2e-2 * abs(gb), (a, b)
 
 
-def _moe_ep_train(rank, world, native):
+def _moe_ep_train(rank, world, native, peer=True):
     os.environ["EMB_NATIVE_MOE"] = "1" if native else "0"
+    os.environ["EMB_EP_PEER"] = "1" if peer else "0"
     from elasticmegatron_b200.config import Args, ModelConfig, TrainConfig, set_args
     from elasticmegatron_b200.parallel.process_groups import create_all_groups
     from elasticmegatron_b200.parallel.strategy import ParallelStrategy
@@ -162,7 +163,11 @@ def _moe_ep_train(rank, world, native):
     ts = TrainingState(s)
     ts.init_weights(0)
     it = DataloaderState.build_iterators(ts, 0)[0]
-    return [train_step(ts, it)["loss"] for _ in range(3)]
+    out = [train_step(ts, it)["loss"] for _ in range(3)]
+    from elasticmegatron_b200.ops.native import ext
+
+    assert ext().comm_error_flag() == 0
+    return out
 
 
 def test_native_moe_expert_parallel_matches_torch_path():
@@ -173,3 +178,14 @@ def test_native_moe_expert_parallel_matches_torch_path():
     a = run_distributed(_moe_ep_train, 2, True, backend="nccl")[0]
     b = run_distributed(_moe_ep_train, 2, False, backend="nccl")[0]
     torch.testing.assert_close(torch.tensor(a), torch.tensor(b), atol=1e-2, rtol=2e-3)
+
+
+def test_ep_peer_dispatch_matches_nccl_all_to_all():
+    """The peer-memory dispatch / combine gives the same training losses as NCCL all-to-all (same kernels around)."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    from dist_utils import run_distributed
+
+    a = run_distributed(_moe_ep_train, 2, True, True, backend="nccl")[0]
+    b = run_distributed(_moe_ep_train, 2, True, False, backend="nccl")[0]
+    torch.testing.assert_close(torch.tensor(a), torch.tensor(b), atol=1e-3, rtol=1e-4)
