@@ -57,8 +57,9 @@ torch::Tensor moe_scatter(torch::Tensor src, int64_t k_div, torch::Tensor pos, c
                           torch::Tensor seg, torch::Tensor counts, int64_t rows_cap);
 torch::Tensor moe_gather(torch::Tensor src, torch::Tensor pos, c10::optional<torch::Tensor> w, int64_t n_out, int64_t k);
 torch::Tensor moe_row_dot(torch::Tensor a, int64_t k, torch::Tensor b, torch::Tensor pos);
-void ep_push(torch::Tensor src, int64_t k_div, torch::Tensor dest_rank, torch::Tensor dest_row,
-             c10::optional<torch::Tensor> w, torch::Tensor bufs, c10::optional<torch::Tensor> origin_ptrs, int64_t me);
+void ep_push(torch::Tensor src, int64_t k_div, torch::Tensor gid, torch::Tensor pos, torch::Tensor seg,
+             torch::Tensor base, int64_t e_loc, c10::optional<torch::Tensor> w, torch::Tensor bufs,
+             c10::optional<torch::Tensor> origin_ptrs, int64_t me);
 void ep_return(torch::Tensor src, torch::Tensor origin, int64_t rows, torch::Tensor rets);
 void ep_pad(torch::Tensor land, torch::Tensor seg, torch::Tensor counts, c10::optional<torch::Tensor> origin);
 void sym_barrier(torch::Tensor sig_ptrs, int64_t me, int64_t epoch, int64_t timeout_ms);
@@ -110,8 +111,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("sym_barrier", &sym_barrier, py::arg("sig_ptrs"), py::arg("me"), py::arg("epoch"),
         py::arg("timeout_ms") = 60000);
   m.def("comm_error_flag", &comm_error_flag);
-  m.def("ep_push", &ep_push, py::arg("src"), py::arg("k_div"), py::arg("dest_rank"), py::arg("dest_row"),
-        py::arg("w"), py::arg("bufs"), py::arg("origin_ptrs"), py::arg("me"));
+  m.def("ep_push", &ep_push, py::arg("src"), py::arg("k_div"), py::arg("gid"), py::arg("pos"), py::arg("seg"),
+        py::arg("base"), py::arg("e_loc"), py::arg("w"), py::arg("bufs"), py::arg("origin_ptrs"), py::arg("me"));
   m.def("ep_return", &ep_return);
   m.def("ep_pad", &ep_pad, py::arg("land"), py::arg("seg"), py::arg("counts"), py::arg("origin"));
   m.def("gemm_grouped", &gemm_grouped);

@@ -7,9 +7,10 @@
 // segments padded to 128 rows) plus an origin array, and a return area of T * k rows.
 //
 //  * dispatch: assignment r (= token * k + slot) of this rank goes to expert e on rank d; its row is stored
-//    straight into rank d's landing area at row dest_row[r] (the host computed every rank's segment layout
-//    from the exchanged counts), optionally scaled by w[r], and origin[dest_row[r]] = (this rank << 24) | r is
-//    stored beside it, so the combine can send each expert output home without another exchange;
+//    straight into rank d's landing area at its final row (the host computed every rank's segment layout from
+//    the exchanged counts; the kernel adds the row's rank inside its expert), optionally scaled by w[r], and
+//    origin[row] = (this rank << 24) | r is stored beside it, so the combine can send each expert output home
+//    without another exchange;
 //  * combine: every valid landing row p sends its expert output back into the return area of rank
 //    origin[p] >> 24 at row origin[p] & 0xffffff.
 //
@@ -26,13 +27,16 @@ struct PeerPtrs {
 
 constexpr int MAX_R = 1 << 24;  // rows addressable through the 24-bit row field of an origin entry
 
-// one warp per assignment row
-__global__ void ep_push_kernel(const __nv_bfloat16* __restrict__ src, int k_div, const int* __restrict__ dest_rank,
-                               const int* __restrict__ dest_row, const float* __restrict__ w, int R, int H8,
-                               PeerPtrs bufs, PeerPtrs origins, int me) {
+// One warp per assignment row.  Assignment r of global expert g = gid[r]: owner rank g / e_loc, row base[g] + (pos[r] - seg[g]) there (pos /
+// seg: the sender's stable expert-sorted order, so rows keep their order inside a segment)
+__global__ void ep_push_kernel(const __nv_bfloat16* __restrict__ src, int k_div, const int* __restrict__ gid,
+                               const int* __restrict__ pos, const int* __restrict__ seg, const int* __restrict__ base,
+                               int e_loc, const float* __restrict__ w, int R, int H8, PeerPtrs bufs,
+                               PeerPtrs origins, int me) {
   const int lane = threadIdx.x & 31, warps = blockDim.x >> 5;
   for (int r = blockIdx.x * warps + (threadIdx.x >> 5); r < R; r += gridDim.x * warps) {
-    const int d = dest_rank[r], row = dest_row[r];
+    const int g = gid[r];
+    const int d = g / e_loc, row = base[g] + (pos[r] - seg[g]);
     const uint4* s = reinterpret_cast<const uint4*>(src + (size_t)(r / k_div) * H8 * 8);
     uint4* o = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(bufs.p[d]) + (size_t)row * H8 * 8);
     if (w == nullptr) {
@@ -96,14 +100,17 @@ int grid_rows(int64_t n) {
 
 }  // namespace
 
-// Push rows src[r / k_div] (times w[r]) to peer dest_rank[r]'s landing buffer at row dest_row[r]; with
-// `origin_ptrs` also record (me << 24 | r) in that peer's origin array.  bufs / origin_ptrs: int64 CPU [ep].
-void ep_push(at::Tensor src, int64_t k_div, at::Tensor dest_rank, at::Tensor dest_row, c10::optional<at::Tensor> w,
-             at::Tensor bufs, c10::optional<at::Tensor> origin_ptrs, int64_t me) {
+// Push rows src[r / k_div] (times w[r]) of assignments r with global experts gid[r] to the owners' landing
+// buffers (see ep_push_kernel for the row); with `origin_ptrs` also record (me << 24 | r) in the owner's origin
+// array.  gid / pos: int32 [R]; seg / base: int32 [E]; bufs / origin_ptrs: int64 CPU [ep].
+void ep_push(at::Tensor src, int64_t k_div, at::Tensor gid, at::Tensor pos, at::Tensor seg, at::Tensor base,
+             int64_t e_loc, c10::optional<at::Tensor> w, at::Tensor bufs, c10::optional<at::Tensor> origin_ptrs,
+             int64_t me) {
   TORCH_CHECK(src.is_cuda() && src.scalar_type() == at::kBFloat16 && src.is_contiguous() && src.size(1) % 8 == 0);
-  TORCH_CHECK(dest_rank.scalar_type() == at::kInt && dest_row.scalar_type() == at::kInt &&
-              dest_rank.numel() == dest_row.numel());
-  const int64_t R = dest_rank.numel();
+  for (const at::Tensor* t : {&gid, &pos, &seg, &base})
+    TORCH_CHECK(t->is_cuda() && t->scalar_type() == at::kInt && t->is_contiguous(), "ep_push: int32 CUDA index arrays");
+  TORCH_CHECK(gid.numel() == pos.numel() && seg.numel() >= base.numel() && e_loc >= 1);
+  const int64_t R = gid.numel();
   TORCH_CHECK(R < MAX_R && me < 128, "ep_push: too many rows for the origin encoding");
   const float* wp = nullptr;
   if (w.has_value() && w->defined()) {
@@ -111,12 +118,13 @@ void ep_push(at::Tensor src, int64_t k_div, at::Tensor dest_rank, at::Tensor des
     wp = w->data_ptr<float>();
   }
   PeerPtrs b = peers_of(bufs);
+  TORCH_CHECK(base.numel() <= e_loc * bufs.numel(), "ep_push: experts beyond the group");
   PeerPtrs o{};
   if (origin_ptrs.has_value() && origin_ptrs->defined()) o = peers_of(*origin_ptrs);
   if (R == 0) return;
   ep_push_kernel<<<grid_rows(R), 256, 0, cur_stream()>>>(
-      reinterpret_cast<const __nv_bfloat16*>(src.data_ptr()), (int)k_div, dest_rank.data_ptr<int>(),
-      dest_row.data_ptr<int>(), wp, (int)R, (int)(src.size(1) / 8), b, o, (int)me);
+      reinterpret_cast<const __nv_bfloat16*>(src.data_ptr()), (int)k_div, gid.data_ptr<int>(), pos.data_ptr<int>(),
+      seg.data_ptr<int>(), base.data_ptr<int>(), (int)e_loc, wp, (int)R, (int)(src.size(1) / 8), b, o, (int)me);
   EMB_LAUNCH_CHECK();
   count_launch();
 }

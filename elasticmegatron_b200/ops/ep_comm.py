@@ -74,17 +74,17 @@ class EPPlan:
         ac = allc.cpu().numpy().astype(np.int64)  # host sync: the next allocations depend on the counts
         seg_me, tot_me, base, tiles, self.cap, self.cap_max = host_layout(ac, self.me, e_loc)
         host = torch.from_numpy(np.concatenate([seg_me, tot_me, base, tiles]).astype(np.int32))
-        dv = host.to(dev, non_blocking=False)
+        dv = host.pin_memory().to(dev, non_blocking=True)
         o = 0
         self.seg = dv[o:o + e_loc + 1]; o += e_loc + 1
         self.counts = dv[o:o + e_loc]; o += e_loc
         base_d = dv[o:o + E]; o += E
         self.tiles = dv[o:]
-        gid = top.reshape(-1).to(torch.int32).contiguous()
-        pos_send, seg_send, _ = ext().moe_layout(gid, counts.to(torch.int32).contiguous(), max(gid.numel(), 1), 1)
-        g64 = gid.long()
-        self.dest_row = (base_d.long()[g64] + pos_send.long() - seg_send.long()[g64]).to(torch.int32).contiguous()
-        self.dest_rank = (gid // e_loc).to(torch.int32).contiguous()
+        self.base = base_d
+        self.e_loc = e_loc
+        self.gid = top.reshape(-1).to(torch.int32).contiguous()
+        self.pos_send, self.seg_send, _ = ext().moe_layout(self.gid, counts.to(torch.int32).contiguous(),
+                                                           max(self.gid.numel(), 1), 1)
         self.ident = torch.arange(self.T * self.k, device=dev, dtype=torch.int32)
         nb = self.H * 2
         self.land = _buffer(group, self.cap_max * nb, dev, "ep_land", 1 << 20)
@@ -103,7 +103,7 @@ class EPPlan:
         if with_origin:
             ho = self.org.next_half()
             optrs = self.org.peers[ho]
-        ext().ep_push(rows.contiguous(), self.k, self.dest_rank, self.dest_row,
+        ext().ep_push(rows.contiguous(), self.k, self.gid, self.pos_send, self.seg_send, self.base, self.e_loc,
                       None if w is None else w.reshape(-1).float().contiguous(), self.land.peers[h], optrs, self.me)
         self.land.barrier()
         land = self.land.view(h, torch.bfloat16, self.cap_max * self.H)[:self.cap * self.H].view(self.cap, self.H)
