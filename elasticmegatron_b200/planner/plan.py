@@ -208,6 +208,37 @@ class ReshardPlan:
         np.add.at(m, (self.desc["src_rank"], self.desc["dst_rank"]), by)
         return m
 
+    def describe(self, cfg: Optional[ModelConfig] = None, ranks: Optional[Iterable[int]] = None,
+                 max_params: Optional[int] = None) -> str:
+        """Human-readable plan: per virtual parameter, which ranks send how many elements of which state to
+        which ranks (the reference prints the same per-parameter send / receive plan in its debug mode,
+        transfer/transfer.py:271-289).  ``ranks`` restricts it to copies that touch those ranks."""
+        cfg = cfg or get_args().model
+        names = {vp.index: vp.name for vp in virtual_params(cfg)}
+        d = self.desc
+        if ranks is not None:
+            rs = np.array(sorted(set(ranks)))
+            d = d[np.isin(d["src_rank"], rs) | np.isin(d["dst_rank"], rs)]
+        lines = [f"reshard plan {self.src} -> {self.dst}: {len(d)} copies"]
+        vps = np.unique(d["vp"])
+        for i, v in enumerate(vps):
+            if max_params is not None and i >= max_params:
+                lines.append(f"  ... {len(vps) - max_params} more parameters")
+                break
+            dv = d[d["vp"] == v]
+            lines.append(f"  {names.get(int(v), v)}")
+            for kind, label in ((KIND_OPT, "fp32 master+moments"), (KIND_PARAM, "bf16 param")):
+                dk = dv[dv["kind"] == kind]
+                if not len(dk):
+                    continue
+                pairs = {}
+                for row in dk:
+                    key = (int(row["src_rank"]), int(row["dst_rank"]))
+                    pairs[key] = pairs.get(key, 0) + int(row["rows"]) * int(row["cols"])
+                moves = ", ".join(f"{s}->{t}:{n}" for (s, t), n in sorted(pairs.items()))
+                lines.append(f"    {label}: {moves}")
+        return "\n".join(lines)
+
     def nvlink_roofline_ms(self, link_gbs: float, opt_elem: int = 4, param_elem: int = 2) -> float:
         """max over GPUs of max(egress, ingress) of non-local bytes / link bandwidth."""
         m = self.bytes_matrix(opt_elem, param_elem)

@@ -22,6 +22,7 @@ A switch (reference call stack: elastic_manager.py:189-258):
 from __future__ import annotations
 
 import json
+import os
 import logging
 from typing import Callable, Dict, List, Optional, Union
 
@@ -184,6 +185,9 @@ class ElasticMegatronManager:
             src.rebuild()
         with nvtx_range("reshard/plan"):
             plan = self.plan(src_s, dst_s)
+        if self._rank == 0 and os.environ.get("EMB_RESHARD_DEBUG", "0") != "0":
+            # per-parameter send / receive plan (the reference's debug print, transfer/transfer.py:271-289)
+            print(plan.describe(), flush=True)
         if is_meta_device:
             # meta mode: no data moves; only pre-build state / connections (reference "fake transfer")
             ms, nbytes = 0.0, 0

@@ -112,3 +112,23 @@ def test_identity_plan_is_local_and_roofline_zero():
     p = build_plan(a, a, cfg, overlap_grad_reduce=False)
     assert (p.desc["src_rank"] == p.desc["dst_rank"]).all()
     assert p.nvlink_roofline_ms(770.0) == 0.0
+
+
+def test_plan_describe_lists_every_parameter():
+    from elasticmegatron_b200.config import Args, ModelConfig, TrainConfig, set_args
+    from elasticmegatron_b200.parallel.strategy import ParallelStrategy
+    from elasticmegatron_b200.planner.layout import virtual_params
+    from elasticmegatron_b200.planner.plan import build_plan
+
+    cfg = ModelConfig(num_layers=2, hidden_size=64, num_attention_heads=4, ffn_hidden_size=128, vocab_size=100,
+                      params_dtype="fp32", make_vocab_size_divisible_by=8, max_tensor_parallel_size=2)
+    set_args(Args(model=cfg, train=TrainConfig()))
+    a = ParallelStrategy(world_size=2, tensor_model_parallel_size=1, pipeline_model_parallel_size=1)
+    b = ParallelStrategy(world_size=2, tensor_model_parallel_size=2, pipeline_model_parallel_size=1)
+    text = build_plan(a, b, cfg).describe(cfg)
+    assert text.startswith("reshard plan ")
+    for vp in virtual_params(cfg):
+        assert vp.name in text
+    assert "fp32 master+moments" in text and "->" in text
+    short = build_plan(a, b, cfg).describe(cfg, ranks=[1], max_params=2)
+    assert "more parameters" in short
