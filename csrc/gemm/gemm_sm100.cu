@@ -132,6 +132,7 @@ struct Params {
   int a_mn, b_mn;  // operand majorness
   int* err;
   int split_tail;  // 2-SM kernel: run the last partial wave as 256 x 128 half tiles when they fit in one wave
+  int no_store;    // 2-SM kernel, measurement only: read the accumulators but write no output
   // grouped GEMM (1-SM kernel; MoE experts).  group_mode 1: A rows come in per-group segments padded to BM,
   // group_info[m tile] = group of that tile (-1: skip); B holds every group's matrix stacked along its row
   // coordinate, group g's rows start at g * group_b_stride.  group_mode 2 (weight gradient): group g reduces
@@ -682,7 +683,7 @@ __global__ void __launch_bounds__(AG ? NUM_THREADS_AG : NUM_THREADS, 1)
         TMEM_LD_32(taddr, r);
         asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
         const int col0 = n0 + c * 32;
-        if (!row_ok || col0 >= p.N) continue;
+        if (!row_ok || col0 >= p.N || p.no_store) continue;
         const int ncols = min(32, p.N - col0);
         void* gdst;
         if (p.scatter) {
@@ -892,8 +893,10 @@ at::Tensor gemm_tc(at::Tensor a, at::Tensor b, bool trans_a, bool trans_b, c10::
   p.err = err_flag();
   const int64_t tiles2 = ((M + 255) / 256) * ((N + 255) / 256);
   // variant: 0 auto, 1 one-SM tiles, 2 two-SM tiles, 3 two-SM tiles without the tail split (for comparison)
-  const bool pair = variant == 2 || variant == 3 || (variant <= 0 && tiles2 >= num_sms() / 2);
+  // variant 9: variant 2 without output stores (epilogue cost measurement; the result is not written)
+  const bool pair = variant == 2 || variant == 3 || variant == 9 || (variant <= 0 && tiles2 >= num_sms() / 2);
   p.split_tail = variant == 3 ? 0 : 1;
+  p.no_store = variant == 9 ? 1 : 0;
   if (pair) {
     // 2-SM clusters: each CTA loads a 128-row half of the A tile and of the B tile
     CUtensorMap tA2 = a_mn ? tA : make_map(a.data_ptr(), M, K, a.stride(0), 64, 128);

@@ -229,7 +229,7 @@ def main():
     ap.add_argument("--baseline", action="store_true")
     ap.add_argument("--variant", type=int, default=0,
                     help="0 = variants 1 and 2; 1 one-SM tiles, 2 two-SM cluster tiles, 3 two-SM tiles without the "
-                         "tail split")
+                         "tail split, 9 two-SM tiles writing no output (measures the epilogue's share)")
     ap.add_argument("--variants", default=None, help="comma list of GEMM variants for 'all' (overrides --variant)")
     a = ap.parse_args()
     variants = [int(v) for v in a.variants.split(",")] if a.variants else ((1, 2) if a.variant == 0 else (a.variant,))
