@@ -47,6 +47,7 @@ class SymmetricBuffer:
     def __init__(self, group, half_bytes: int, device: torch.device):
         self.group = group
         ranks = dist.get_process_group_ranks(group)
+        self.ranks = tuple(ranks)
         self.n = len(ranks)
         self.idx = ranks.index(dist.get_rank())
         half_bytes = (half_bytes + 4095) // 4096 * 4096
@@ -109,6 +110,24 @@ def _buffer(group, nbytes: int, device, tag: str = "", min_bytes: int = 64 << 20
         b = SymmetricBuffer(group, max(nbytes, min_bytes), device)
         _BUFS[key] = b
     return b
+
+
+def release_buffers() -> None:
+    """Unmap and free every symmetric buffer of this process (all ranks call it together, e.g. before the NCCL
+    communicators are re-created).  Buffers are visited in one global order (by rank set, then name) and each
+    is fenced by two barriers on its own group: nobody still uses a peer's arena when it is unmapped, and
+    nobody frees its arena while a peer still maps it."""
+    if not _BUFS:
+        return
+    for key, b in sorted(_BUFS.items(), key=lambda kv: (kv[1].ranks, kv[0][2])):
+        torch.cuda.synchronize(b.arena.device)
+        dist.all_reduce(b.flag, group=b.group)
+        torch.cuda.synchronize(b.arena.device)
+        b.close()
+        dist.all_reduce(b.flag, group=b.group)
+        torch.cuda.synchronize(b.arena.device)
+    _BUFS.clear()
+    _READY.clear()
 
 
 def enabled() -> bool:

@@ -86,6 +86,11 @@ class _ProcessGroupPool:
 
     def recreate_nccl_groups(self) -> None:
         """Destroy and re-create every cached NCCL group (frees NCCL buffers; all ranks must call)."""
+        import sys
+
+        tp_fused = sys.modules.get("elasticmegatron_b200.ops.tp_fused")
+        if tp_fused is not None:
+            tp_fused.release_buffers()  # symmetric buffers belong to the old communicators
         keys = sorted([k for k in self._groups if k[1] == "nccl"], key=lambda k: (len(k[0]), sorted(k[0])))
         for k in keys:
             pg = self._groups.pop(k)

@@ -25,6 +25,11 @@ def _rs_case(rank, world):
         got = tp_fused.gemm_reduce_scatter(a, b, False, trans_b, g)
         torch.cuda.synchronize()
         ok &= torch.allclose(got.float(), ref.float(), atol=0.05 * (K ** 0.5), rtol=2e-2)
+    # the buffers can be released (as before re-creating communicators) and are rebuilt on the next call
+    tp_fused.release_buffers()
+    got = tp_fused.gemm_reduce_scatter(a, b, False, trans_b, g)
+    torch.cuda.synchronize()
+    ok &= torch.allclose(got.float(), ref.float(), atol=0.05 * (K ** 0.5), rtol=2e-2)
     ok &= ext().comm_error_flag() == 0
     return bool(ok)
 
