@@ -70,7 +70,7 @@ def _summarize_clocks(samples: list) -> dict:
 def reference_arm(args):
     print(json.dumps({"impl": "reference", "unavailable": (
         "the reference (infinigence/ElasticMegatron) is a plug-in for Megatron-LM core_r0.11 + TransformerEngine, "
-        "neither of which is installed or installable offline; /root/reference has no setup.py/pyproject.toml so "
+        "neither of which is installed or installable offline; the reference source tree has no setup.py / pyproject.toml, so "
         "pip cannot install it either")}))
 
 
