@@ -237,6 +237,8 @@ def _hetero(rank, world, strat_idx):
     apply_hetero_dp(True)
     S = [ParallelStrategy(world_size=2, tensor_model_parallel_size=1, pipeline_model_parallel_size=1),
          ParallelStrategy(world_size=1, tensor_model_parallel_size=1, pipeline_model_parallel_size=1)]
+    if world == 4:  # DP2 x PP2: each pipeline runs 1F1B over its own number of micro-batches
+        S.append(ParallelStrategy(world_size=4, tensor_model_parallel_size=1, pipeline_model_parallel_size=2))
     create_all_groups(S)
     s = S[strat_idx]
     if rank >= s.world_size:
@@ -251,6 +253,13 @@ def test_hetero_dp_matches_single_rank():
     dp2 = run_distributed(_hetero, 2, 0)
     one = run_distributed(_hetero, 2, 1)
     np.testing.assert_allclose(dp2[0], one[0], rtol=2e-6)
+
+
+def test_hetero_dp_with_pipeline():
+    one = run_distributed(_hetero, 2, 1)
+    pp = run_distributed(_hetero, 4, 2)
+    last_stage = next(x for x in pp if x is not None and x[0] is not None)
+    np.testing.assert_allclose(one[0], last_stage, rtol=2e-6)
 
 
 def test_meta_device_context_and_exports():
