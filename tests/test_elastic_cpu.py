@@ -280,3 +280,18 @@ def test_meta_device_context_and_exports():
     ts.rebuild()
     assert ts.param_flat is not None and not ts.is_meta_device
     assert next(iter(ts.stage.params_by_name.values())).device.type == "cpu"
+
+
+MOE4 = [dict(world_size=4, tensor_model_parallel_size=1, pipeline_model_parallel_size=1,
+             expert_model_parallel_size=4, expert_tensor_parallel_size=1),
+        dict(world_size=4, tensor_model_parallel_size=2, pipeline_model_parallel_size=1,
+             expert_model_parallel_size=2, expert_tensor_parallel_size=1),
+        dict(world_size=4, tensor_model_parallel_size=1, pipeline_model_parallel_size=2,
+             expert_model_parallel_size=2, expert_tensor_parallel_size=1)]
+
+
+def test_moe_ep_schedule_on_four_ranks():
+    """The MoE switching schedule of the Mixtral configuration, scaled down: EP4 -> EP2*TP2 -> EP2*PP2 -> EP4."""
+    base = run_distributed(_train, 4, [None] * 5, True, False, MOE4)
+    sw = run_distributed(_train, 4, [None, 1, 2, 0, None], True, False, MOE4)
+    np.testing.assert_allclose(base[0], sw[0], rtol=2e-5)
