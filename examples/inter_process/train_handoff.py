@@ -4,6 +4,9 @@
         examples/inter_process/train_handoff.py --model llama2-7b --strategy ws8 \
         --successor-strategy ws4-tp2 --successor-nproc 4 --handoff-at 5 --train-iters 20
 
+``--chain a,b,c`` runs several hops (e.g. 8 -> 4 -> 8 GPUs with Group-ZeRO replicas dropped and rebuilt); every
+job behaves as below towards the next one.
+
 Old job ("primary"): trains on ``--strategy``; at iteration ``--handoff-at`` its rank 0 starts the successor
 job (``torchrun`` with ``--successor-nproc`` ranks on ``--successor-port``) through ``runtime/agent.py``, then
 keeps training and checks once per iteration whether the successor is ready (built its process group and
@@ -39,6 +42,10 @@ def parse_args(argv=None):
     ap.add_argument("--model", default="tiny-llama")
     ap.add_argument("--layers", type=int, default=None)
     ap.add_argument("--seq-length", type=int, default=None)
+    ap.add_argument("--chain", default=None,
+                    help="comma list of strategies, one job each, e.g. ws8-inst2,ws4,ws8-inst2 (8 -> 4 -> 8 GPUs); "
+                         "job h hands off at iteration (h + 1) * --handoff-at (overrides --strategy / "
+                         "--successor-strategy)")
     ap.add_argument("--strategy", default="ws2")
     ap.add_argument("--successor-strategy", default="ws1")
     ap.add_argument("--successor-nproc", type=int, default=None, help="default: world size of the successor")
@@ -94,82 +101,78 @@ def main(argv=None):
                   train=TrainConfig(micro_batch_size=a.micro_batch_size, global_batch_size=a.global_batch_size,
                                     lr=a.lr, train_iters=a.train_iters)))
     args = get_args()
-    old_s = ParallelStrategy.parse(a.strategy)
-    new_s = ParallelStrategy.parse(a.successor_strategy)
+    # the jobs of the run: hop h trains under chain[h] and hands its state to hop h + 1
+    chain = [ParallelStrategy.parse(x) for x in (a.chain.split(",") if a.chain else
+                                                    [a.strategy, a.successor_strategy])]
+    hop = int(os.environ.get("EMB_HOP", "0"))
+    me_s = chain[hop]
+    nxt = chain[hop + 1] if hop + 1 < len(chain) else None
+    last_iter = a.handoff_at * (hop + 1) if nxt is not None else None  # iteration at which the next job starts
     gloo_world = ProcessGroupPool.get(list(range(world)), "gloo")
-
-    if agent.role() == "successor":
-        root, tag = agent.handoff_location()
-        assert world >= new_s.world_size
-        create_all_groups([new_s])
-        ts = TrainingState(new_s) if rank < new_s.world_size else None
-        agent.mark_ready(root, tag, rank)
-        recs = import_records(root, tag, old_world=old_s.world_size, timeout=a.timeout)
+    create_all_groups([me_s])
+    ts = TrainingState(me_s) if rank < me_s.world_size else None
+    tag_me = f"hop{hop}"
+    if hop == 0:
+        if ts is not None:
+            ts.init_weights(a.seed)
+        start = 1
+        root = a.handoff_root or (tempfile.mkdtemp(prefix="emb_handoff_") if rank == 0 else None)
+        obj = [root]
+        dist.broadcast_object_list(obj, src=0, group=gloo_world)
+        root = obj[0]
+    else:
+        root, _ = agent.handoff_location()
+        agent.mark_ready(root, tag_me, rank)
+        recs = import_records(root, tag_me, old_world=chain[hop - 1].world_size, timeout=a.timeout)
         info = adopt(ts, recs) if ts is not None else None
-        ack(root, tag, rank)
+        ack(root, tag_me, rank)
         start = int(recs[0]["iteration"]) + 1
         args.iteration = start - 1
         args.consumed_train_samples = int(recs[0]["consumed_train_samples"])
-        if ts is not None:
-            if rank == 0:
-                print(f"successor adopted {info['src_strategy']} -> {new_s} at iteration {start - 1}", flush=True)
-            it = DataloaderState.build_iterators(ts, args.consumed_train_samples)[0]
-            for i in range(start, a.train_iters + 1):
-                t0 = time.perf_counter()
-                out = train_step(ts, it)
-                _log(rank, i, a.train_iters, out["loss"], (time.perf_counter() - t0) * 1e3, new_s, "successor")
-                args.iteration = i
-                args.consumed_train_samples += a.global_batch_size
-        dist.barrier(group=gloo_world)
-        dist.destroy_process_group()
-        return
-
-    # ---------------------------------------------------------------- primary (old) job
-    create_all_groups([old_s])
-    ts = TrainingState(old_s) if rank < old_s.world_size else None
-    if ts is not None:
-        ts.init_weights(a.seed)
-    it = DataloaderState.build_iterators(ts, 0)[0] if ts is not None else None
-    root = a.handoff_root or (tempfile.mkdtemp(prefix="emb_handoff_") if rank == 0 else None)
-    obj = [root]
-    dist.broadcast_object_list(obj, src=0, group=gloo_world)
-    root, tag = obj[0], "handoff"
-    child = None
-    n_new = a.successor_nproc or new_s.world_size
-    spawned = False
-    for i in range(1, a.train_iters + 1):
-        if spawned and agent.ready_consensus(root, tag, n_new, gloo_world):
+        if rank == 0 and info is not None:
+            print(f"job {hop} adopted {info['src_strategy']} -> {me_s} at iteration {start - 1}", flush=True)
+    it = DataloaderState.build_iterators(ts, args.consumed_train_samples)[0] if ts is not None else None
+    job = "primary" if hop == 0 else f"successor{hop}" if len(chain) > 2 else "successor"
+    tag_next = f"hop{hop + 1}"
+    n_new = (a.successor_nproc if (a.successor_nproc and len(chain) == 2) else nxt.world_size) if nxt else 0
+    child, spawned = None, False
+    for i in range(start, a.train_iters + 1):
+        if spawned and agent.ready_consensus(root, tag_next, n_new, gloo_world):
             break
         if ts is not None:
             t0 = time.perf_counter()
             out = train_step(ts, it)
-            _log(rank, i, a.train_iters, out["loss"], (time.perf_counter() - t0) * 1e3, old_s, "primary")
+            _log(rank, i, a.train_iters, out["loss"], (time.perf_counter() - t0) * 1e3, me_s, job)
         args.iteration = i
         args.consumed_train_samples += a.global_batch_size
-        if i == a.handoff_at:
+        if nxt is not None and i == last_iter:
             if rank == 0:
                 script = os.path.abspath(__file__)
                 cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", f"--nproc-per-node={n_new}",
-                       "--master-addr=127.0.0.1", f"--master-port={a.successor_port}", script] + \
+                       "--master-addr=127.0.0.1", f"--master-port={a.successor_port + hop}", script] + \
                     (argv if argv is not None else sys.argv[1:])
-                child = agent.spawn_successor(cmd, root, tag, log_path=os.path.join(root, "successor.log"))
+                child = agent.spawn_successor(cmd, root, tag_next, env={"EMB_HOP": str(hop + 1)},
+                                              log_path=os.path.join(root, f"{tag_next}.log"))
             spawned = True
             if a.block_at_handoff:
                 if rank == 0:
-                    agent.wait_ready(root, tag, n_new, timeout=a.timeout)
+                    agent.wait_ready(root, tag_next, n_new, timeout=a.timeout)
                 dist.barrier(group=gloo_world)
-    if ts is not None:
-        export_state(ts, root, tag)
-        wait_for_acks(root, tag, n_new, timeout=a.timeout)
-    dist.barrier(group=gloo_world)
-    if rank == 0:
-        print(f"primary exported {old_s} at iteration {args.iteration}; successor log: "
-              f"{os.path.join(root, 'successor.log')}", flush=True)
-        if a.wait_successor and child is not None:
-            rc = child.wait(timeout=a.timeout)
-            with open(os.path.join(root, "successor.log")) as f:
-                sys.stdout.write(f.read())
-            print(f"successor exit code {rc}", flush=True)
+    if nxt is not None:
+        if ts is not None:
+            export_state(ts, root, tag_next)
+            wait_for_acks(root, tag_next, n_new, timeout=a.timeout)
+        dist.barrier(group=gloo_world)
+        if rank == 0:
+            print(f"job {hop} exported {me_s} at iteration {args.iteration}; next job's log: "
+                  f"{os.path.join(root, tag_next + '.log')}", flush=True)
+            if a.wait_successor and child is not None:
+                rc = child.wait(timeout=a.timeout)
+                with open(os.path.join(root, f"{tag_next}.log")) as f:
+                    sys.stdout.write(f.read())
+                print(f"successor exit code {rc}", flush=True)
+    else:
+        dist.barrier(group=gloo_world)
     dist.destroy_process_group()
 
 

@@ -92,3 +92,19 @@ def test_examples_handoff_matches_intra_process_switch(tmp_path):
     for i in range(1, 7):
         assert abs(a[i] - b[i]) <= 1e-5 * abs(a[i]), (i, a[i], b[i])
     assert "successor exit code 0" in inter
+
+
+def test_handoff_chain_scale_down_and_up(tmp_path):
+    """Three jobs: 2 ranks -> 1 rank -> 2 ranks (the 8 -> 4 -> 8 configuration in small), each adopting the
+    previous job's state; the losses equal one job that switches at the same iterations."""
+    common = ["--cpu", "--layers", "2", "--seq-length", "64", "--train-iters", "6", "--global-batch-size", "8"]
+    intra = _torchrun(2, "intra_process/train_elastic.py",
+                      common + ["--strategies", "ws2,ws1,ws2", "--switch-every", "2", "--lr-warmup-iters", "0"])
+    inter = _torchrun(2, "inter_process/train_handoff.py",
+                      common + ["--chain", "ws2,ws1,ws2", "--handoff-at", "2", "--block-at-handoff", "--wait-successor",
+                                "--successor-port", str(free_port()), "--handoff-root", str(tmp_path)])
+    a, b = _losses(intra), _losses(inter)
+    assert sorted(a) == sorted(b) == list(range(1, 7)), (intra[-2000:], inter[-3000:])
+    for i in range(1, 7):
+        assert abs(a[i] - b[i]) <= 1e-5 * abs(a[i]), (i, a[i], b[i])
+    assert inter.count("successor exit code 0") == 2
