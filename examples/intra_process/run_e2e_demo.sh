@@ -10,10 +10,16 @@ LAYERS="${LAYERS:-}"
 PORT="${MASTER_PORT:-29500}"
 ITERS="${TRAIN_ITERS:-20}"
 STRATEGIES="${STRATEGIES:-}"   # e.g. ws8,ws2-tp2,ws4,ws2 (default: the reference's demo schedule)
+GBS="${GBS:-32}"
+if [ "${SCHEDULE:-}" = "tp-sweep" ]; then
+  # TP8 -> TP4*DP2 -> TP2*PP2*DP2 -> TP1*DP8 on 8 GPUs, global batch 128 (SP on whenever TP > 1)
+  STRATEGIES="ws8-tp8,ws8-tp4,ws8-tp2-pp2,ws8"
+  GBS=128
+fi
 LOG_DIR="${LOG_DIR:-$HERE/logs}"
 mkdir -p "$LOG_DIR"
 export CUDA_DEVICE_MAX_CONNECTIONS="${CUDA_DEVICE_MAX_CONNECTIONS:-1}"
-ARGS=(--model "$MODEL" --train-iters "$ITERS" --switch-every 2 --micro-batch-size 1 --global-batch-size 32
+ARGS=(--model "$MODEL" --train-iters "$ITERS" --switch-every 2 --micro-batch-size 1 --global-batch-size "$GBS"
       --lr 3e-4 --min-lr 3e-5 --lr-warmup-iters 2 --overlap-grad-reduce)
 [ -n "$LAYERS" ] && ARGS+=(--layers "$LAYERS")
 [ -n "$STRATEGIES" ] && ARGS+=(--strategies "$STRATEGIES")
