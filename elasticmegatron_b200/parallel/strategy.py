@@ -110,7 +110,7 @@ class ParallelStrategy:
         return (f"ws{self.world_size}-tp{self.tensor_model_parallel_size}-pp{self.pipeline_model_parallel_size}"
                 f"-cp{self.context_parallel_size}-dp{self.data_parallel_size}-ep{self.expert_model_parallel_size}"
                 f"-etp{self.expert_tensor_parallel_size}-inst{self.num_distributed_optimizer_instances}"
-                f"{'-sp' if self.sequence_parallel else ''}")
+                f"{'-sp' if self.sequence_parallel else ('-nosp' if self.tensor_model_parallel_size > 1 else '')}")
 
     def __repr__(self):
         return f"ParallelStrategy({self})"

@@ -78,3 +78,19 @@ def test_identity_includes_sp():
     b = ParallelStrategy(world_size=2, tensor_model_parallel_size=2, pipeline_model_parallel_size=1,
                          sequence_parallel=False, expert_tensor_parallel_size=1)
     assert a != b and a.layout_key() == b.layout_key()
+
+
+def test_parse_round_trip():
+    from elasticmegatron_b200.parallel.strategy import ParallelStrategy as P
+
+    for spec in ("ws8", "ws2-tp2", "ws4-tp2-nosp", "ws8-tp2-pp2-cp1-dp2-ep1-etp2-inst1-sp", "ws8-ep4-inst2",
+                 "ws8-tp2-cp2-pp2"):
+        s = P.parse(spec)
+        assert P.parse(str(s)) == s and P.from_any(str(s)) == s
+    assert P.parse("ws4-tp2").sequence_parallel and not P.parse("ws4-tp2-nosp").sequence_parallel
+    import pytest
+
+    with pytest.raises(ValueError):
+        P.parse("tp2")
+    with pytest.raises(ValueError):
+        P.parse("ws4-xx2")
