@@ -81,7 +81,10 @@ def test_identity_includes_sp():
 
 
 def test_parse_round_trip():
+    from elasticmegatron_b200.config import Args, set_args
     from elasticmegatron_b200.parallel.strategy import ParallelStrategy as P
+
+    set_args(Args())  # a dense model (with experts, ETP must be given as etp1 when TP > 1)
 
     for spec in ("ws8", "ws2-tp2", "ws4-tp2-nosp", "ws8-tp2-pp2-cp1-dp2-ep1-etp2-inst1-sp", "ws8-ep4-inst2",
                  "ws8-tp2-cp2-pp2"):
