@@ -9,7 +9,7 @@ PORT="${MASTER_PORT:-29500}"
 ITERS="${TRAIN_ITERS:-20}"
 LOG_DIR="${LOG_DIR:-$HERE/logs}"
 mkdir -p "$LOG_DIR"
-STRATEGIES="${STRATEGIES:-ws${NPROC}-ep4,ws${NPROC}-tp2-ep4,ws${NPROC}-ep8,ws${NPROC}-ep2}"
+STRATEGIES="${STRATEGIES:-ws${NPROC}-ep4,ws${NPROC}-tp2-ep4-etp1,ws${NPROC}-ep8,ws${NPROC}-ep2}"  # ETP stays 1 (experts are not TP-split)
 python -m torch.distributed.run --nnodes=1 --nproc-per-node "$NPROC" --master-addr 127.0.0.1 --master-port "$PORT" \
     "$HERE/train_elastic.py" --model mixtral-8x7b --layers 2 --train-iters "$ITERS" --switch-every 2 \
     --micro-batch-size 1 --global-batch-size 32 --strategies "$STRATEGIES" "$@" \
