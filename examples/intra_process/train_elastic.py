@@ -32,6 +32,8 @@ def parse_args(argv=None):
     ap.add_argument("--model", default="tiny-llama", help="preset name (config.PRESETS)")
     ap.add_argument("--layers", type=int, default=None)
     ap.add_argument("--seq-length", type=int, default=None)
+    ap.add_argument("--num-experts", type=int, default=None, help="override the preset's expert count (MoE)")
+    ap.add_argument("--moe-ffn", type=int, default=None, help="override the experts' ffn size")
     ap.add_argument("--strategies", default=None,
                     help="comma list of strategy specs, e.g. ws8,ws2-tp2,ws4,ws2 (default: the reference's demo "
                          "schedule scaled to the job size)")
@@ -89,6 +91,10 @@ def main(argv=None):
         over["num_layers"] = a.layers
     if a.seq_length:
         over["seq_length"] = a.seq_length
+    if a.num_experts:
+        over["num_experts"] = a.num_experts
+    if a.moe_ffn:
+        over["moe_ffn_hidden_size"] = a.moe_ffn
     if not use_cuda:
         over["params_dtype"] = "fp32"
     cfg = preset(a.model, **over)
