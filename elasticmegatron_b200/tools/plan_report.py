@@ -1,0 +1,71 @@
+"""What a switch will move, before running it: bytes per GPU pair, the NVLink roofline, the per-parameter plan.
+
+    python -m elasticmegatron_b200.tools.plan_report --model llama2-13b ws8 ws8-tp4
+    python -m elasticmegatron_b200.tools.plan_report --model mixtral-8x7b --layers 2 ws8-ep8 ws8-tp2-ep4-etp1 --params
+
+Runs the planner on the host only (no GPU, no processes).  The roofline is max over GPUs of max(egress, ingress)
+bytes that cross NVLink divided by ``--link-gbs`` (default: the measured 770 GB/s per direction of B200 peer
+copies); the JSON line at the end holds the same figures.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import sys
+
+import numpy as np
+
+
+def report(model: str, src: str, dst: str, layers=None, link_gbs: float = 770.0, params: bool = False,
+           max_params=None) -> dict:
+    from ..config import Args, TrainConfig, preset, set_args
+    from ..parallel.strategy import ParallelStrategy
+    from ..planner.plan import build_plan
+
+    over = {"max_tensor_parallel_size": 8}
+    if layers:
+        over["num_layers"] = layers
+    cfg = preset(model, **over)
+    set_args(Args(model=cfg, train=TrainConfig(overlap_grad_reduce=True)))
+    a, b = ParallelStrategy.parse(src), ParallelStrategy.parse(dst)
+    plan = build_plan(a, b, cfg, overlap_grad_reduce=True, ddp_bucket_size=None)
+    dt = 4
+    m = plan.bytes_matrix(dt, 2)
+    local = int(np.trace(m))
+    np.fill_diagonal(m, 0)
+    out = {"model": model, "src": str(a), "dst": str(b), "copies": int(len(plan.desc)),
+           "nvlink_bytes": int(m.sum()), "local_bytes": local,
+           "max_egress_bytes": int(m.sum(1).max(initial=0)), "max_ingress_bytes": int(m.sum(0).max(initial=0)),
+           "roofline_ms": plan.nvlink_roofline_ms(link_gbs, dt, 2), "link_gbs": link_gbs,
+           "bytes_matrix_gb": (m / 1e9).round(3).tolist()}
+    if params:
+        out["plan"] = plan.describe(cfg, max_params=max_params)
+    return out
+
+
+def main(argv=None) -> int:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("src")
+    ap.add_argument("dst")
+    ap.add_argument("--model", default="llama2-7b")
+    ap.add_argument("--layers", type=int, default=None)
+    ap.add_argument("--link-gbs", type=float, default=770.0)
+    ap.add_argument("--params", action="store_true", help="also print the per-parameter plan")
+    ap.add_argument("--max-params", type=int, default=None)
+    a = ap.parse_args(argv)
+    r = report(a.model, a.src, a.dst, a.layers, a.link_gbs, a.params, a.max_params)
+    print(f"{r['src']} -> {r['dst']} ({r['model']}): {r['copies']} copies, "
+          f"{r['nvlink_bytes'] / 1e9:.2f} GB over NVLink, {r['local_bytes'] / 1e9:.2f} GB local; "
+          f"busiest GPU sends {r['max_egress_bytes'] / 1e9:.2f} GB / receives {r['max_ingress_bytes'] / 1e9:.2f} GB; "
+          f"NVLink roofline {r['roofline_ms']:.2f} ms at {r['link_gbs']:.0f} GB/s")
+    print("GB sent (row) -> received (column):")
+    for i, row in enumerate(r["bytes_matrix_gb"]):
+        print(f"  {i}: " + " ".join(f"{x:7.2f}" for x in row))
+    if "plan" in r:
+        print(r.pop("plan"))
+    print(json.dumps({k: v for k, v in r.items() if k != "bytes_matrix_gb"}))
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -34,3 +34,13 @@ def test_loss_curve_reads_three_formats(tmp_path):
     assert read_log(str(p1)) == {1: (10.5, 812.5), 2: (10.4, 800.0)}
     assert read_log(str(p2)) == {1: (10.5, 10.0)}
     assert {k: v[0] for k, v in read_log(str(p3)).items()} == {1: 10.5, 2: 10.4}
+
+
+def test_plan_report(capsys):
+    from elasticmegatron_b200.tools.plan_report import main, report
+
+    r = report("tiny-llama", "ws2", "ws2-tp2", layers=2, params=True, max_params=3)
+    assert r["nvlink_bytes"] > 0 and r["roofline_ms"] > 0 and "reshard plan" in r["plan"]
+    assert len(r["bytes_matrix_gb"]) == 2 and r["bytes_matrix_gb"][0][0] == 0
+    assert main(["ws2-tp2", "ws2", "--model", "tiny-llama", "--layers", "2"]) == 0
+    assert "NVLink roofline" in capsys.readouterr().out
