@@ -13,6 +13,7 @@ _EXPORTS = {
     "meta_device_context": ("runtime.meta", "meta_device_context"),
     "nccl_group_recreate": ("parallel.process_groups", "nccl_group_recreate"),
     "global_barrier_by_gloo": ("parallel.process_groups", "global_barrier_by_gloo"),
+    "build_nccl_connection_context": ("runtime.manager", "build_nccl_connection_context"),
     "ParallelStrategy": ("parallel.strategy", "ParallelStrategy"),
     "TrainingState": ("runtime.training_state", "TrainingState"),
     "train_step": ("runtime.train", "train_step"),

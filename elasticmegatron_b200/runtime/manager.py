@@ -21,6 +21,7 @@ A switch (reference call stack: elastic_manager.py:189-258):
 """
 from __future__ import annotations
 
+import contextlib
 import json
 import os
 import logging
@@ -84,6 +85,7 @@ class ElasticMegatronManager:
             self.engine_name = engine or ("native" if torch.cuda.is_available() else "torch")
             self.engine = self._make_engine(self.engine_name)
         self.last_switch: Dict = {}
+        self._warm_only = False
         set_world_group(ProcessGroupPool.get(self.current.ranks))
 
     # ------------------------------------------------------------------ helpers
@@ -264,6 +266,64 @@ class ElasticMegatronManager:
             log_json("recover", logger, src=str(src_s), dst=str(dst_s), failed=sorted(failed))
         return dst
 
+    # ------------------------------------------------------------------ the reference's step-level API
+    # The reference's manager exposes the steps of a switch as methods taking its per-strategy state objects
+    # (elastic_manager.py:106-178); these take TrainingState objects (or None on ranks outside a strategy) and
+    # are what ``reshard`` runs.
+
+    def transfer_params(self, src_state: Optional[TrainingState], dst_state: Optional[TrainingState],
+                        union_world_group=None, is_meta_device: bool = False, src_strategy=None,
+                        dst_strategy=None) -> float:
+        """Move parameters and optimizer state from ``src_state``'s layout to ``dst_state``'s; returns the
+        device time in ms (0 in meta mode - or inside ``build_nccl_connection_context`` - which only maps peers
+        and builds the task tables).  A rank without state under a layout passes None and names the layout."""
+        src_s = self._strategy_of(src_state, src_strategy)
+        dst_s = self._strategy_of(dst_state, dst_strategy)
+        plan = self.plan(src_s, dst_s)
+        ugroup = union_world_group or ProcessGroupPool.get(union_ranks(src_s, dst_s))
+        if is_meta_device or self._warm_only:
+            if hasattr(self.engine, "warmup"):
+                self.engine.warmup(plan, self._rank, src_state, dst_state, ugroup)
+            return 0.0
+        ms, _ = self._transfer(plan, src_state, dst_state, ugroup, src_s.layout_key() == dst_s.layout_key())
+        return ms
+
+    def redundant_backup(self, src_state: Optional[TrainingState], dst_state: Optional[TrainingState],
+                         is_scale_up: bool = False, is_meta_device: bool = False, src_strategy=None,
+                         dst_strategy=None) -> float:
+        """Group-ZeRO instance-count change.  Dropping replicas (scale-down) and rebuilding them (scale-up) are
+        plans like any other switch here, so this is ``transfer_params``; ``is_scale_up`` is accepted for the
+        reference's signature."""
+        return self.transfer_params(src_state, dst_state, None, is_meta_device, src_strategy, dst_strategy)
+
+    def transfer_learning_rate(self, src_state: Optional[TrainingState], dst_state: Optional[TrainingState],
+                               src_strategy=None, dst_strategy=None) -> None:
+        """Optimizer step counters, LR and scheduler position from rank 0 to every rank of ``dst_state``."""
+        self._transfer_lr(src_state, dst_state, union_ranks(self._strategy_of(src_state, src_strategy),
+                                                            self._strategy_of(dst_state, dst_strategy)))
+
+    def log_communication_info(self, transfer_time: float, union_world_group=None,
+                               logger: Optional[logging.Logger] = None, nbytes: int = 0) -> Dict:
+        """MAX over the union of (transfer ms, GB moved); logged as one JSON line on rank 0 (or to ``logger``).
+        ``union_world_group`` must be a host (gloo) group when given."""
+        grp = union_world_group
+        if grp is None and dist.is_initialized():
+            grp = ProcessGroupPool.gloo_world()
+        mx = max_over_ranks([transfer_time, nbytes / 1e9], group=grp)
+        info = {"transfer_ms": mx[0], "gbytes": mx[1],
+                "bandwidth_gbs": (mx[1] / (mx[0] / 1e3)) if mx[0] > 0 else None}
+        if self._rank == 0 or logger is not None:
+            log_json("communication", logger, **info)
+        return info
+
+    @staticmethod
+    def _strategy_of(state: Optional[TrainingState], strategy=None) -> ParallelStrategy:
+        if state is not None:
+            return state.strategy
+        if strategy is None:
+            raise ValueError("a rank without state under a layout must name the layout (src_strategy / dst_strategy)")
+        return ParallelStrategy.from_any(strategy)
+
     # ------------------------------------------------------------------ internals
     def _transfer(self, plan, src, dst, ugroup, same_layout: bool):
         eng = self.engine
@@ -297,3 +357,17 @@ class ElasticMegatronManager:
         if dst is not None and obj[0] is not None:
             dst.optimizer.load_state_dict(obj[0]["opt"])
             dst.opt_param_scheduler.load_state_dict(obj[0]["sched"])
+
+
+@contextlib.contextmanager
+def build_nccl_connection_context(manager: "ElasticMegatronManager"):
+    """Inside the block the manager's transfers (``transfer_params`` / ``redundant_backup``) only pre-build
+    what a switch needs - peer mappings and task tables - and move no data: the reference's "fake transfer",
+    used to pay the connection set-up outside the timed switch (elastic_manager.py:268-304).  ``reshard`` has
+    the same mode as ``reshard(..., is_meta_device=True)``."""
+    prev = manager._warm_only
+    manager._warm_only = True
+    try:
+        yield manager
+    finally:
+        manager._warm_only = prev

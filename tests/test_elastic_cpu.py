@@ -295,3 +295,39 @@ def test_moe_ep_schedule_on_four_ranks():
     base = run_distributed(_train, 4, [None] * 5, True, False, MOE4)
     sw = run_distributed(_train, 4, [None, 1, 2, 0, None], True, False, MOE4)
     np.testing.assert_allclose(base[0], sw[0], rtol=2e-5)
+
+
+def _step_api(rank, world, use_steps):
+    from elasticmegatron_b200 import build_nccl_connection_context
+    from elasticmegatron_b200.parallel.process_groups import create_all_groups
+    from elasticmegatron_b200.parallel.strategy import ParallelStrategy
+    from elasticmegatron_b200.runtime.data import DataloaderState
+    from elasticmegatron_b200.runtime.manager import ElasticMegatronManager
+    from elasticmegatron_b200.runtime.train import train_step
+    from elasticmegatron_b200.runtime.training_state import TrainingState
+
+    _setup()
+    S = [ParallelStrategy(**s) for s in STRATS[:2]]
+    create_all_groups(S)
+    ts = TrainingState(S[0])
+    ts.init_weights(0)
+    mgr = ElasticMegatronManager(STRATS[:2], training_state=ts, engine="torch")
+    train_step(ts, mgr.build_iterators(0)[0])
+    if not use_steps:
+        dst = mgr.reshard(STRATS[1])
+    else:  # the reference's step-level API
+        dst = TrainingState(S[1])
+        with build_nccl_connection_context(mgr):
+            assert mgr.transfer_params(ts, dst) == 0.0  # pre-build only
+        ms = mgr.transfer_params(ts, dst)
+        mgr.transfer_learning_rate(ts, dst)
+        info = mgr.log_communication_info(ms, nbytes=1 << 20)
+        assert info["transfer_ms"] >= 0 and info["gbytes"] > 0
+    it = mgr.build_iterators(8)[0] if not use_steps else DataloaderState.build_iterators(dst, 8)[0]
+    return train_step(dst, it)["loss"]
+
+
+def test_reference_step_level_api_matches_reshard():
+    a = run_distributed(_step_api, 2, False)
+    b = run_distributed(_step_api, 2, True)
+    np.testing.assert_allclose(a[0], b[0], rtol=1e-7)
