@@ -144,6 +144,10 @@ class ElasticMegatronManager:
             dist.broadcast(t, src=0, group=ProcessGroupPool.get(self.current.ranks, "gloo"))
         return DataloaderState.build_iterators(ts, int(t.item()))
 
+    def need_resharding(self, parallel_strategy) -> bool:
+        """True when ``parallel_strategy`` differs from the current one (reference: megatron_state.py:151-156)."""
+        return ParallelStrategy.from_any(parallel_strategy) != self.current
+
     def get_data_parallel_group(self, parallel_strategy):
         s = ParallelStrategy.from_any(parallel_strategy)
         if self._rank >= s.world_size:

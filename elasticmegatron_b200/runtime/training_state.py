@@ -8,7 +8,7 @@ optimizer, scheduler) survives a release.
 """
 from __future__ import annotations
 
-from typing import Callable, Dict, Optional
+from typing import Callable, Dict, List, Optional
 
 import torch
 
@@ -212,3 +212,24 @@ class TrainingState:
         for a, o, n, wd, c in self.optimizer.segs:
             P[a:a + n].copy_(O[0, o:o + n].to(P.dtype))
         self.ddp.start_param_sync()
+
+    def save_checkpoint(self, path: str, iteration: Optional[int] = None) -> str:
+        """Megatron legacy checkpoint of this layout (collective over the strategy's ranks; reference:
+        training_state.py:325-366)."""
+        from .checkpoint import save_checkpoint
+
+        return save_checkpoint(self, path, iteration)
+
+    def get_metadata(self) -> Dict:
+        """Where this rank's state lives: strategy, arena sizes and the ZeRO segments of the optimizer (the
+        reference keeps per-parameter metadata for its planner, training_state.py:145-174; here the layout is a
+        pure function of the strategy, so this is a description, not an input)."""
+        return {"strategy": self.strategy.to_dict(), "rank": self.rank,
+                "param_numel": self.layout.param_numel, "opt_numel": self.layout.opt_numel,
+                "segments": [(int(a), int(o), int(n)) for a, o, n, *_ in self.optimizer.segs],
+                "model_released": self.model_released, "optimizer_released": self.optimizer_released}
+
+    def all_optimizer_tensors(self) -> List[torch.Tensor]:
+        """fp32 master, exp_avg and exp_avg_sq of this rank's shard (views into the optimizer arena)."""
+        O = self.opt_flat
+        return [] if O is None else [O[0], O[1], O[2]]

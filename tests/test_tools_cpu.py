@@ -44,3 +44,22 @@ def test_plan_report(capsys):
     assert len(r["bytes_matrix_gb"]) == 2 and r["bytes_matrix_gb"][0][0] == 0
     assert main(["ws2-tp2", "ws2", "--model", "tiny-llama", "--layers", "2"]) == 0
     assert "NVLink roofline" in capsys.readouterr().out
+
+
+def test_training_state_reference_helpers(tmp_path):
+    import os
+
+    from test_elastic_cpu import _setup
+
+    from elasticmegatron_b200.parallel.strategy import ParallelStrategy
+    from elasticmegatron_b200.runtime.training_state import TrainingState
+
+    _setup()
+    ts = TrainingState(ParallelStrategy(world_size=1, tensor_model_parallel_size=1, pipeline_model_parallel_size=1))
+    ts.init_weights(0)
+    md = ts.get_metadata()
+    assert md["param_numel"] == ts.layout.param_numel and md["segments"]
+    master, m, v = ts.all_optimizer_tensors()
+    assert master.shape == m.shape == v.shape
+    d = ts.save_checkpoint(str(tmp_path), iteration=5)
+    assert os.path.exists(os.path.join(d, "model_optim_rng.pt"))
