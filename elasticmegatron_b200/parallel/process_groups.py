@@ -206,6 +206,10 @@ class ParallelState:
     def _set(self, name: str, ranks: List[int]):
         self.group_ranks[name] = ranks
         self.groups[name] = ProcessGroupPool.get(ranks, self.backend) if dist.is_initialized() else None
+        if dist.is_initialized() and len(ranks) > 1 and self.groups[name] is None:
+            raise RuntimeError(
+                f"no {self.backend} process group for ranks {ranks} ({name} of {self.strategy}); create the groups of "
+                f"every strategy first, on all ranks: create_all_groups([...]) or ElasticMegatronManager(...)")
 
     def group(self, name: str):
         return self.groups[name]

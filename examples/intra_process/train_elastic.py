@@ -82,6 +82,7 @@ def main(argv=None):
 
     from elasticmegatron_b200 import ElasticMegatronManager
     from elasticmegatron_b200.config import Args, TrainConfig, get_args, preset, set_args
+    from elasticmegatron_b200.parallel.process_groups import create_all_groups
     from elasticmegatron_b200.parallel.strategy import ParallelStrategy
     from elasticmegatron_b200.runtime.train import train_step
     from elasticmegatron_b200.runtime.training_state import TrainingState
@@ -107,6 +108,7 @@ def main(argv=None):
     uniq = list(dict.fromkeys(strategies))
     assert strategies[0].world_size <= world
 
+    create_all_groups(uniq)  # collectively, on every rank, before any state is built
     ts = TrainingState(strategies[0]) if rank < strategies[0].world_size else None
     if ts is not None:
         ts.init_weights(a.seed)
