@@ -38,6 +38,11 @@ def report(model: str, src: str, dst: str, layers=None, link_gbs: float = 770.0,
            "max_egress_bytes": int(m.sum(1).max(initial=0)), "max_ingress_bytes": int(m.sum(0).max(initial=0)),
            "roofline_ms": plan.nvlink_roofline_ms(link_gbs, dt, 2), "link_gbs": link_gbs,
            "bytes_matrix_gb": (m / 1e9).round(3).tolist()}
+    from ..planner.memory import layout_report, switch_peak_bytes
+
+    out["memory_gb"] = {"src": {k: v / 1e9 for k, v in layout_report(cfg, a).items()},
+                        "dst": {k: v / 1e9 for k, v in layout_report(cfg, b).items()},
+                        "switch_peak_state": switch_peak_bytes(cfg, a, b) / 1e9}
     if params:
         out["plan"] = plan.describe(cfg, max_params=max_params)
     return out
@@ -58,6 +63,10 @@ def main(argv=None) -> int:
           f"{r['nvlink_bytes'] / 1e9:.2f} GB over NVLink, {r['local_bytes'] / 1e9:.2f} GB local; "
           f"busiest GPU sends {r['max_egress_bytes'] / 1e9:.2f} GB / receives {r['max_ingress_bytes'] / 1e9:.2f} GB; "
           f"NVLink roofline {r['roofline_ms']:.2f} ms at {r['link_gbs']:.0f} GB/s")
+    mem = r["memory_gb"]
+    print(f"per-GPU memory (largest rank): source {mem['src']['peak']:.1f} GB (state {mem['src']['total']:.1f} + "
+          f"activations ~{mem['src']['activations']:.1f}), destination {mem['dst']['peak']:.1f} GB; during the "
+          f"switch both states: {mem['switch_peak_state']:.1f} GB")
     print("GB sent (row) -> received (column):")
     for i, row in enumerate(r["bytes_matrix_gb"]):
         print(f"  {i}: " + " ".join(f"{x:7.2f}" for x in row))

@@ -116,6 +116,18 @@ def main():
     engines = {"native": NativeP2PEngine, "torch": TorchP2PEngine, "reference": ReferenceAlgorithmEngine}
     results = []
 
+    def fits(a, b) -> bool:
+        """Source and destination arenas (params + optimizer) of the largest rank must fit together."""
+        need = 0
+        for r in range(max(a.world_size, b.world_size)):
+            n = 0
+            for s in (a, b):
+                if r < s.world_size:
+                    rl = rank_layout(cfg, s, r, True, None)
+                    n += rl.param_numel * 2 + rl.opt_numel * 12
+            need = max(need, n)
+        return need * 1.05 < torch.cuda.get_device_properties(dev).total_memory
+
     def run_pair(eng_name, eng, a, b, iters):
         plan = build_plan(a, b, cfg, overlap_grad_reduce=True, ddp_bucket_size=None)
         sa = arenas(a) if rank < a.world_size else None
@@ -152,6 +164,12 @@ def main():
     for eng_name in args.engines.split(","):
         eng = engines[eng_name](mode=args.mode) if eng_name == "native" else engines[eng_name]()
         for a, b in pairs:
+            if not fits(a, b):
+                if rank == 0:
+                    print(json.dumps({"engine": eng_name, "src": str(a), "dst": str(b), "skipped":
+                                      "source and destination state do not fit in one GPU's memory together "
+                                      "(use --layers to shrink the model)"}), flush=True)
+                continue
             ts, nbytes, roof = run_pair(eng_name, eng, a, b, args.iters)
             p50 = statistics.median(ts)
             rec = {"engine": eng_name + (f"-{args.mode}" if eng_name == "native" else ""), "src": str(a), "dst": str(b), "p50_ms": p50, "all_ms": ts,

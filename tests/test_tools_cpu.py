@@ -63,3 +63,22 @@ def test_training_state_reference_helpers(tmp_path):
     assert master.shape == m.shape == v.shape
     d = ts.save_checkpoint(str(tmp_path), iteration=5)
     assert os.path.exists(os.path.join(d, "model_optim_rng.pt"))
+
+
+def test_memory_estimate():
+    from elasticmegatron_b200.config import Args, TrainConfig, preset, set_args
+    from elasticmegatron_b200.parallel.strategy import ParallelStrategy as P
+    from elasticmegatron_b200.planner.memory import fits, layout_report, state_bytes, switch_peak_bytes
+
+    cfg = preset("llama2-13b", max_tensor_parallel_size=8)
+    set_args(Args(model=cfg, train=TrainConfig(overlap_grad_reduce=True)))
+    s1, s2 = P.parse("ws8"), P.parse("ws8-tp4")
+    st = state_bytes(cfg, s1, 0)
+    assert st["params"] * 2 == st["grads"] and st["total"] == st["params"] + st["grads"] + st["optimizer"]
+    assert layout_report(cfg, s2)["peak"] < layout_report(cfg, s1)["peak"]  # TP4 shards params and activations
+    assert switch_peak_bytes(cfg, s1, s2) == max(state_bytes(cfg, s1, r)["total"] + state_bytes(cfg, s2, r)["total"]
+                                                 for r in range(8))
+    ok = fits(cfg, [s1, s2], 183 * 2**30)
+    assert set(ok) == {str(s1), str(s2)} and all("fits" in v for v in ok.values())
+    two = fits(cfg, [P.parse("ws2"), P.parse("ws2-tp2")], 183 * 2**30)
+    assert not any(v["fits"] for v in two.values())  # 13B on 2 GPUs: switching needs both layouts at once
