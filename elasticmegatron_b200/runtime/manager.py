@@ -87,6 +87,31 @@ class ElasticMegatronManager:
         self.last_switch: Dict = {}
         self._warm_only = False
         set_world_group(ProcessGroupPool.get(self.current.ranks))
+        self.memory_warnings = self._check_memory()
+
+    def _check_memory(self) -> List[Dict]:
+        """Warn (one JSON line each, never fail) about switches whose source and destination state cannot sit
+        in this GPU's memory together (``planner/memory.py``)."""
+        if not torch.cuda.is_available():
+            return []
+        try:
+            from ..planner.memory import state_bytes
+
+            cap = torch.cuda.get_device_properties(torch.cuda.current_device()).total_memory
+            tc = get_args().train
+            cfg = get_args().model
+            mine = {s: state_bytes(cfg, s, self._rank, tc.overlap_grad_reduce, tc.ddp_bucket_size)["total"]
+                    for s in self.strategies if self._rank < s.world_size}
+            out = []
+            for a in mine:
+                for b in mine:
+                    if a != b and mine[a] + mine[b] > 0.95 * cap:
+                        w = {"src": str(a), "dst": str(b), "state_gb": (mine[a] + mine[b]) / 1e9, "device_gb": cap / 1e9}
+                        out.append(w)
+                        log_json("memory_warning", None, **w)
+            return out
+        except Exception:  # an estimate must never stop a job
+            return []
 
     # ------------------------------------------------------------------ helpers
     def _make_engine(self, name: str):
