@@ -93,7 +93,6 @@ def main():
         reference_arm(args)
         return
 
-    import numpy as np
     import torch
     import torch.distributed as dist
 

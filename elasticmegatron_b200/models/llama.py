@@ -19,7 +19,6 @@ from __future__ import annotations
 from typing import Dict, List, Optional
 
 import torch
-import torch.distributed as dist
 from torch import nn
 
 from ..config import ModelConfig

@@ -8,7 +8,6 @@ which the DDP layer uses to start bucket reduce-scatters.
 """
 from __future__ import annotations
 
-import math
 from typing import Optional
 
 import torch

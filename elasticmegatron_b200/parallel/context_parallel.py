@@ -8,7 +8,6 @@ prefix of keys that ends with its own chunk.  In the reference CP lives entirely
 from __future__ import annotations
 
 import torch
-import torch.distributed as dist
 
 from ..ops import functional as F_
 

@@ -19,7 +19,7 @@ from typing import Dict, List, Optional
 import torch
 import torch.distributed as dist
 
-from ..planner.layout import BufferLayout, RankLayout
+from ..planner.layout import RankLayout
 
 
 def _rs_inplace(buf: torch.Tensor, shard_index: int, group) -> None:

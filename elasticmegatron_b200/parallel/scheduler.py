@@ -8,7 +8,7 @@ restore the position without stepping.
 from __future__ import annotations
 
 import math
-from typing import Dict, List
+from typing import Dict
 
 
 class OptimizerParamScheduler:

@@ -19,7 +19,7 @@ Differences by design:
 """
 from __future__ import annotations
 
-from dataclasses import dataclass, field, fields
+from dataclasses import dataclass, fields
 from typing import Dict, List, Optional
 
 from ..config import get_args

@@ -22,7 +22,6 @@ its optimizer arena ``[dense shards | expert shards]``.
 from __future__ import annotations
 
 from dataclasses import dataclass, field
-from functools import lru_cache
 from typing import Dict, List, Optional, Tuple
 
 from ..config import ModelConfig

@@ -11,7 +11,6 @@ from typing import Dict, Optional
 import torch
 
 from ..config import ModelConfig
-from ..models.spec import VParam
 from .plan import _StrategyView
 
 

@@ -13,7 +13,7 @@ from __future__ import annotations
 
 import threading
 import time
-from typing import Iterable, Optional, Set
+from typing import Iterable, Set
 
 import torch.distributed as dist
 

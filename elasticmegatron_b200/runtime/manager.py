@@ -22,7 +22,6 @@ A switch (reference call stack: elastic_manager.py:189-258):
 from __future__ import annotations
 
 import contextlib
-import json
 import os
 import logging
 from typing import Callable, Dict, List, Optional, Union

@@ -27,7 +27,7 @@ import torch.distributed as dist
 
 from ..ops.native import ext
 from ..parallel.process_groups import ProcessGroupPool
-from ..planner.plan import KIND_OPT, KIND_PARAM, ReshardPlan
+from ..planner.plan import KIND_OPT, ReshardPlan
 
 TASK_DTYPE = np.dtype([
     ("src", np.uint64), ("dst", np.uint64), ("src_stride", np.uint64), ("dst_stride", np.uint64),

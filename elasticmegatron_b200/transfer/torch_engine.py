@@ -9,7 +9,6 @@ peer) in three phases (elastic_megatron/transfer/transfer.py:291-341, p2p_to_col
 """
 from __future__ import annotations
 
-from collections import defaultdict
 from typing import Dict, List, Optional, Tuple
 
 import numpy as np
