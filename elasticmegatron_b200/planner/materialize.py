@@ -14,13 +14,6 @@ from ..config import ModelConfig
 from .plan import _StrategyView
 
 
-def _box_views(piece, arena: torch.Tensor, r0, r1, c0, c1):
-    """Yield (row_index, arena_slice) for each row of the box inside a flat arena."""
-    for gr in range(r0, r1):
-        o = piece.off(gr, c0)
-        yield gr, arena[o:o + (c1 - c0)]
-
-
 def _global2d(t: torch.Tensor) -> torch.Tensor:
     return t.reshape(1, -1) if t.dim() == 1 else t.reshape(-1, t.shape[-1])
 
