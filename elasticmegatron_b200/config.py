@@ -114,6 +114,8 @@ class TrainConfig:
     grad_reduce_in_fp32: bool = True
     # memory
     recompute: bool = False
+    # context parallelism: "all_gather" (K/V gathered over the CP group) or "p2p" (K/V passed round a ring)
+    cp_comm_type: str = "all_gather"
 
 
 @dataclass

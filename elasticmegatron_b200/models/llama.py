@@ -26,7 +26,7 @@ from ..ops import functional as F_
 from ..ops import reference as ref
 from ..models.spec import LocalParam
 from .moe import MoELayer
-from ..parallel.context_parallel import cp_attention
+from ..parallel.context_parallel import CP_COMM_TYPES, cp_attention, cp_ring_attention
 
 
 class RotaryCache:
@@ -58,8 +58,10 @@ def cp_positions(seq: int, cp: int, cp_rank: int) -> torch.Tensor:
 
 class GPTStage(nn.Module):
     def __init__(self, cfg: ModelConfig, pstate, params: List[LocalParam], views: Dict[str, torch.Tensor],
-                 micro_batch_size: int):
+                 micro_batch_size: int, cp_comm_type: str = "all_gather"):
         super().__init__()
+        if cp_comm_type not in CP_COMM_TYPES:
+            raise ValueError(f"cp_comm_type must be one of {CP_COMM_TYPES}, got {cp_comm_type!r}")
         self.cfg, self.ps = cfg, pstate
         s = pstate.strategy
         self.tp = s.tensor_model_parallel_size
@@ -69,6 +71,7 @@ class GPTStage(nn.Module):
         self.mbs = micro_batch_size
         self.tp_group = pstate.group("tp") if self.tp > 1 else None
         self.cp_group = pstate.group("cp") if self.cp > 1 else None
+        self.cp_attention = cp_ring_attention if cp_comm_type == "p2p" else cp_attention
         self.params_by_name: Dict[str, nn.Parameter] = {}
         for lp in params:
             p = nn.Parameter(views[lp.name], requires_grad=True)
@@ -135,7 +138,7 @@ class GPTStage(nn.Module):
         qkv = qkv.view(seq_local, b, G_loc, hpg + 2, d)
         qkv = F_.rope_qkv(qkv, cos, sin, hpg + 1)
         if self.cp > 1:
-            attn = cp_attention(qkv, hpg, self.cp_group, self.ps.cp_rank, self.cp)
+            attn = self.cp_attention(qkv, hpg, self.cp_group, self.ps.cp_rank, self.cp)
         else:
             attn = F_.attention(qkv, hpg)
         o = F_.linear(attn.view(seq_local * b, -1), self._p(i, "self_attention.linear_proj.weight"),

@@ -1,15 +1,30 @@
 """Context parallelism: attention over a sequence split into 2*CP load-balanced chunks.
 
-CP rank ``r`` holds chunks ``r`` and ``2*CP-1-r`` (so every rank does the same amount of causal work).  K and
-V are all-gathered over the CP group (reduce-scattered in backward); each query chunk attends to the global
-prefix of keys that ends with its own chunk.  In the reference CP lives entirely in Megatron/TE
-(context_parallel_size is only carried and folded into the ZeRO group, parallel_strategy.py:131-147).
+CP rank ``r`` holds chunks ``r`` and ``2*CP-1-r`` (so every rank does the same amount of causal work).  Two
+ways to exchange keys and values over the CP group (Megatron's ``--cp-comm-type``):
+
+* ``"all_gather"`` (default, :func:`cp_attention`): K and V are all-gathered (reduce-scattered in backward);
+  each query chunk is one fused attention call over the global prefix of keys that ends with its own chunk.
+* ``"p2p"`` (:func:`cp_ring_attention`): a ring.  Every step each rank sends the K/V block it holds to the
+  next CP rank and receives one from the previous; the transfer of step ``t+1`` is posted before the math of
+  step ``t``, so the exchange overlaps the attention.  Partial outputs are merged by their log-sum-exp; the
+  backward pass sends the K/V blocks round again with their dK/dV accumulators, which end at their owners.
+  No rank ever holds more than two K/V blocks.
+
+In the reference CP lives entirely in Megatron/TE (context_parallel_size is only carried and folded into the
+ZeRO group, parallel_strategy.py:131-147).
 """
 from __future__ import annotations
 
+import math
+from typing import List, Tuple
+
 import torch
+import torch.distributed as dist
 
 from ..ops import functional as F_
+
+CP_COMM_TYPES = ("all_gather", "p2p")
 
 
 def _global_chunk_starts(s: int, cp: int):
@@ -46,3 +61,153 @@ def cp_attention(qkv: torch.Tensor, hpg: int, group, cp_rank: int, cp: int) -> t
                                                              enable_gqa=hpg > 1)
         outs.append(o.permute(2, 0, 1, 3).reshape(c, b, G * hpg * d))
     return torch.cat(outs, 0)
+
+
+# ------------------------------------------------------------------------------------------------ ring
+def _chunks_of(rank: int, cp: int) -> Tuple[int, int]:
+    """Global chunk indices held by CP rank ``rank`` (first and second half of its local sequence)."""
+    return rank, 2 * cp - 1 - rank
+
+
+def _relation(qi: int, kj: int) -> int:
+    """0: key chunk entirely after the query chunk (skipped); 1: the same chunk (causal); 2: entirely before."""
+    return 0 if kj > qi else (1 if kj == qi else 2)
+
+
+def _scores(q, k, scale, causal):
+    """q [b, G, hpg, c, d], k [b, G, c, d] -> fp32 scores [b, G, hpg, c, c] (upper triangle -inf if causal)."""
+    s = torch.einsum("bghid,bgjd->bghij", q.float(), k.float()) * scale
+    if causal:
+        c = s.shape[-1]
+        s = s.masked_fill(torch.ones(c, c, dtype=torch.bool, device=s.device).triu(1), float("-inf"))
+    return s
+
+
+class _Ring:
+    """Posts the exchange of one step's blocks with the CP neighbours (send to next, receive from previous)."""
+
+    def __init__(self, group, cp_rank: int, cp: int):
+        ranks = dist.get_process_group_ranks(group)
+        self.group, self.nxt, self.prv = group, ranks[(cp_rank + 1) % cp], ranks[(cp_rank - 1) % cp]
+
+    def start(self, send: torch.Tensor) -> Tuple[torch.Tensor, list]:
+        recv = torch.empty_like(send)
+        ops = [dist.P2POp(dist.isend, send, self.nxt, self.group), dist.P2POp(dist.irecv, recv, self.prv, self.group)]
+        return recv, dist.batch_isend_irecv(ops)
+
+    @staticmethod
+    def wait(reqs) -> None:
+        for r in reqs:
+            r.wait()
+
+
+def _split_q(qkv: torch.Tensor, hpg: int) -> List[torch.Tensor]:
+    """[s, b, G, hpg+2, d] -> the two query chunks as [b, G, hpg, c, d]."""
+    s = qkv.shape[0]
+    c = s // 2
+    return [qkv[h * c:(h + 1) * c, :, :, :hpg].permute(1, 2, 3, 0, 4) for h in range(2)]
+
+
+def _split_kv(kv: torch.Tensor) -> List[Tuple[torch.Tensor, torch.Tensor]]:
+    """[s, b, G, 2, d] -> ((k, v) of each half) as [b, G, c, d]."""
+    c = kv.shape[0] // 2
+    return [(kv[h * c:(h + 1) * c, :, :, 0].permute(1, 2, 0, 3), kv[h * c:(h + 1) * c, :, :, 1].permute(1, 2, 0, 3))
+            for h in range(2)]
+
+
+class _RingAttnFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, qkv, hpg, group, cp_rank, cp):
+        s, b, G, _, d = qkv.shape
+        c = s // 2
+        scale = 1.0 / math.sqrt(d)
+        qs = _split_q(qkv, hpg)
+        my = _chunks_of(cp_rank, cp)
+        ring = _Ring(group, cp_rank, cp)
+        kv = qkv[:, :, :, hpg:].contiguous()
+        out = [torch.zeros(b, G, hpg, c, d, dtype=torch.float32, device=qkv.device) for _ in range(2)]
+        lse = [torch.full((b, G, hpg, c), float("-inf"), dtype=torch.float32, device=qkv.device) for _ in range(2)]
+        for t in range(cp):
+            if t + 1 < cp:
+                nxt, reqs = ring.start(kv)
+            src = (cp_rank - t) % cp
+            for hk, (k, v) in enumerate(_split_kv(kv)):
+                kj = _chunks_of(src, cp)[hk]
+                for hq in range(2):
+                    rel = _relation(my[hq], kj)
+                    if rel == 0:
+                        continue
+                    sc = _scores(qs[hq], k, scale, rel == 1)
+                    l_b = torch.logsumexp(sc, -1)
+                    o_b = torch.einsum("bghij,bgjd->bghid", torch.exp(sc - l_b[..., None]), v.float())
+                    l_n = torch.logaddexp(lse[hq], l_b)
+                    out[hq] = out[hq] * torch.exp(lse[hq] - l_n)[..., None] + o_b * torch.exp(l_b - l_n)[..., None]
+                    lse[hq] = l_n
+            if t + 1 < cp:
+                _Ring.wait(reqs)
+                kv = nxt
+        ctx.save_for_backward(qkv, *out, *lse)
+        ctx.hpg, ctx.group, ctx.cp_rank, ctx.cp = hpg, group, cp_rank, cp
+        o = torch.cat([x.permute(3, 0, 1, 2, 4).reshape(c, b, G * hpg * d) for x in out], 0)
+        return o.to(qkv.dtype)
+
+    @staticmethod
+    def backward(ctx, dout):
+        qkv, o0, o1, l0, l1 = ctx.saved_tensors
+        hpg, group, cp_rank, cp = ctx.hpg, ctx.group, ctx.cp_rank, ctx.cp
+        s, b, G, _, d = qkv.shape
+        c = s // 2
+        scale = 1.0 / math.sqrt(d)
+        qs = _split_q(qkv, hpg)
+        my = _chunks_of(cp_rank, cp)
+        ring = _Ring(group, cp_rank, cp)
+        dos = [dout[h * c:(h + 1) * c].reshape(c, b, G, hpg, d).permute(1, 2, 3, 0, 4).float() for h in range(2)]
+        outs, lses = (o0, o1), (l0, l1)
+        D = [(dos[h] * outs[h]).sum(-1) for h in range(2)]  # [b, G, hpg, c]
+        dq = [torch.zeros(b, G, hpg, c, d, dtype=torch.float32, device=qkv.device) for _ in range(2)]
+        # the block in flight: K/V of rank src, and the fp32 dK/dV ([s, b, G, 2, d]) accumulated for it by the
+        # ranks it has visited, which arrives one step behind it; after CP hops the sum is back at src
+        kv = qkv[:, :, :, hpg:].contiguous()
+        incoming = None
+        for t in range(cp):
+            if t + 1 < cp:
+                nxt_kv, reqs_kv = ring.start(kv)
+            src = (cp_rank - t) % cp
+            acc = torch.zeros(kv.shape, dtype=torch.float32, device=qkv.device)
+            for hk, (k, v) in enumerate(_split_kv(kv)):
+                kj = _chunks_of(src, cp)[hk]
+                dk = acc[hk * c:(hk + 1) * c, :, :, 0].permute(1, 2, 0, 3)
+                dv = acc[hk * c:(hk + 1) * c, :, :, 1].permute(1, 2, 0, 3)
+                for hq in range(2):
+                    rel = _relation(my[hq], kj)
+                    if rel == 0:
+                        continue
+                    p = torch.exp(_scores(qs[hq], k, scale, rel == 1) - lses[hq][..., None])  # [b, G, hpg, c, c]
+                    dv += torch.einsum("bghij,bghid->bgjd", p, dos[hq])
+                    dp = torch.einsum("bghid,bgjd->bghij", dos[hq], v.float())
+                    ds = p * (dp - D[hq][..., None]) * scale
+                    dq[hq] += torch.einsum("bghij,bgjd->bghid", ds, k.float())
+                    dk += torch.einsum("bghij,bghid->bgjd", ds, qs[hq].float())
+            if incoming is not None:
+                _Ring.wait(incoming[1])
+                acc += incoming[0]
+            incoming = ring.start(acc)
+            if t + 1 < cp:
+                _Ring.wait(reqs_kv)
+                kv = nxt_kv
+        _Ring.wait(incoming[1])
+        dkv = incoming[0]
+        dqkv = torch.empty_like(qkv)
+        for h in range(2):
+            dqkv[h * c:(h + 1) * c, :, :, :hpg] = dq[h].permute(3, 0, 1, 2, 4).to(qkv.dtype)
+        dqkv[:, :, :, hpg:] = dkv.to(qkv.dtype)
+        return dqkv, None, None, None, None
+
+
+def cp_ring_attention(qkv: torch.Tensor, hpg: int, group, cp_rank: int, cp: int) -> torch.Tensor:
+    """Causal attention of this rank's two query chunks with K/V passed round the CP ring.
+
+    Same inputs and output as :func:`cp_attention` (``qkv`` [s, b, G, hpg+2, d] after RoPE, out
+    [s, b, G*hpg*d]).  Scores, softmax statistics and accumulators are fp32 whatever the input dtype; the
+    math is plain tensor algebra, so the same code runs on the host and on the device."""
+    return _RingAttnFn.apply(qkv, hpg, group, cp_rank, cp)

@@ -46,6 +46,8 @@ def parse_args(argv=None):
     ap.add_argument("--lr-warmup-iters", type=int, default=2)
     ap.add_argument("--engine", default=None, choices=[None, "native", "torch", "reference"])
     ap.add_argument("--overlap-grad-reduce", action="store_true")
+    ap.add_argument("--cp-comm-type", default="all_gather", choices=["all_gather", "p2p"],
+                    help="context parallelism: gather K/V over the CP group, or pass it round a ring")
     ap.add_argument("--save", default=None, help="checkpoint directory written at the end")
     ap.add_argument("--save-around-reshard", action="store_true",
                     help="write before_reshard/ and after_reshard/ checkpoints at every switch (for compare_ckpt)")
@@ -102,7 +104,8 @@ def main(argv=None):
     set_args(Args(model=cfg, train=TrainConfig(micro_batch_size=a.micro_batch_size,
                                                global_batch_size=a.global_batch_size, lr=a.lr, min_lr=a.min_lr,
                                                lr_warmup_iters=a.lr_warmup_iters, train_iters=a.train_iters,
-                                               overlap_grad_reduce=a.overlap_grad_reduce)))
+                                               overlap_grad_reduce=a.overlap_grad_reduce,
+                                               cp_comm_type=a.cp_comm_type)))
     specs = a.strategies.split(",") if a.strategies else default_schedule(world)
     strategies = [ParallelStrategy.parse(s) for s in specs]
     uniq = list(dict.fromkeys(strategies))

@@ -8,7 +8,7 @@ CP = [dict(world_size=2, tensor_model_parallel_size=1, pipeline_model_parallel_s
       dict(world_size=2, tensor_model_parallel_size=1, pipeline_model_parallel_size=1, context_parallel_size=2)]
 
 
-def _run(rank, world, schedule, gqa):
+def _run(rank, world, schedule, gqa, cp_comm_type="all_gather"):
     from elasticmegatron_b200.config import Args, ModelConfig, TrainConfig, set_args
     from elasticmegatron_b200.parallel.process_groups import create_all_groups
     from elasticmegatron_b200.parallel.strategy import ParallelStrategy
@@ -19,7 +19,8 @@ def _run(rank, world, schedule, gqa):
     cfg = ModelConfig(num_layers=2, hidden_size=64, num_attention_heads=4, num_query_groups=2 if gqa else 4,
                       ffn_hidden_size=128, vocab_size=500, seq_length=32, params_dtype="fp32",
                       max_tensor_parallel_size=2, make_vocab_size_divisible_by=8)
-    set_args(Args(model=cfg, train=TrainConfig(micro_batch_size=2, global_batch_size=8, lr=1e-3)))
+    set_args(Args(model=cfg, train=TrainConfig(micro_batch_size=2, global_batch_size=8, lr=1e-3,
+                                               cp_comm_type=cp_comm_type)))
     S = [ParallelStrategy(**s) for s in CP]
     create_all_groups(S)
     ts = TrainingState(S[schedule[0]])
@@ -85,3 +86,52 @@ def test_cp_combined_with_tp_and_pp_switches():
     base = run_distributed(_run4, 4, [0, 0, 0, 0])[0]
     sw = run_distributed(_run4, 4, [0, 1, 2, 0])[0]
     np.testing.assert_allclose(base, sw, rtol=1e-5)
+
+
+def _ring_vs_gather(rank, world, gqa):
+    import torch
+    import torch.distributed as dist
+
+    from elasticmegatron_b200.parallel.context_parallel import cp_attention, cp_ring_attention
+
+    G, hpg, d, b, s = (2, 2, 16, 2, 12) if gqa else (4, 1, 16, 2, 12)
+    gen = torch.Generator().manual_seed(7)
+    # one global sequence; rank r holds global chunks r and 2*CP-1-r
+    full = torch.randn(2 * world * (s // 2), b, G, hpg + 2, d, generator=gen, dtype=torch.float64)
+    dfull = torch.randn(2 * world * (s // 2), b, G * hpg * d, generator=gen, dtype=torch.float64)
+    c = s // 2
+    idx = torch.cat([torch.arange(rank * c, (rank + 1) * c),
+                     torch.arange((2 * world - 1 - rank) * c, (2 * world - rank) * c)])
+    mine, dmine = full[idx].float(), dfull[idx].float()
+    out = {}
+    res = []
+    for fn in (cp_attention, cp_ring_attention):
+        x = mine.clone().requires_grad_()
+        y = fn(x, hpg, dist.group.WORLD, rank, world)
+        y.backward(dmine)
+        res.append((y.detach(), x.grad))
+    out["fwd"] = (res[0][0] - res[1][0]).abs().max().item()
+    out["bwd"] = (res[0][1] - res[1][1]).abs().max().item()
+    # the whole-sequence oracle on every rank: plain causal attention of the global sequence
+    q = full[:, :, :, :hpg].permute(1, 2, 3, 0, 4)
+    k, v = full[:, :, :, hpg].permute(1, 2, 0, 3), full[:, :, :, hpg + 1].permute(1, 2, 0, 3)
+    sc = torch.einsum("bghid,bgjd->bghij", q, k) / d ** 0.5
+    n = sc.shape[-1]
+    sc = sc.masked_fill(torch.ones(n, n, dtype=torch.bool).triu(1), float("-inf"))
+    o = torch.einsum("bghij,bgjd->bghid", sc.softmax(-1), v).permute(3, 0, 1, 2, 4).reshape(n, b, -1)
+    out["oracle"] = (o[idx].float() - res[1][0]).abs().max().item()
+    return out
+
+
+def test_ring_attention_matches_all_gather():
+    """cp_comm_type p2p (ring) against all_gather and against causal attention of the unsplit sequence."""
+    for world in (2, 4):
+        for gqa in (False, True):
+            for r in run_distributed(_ring_vs_gather, world, gqa):
+                assert r["fwd"] < 1e-5 and r["bwd"] < 1e-5 and r["oracle"] < 1e-5, (world, gqa, r)
+
+
+def test_cp2_ring_equals_dp2():
+    dp = run_distributed(_run, 2, [0, 0, 0], True)[0]
+    ring = run_distributed(_run, 2, [1, 1, 1], True, "p2p")[0]
+    np.testing.assert_allclose(dp, ring, rtol=1e-5)
