@@ -236,6 +236,10 @@ class ElasticMegatronManager:
         set_world_group(ProcessGroupPool.get(dst_s.ranks))
         if dst is not None and not is_meta_device:
             dst.ddp.zero_grad()
+            if dst.pool.guard:
+                from .memory import check_guards
+
+                check_guards(f"reshard {src_s} -> {dst_s}")
         mx = max_over_ranks([ms, nbytes / 1e9], group=ProcessGroupPool.get(union, "gloo")
                             if dist.is_initialized() else None)
         roof = plan.nvlink_roofline_ms(NVLINK_GBS, 4, torch.finfo(get_args().model.torch_dtype).bits // 8)

@@ -10,12 +10,26 @@ On CUDA the arenas are ``cudaMalloc`` allocations made by the native extension (
 so each can be exported as one CUDA IPC handle and mapped by peer processes for the direct-transfer engine;
 peer mappings are cached by the engine, and because the pool reuses arenas across switches the mappings
 stay valid.
+
+Guard words (``EMB_ARENA_GUARD=1``): every arena gets ``GUARD_BYTES`` past its requested size filled with
+``GUARD_FILL``; :func:`check_guards` (run by the manager after each switch and by ``train_step`` after each
+step while enabled) raises if any live arena's tail changed, i.e. a transfer task or a kernel wrote past the
+end of the state it was given.  This stands in for a sanitizer's out-of-bounds check on state arenas.
 """
 from __future__ import annotations
 
+import os
+import weakref
 from typing import Dict, List, Optional
 
 import torch
+
+GUARD_BYTES = 4096
+GUARD_FILL = 0xA5
+
+
+def guard_enabled() -> bool:
+    return os.environ.get("EMB_ARENA_GUARD", "0") not in ("", "0")
 
 _ELEM = {torch.float32: 4, torch.bfloat16: 2, torch.float16: 2, torch.uint8: 1, torch.int64: 8}
 
@@ -27,6 +41,8 @@ class Arena:
 
     def __init__(self, raw: torch.Tensor, nbytes: int, native: bool):
         self.raw, self.nbytes, self.native = raw, nbytes, native
+        self.used = nbytes  # bytes requested by the current owner (views never extend past it)
+        self.guard = 0  # guard bytes armed right after ``used``
         self.id = Arena._next_id
         Arena._next_id += 1
         self._ipc = None
@@ -35,8 +51,17 @@ class Arena:
         n = 1
         for s in shape:
             n *= s
-        assert n * _ELEM[dtype] <= self.nbytes, (shape, dtype, self.nbytes)
+        assert n * _ELEM[dtype] <= self.used, (shape, dtype, self.used)
         return self.raw[: n * _ELEM[dtype]].view(dtype).view(shape)
+
+    def arm_guard(self, nbytes: int) -> None:
+        self.guard = nbytes
+        self.raw[self.used:self.used + nbytes].fill_(GUARD_FILL)
+
+    def guard_intact(self) -> bool:
+        if not self.guard:
+            return True
+        return bool((self.raw[self.used:self.used + self.guard] == GUARD_FILL).all().item())
 
     @property
     def ptr(self) -> int:
@@ -71,6 +96,8 @@ class ArenaPool:
                 total = torch.cuda.get_device_properties(self.device).total_memory
             max_cached_bytes = int(0.4 * total) if total else (1 << 62)
         self.max_cached_bytes = max_cached_bytes
+        self.guard = GUARD_BYTES if guard_enabled() else 0
+        self._live: "weakref.WeakSet[Arena]" = weakref.WeakSet()
 
     @staticmethod
     def _round(nbytes: int) -> int:
@@ -90,7 +117,8 @@ class ArenaPool:
         return Arena(torch.empty(nbytes, dtype=torch.uint8, device=self.device), nbytes, False)
 
     def alloc(self, nbytes: int, zero: bool = False) -> Arena:
-        nbytes = self._round(nbytes)
+        used = nbytes
+        nbytes = self._round(used + self.guard)
         fits = [a for a in self._free if nbytes <= a.nbytes <= self.slack * nbytes]
         if fits:
             a = min(fits, key=lambda x: x.nbytes)
@@ -102,13 +130,18 @@ class ArenaPool:
                 self.trim()
                 a = self._new(nbytes)
             self.allocated_bytes += nbytes
+        a.used = used
         if zero:
             a.raw.zero_()
+        if self.guard:
+            a.arm_guard(self.guard)
+        self._live.add(a)
         return a
 
     def free(self, a: Optional[Arena]) -> None:
         if a is None:
             return
+        self._live.discard(a)
         self._free.append(a)
         while self.cached_bytes() > self.max_cached_bytes and self._free:
             old = self._free.pop(0)
@@ -132,3 +165,14 @@ def get_pool(device) -> ArenaPool:
     if key not in _POOLS:
         _POOLS[key] = ArenaPool(torch.device(device))
     return _POOLS[key]
+
+
+def check_guards(where: str = "") -> None:
+    """Raise if a guard word of any live arena of any pool was overwritten (no-op unless guards are armed)."""
+    bad = []
+    for key, pool in _POOLS.items():
+        for a in list(pool._live):
+            if not a.guard_intact():
+                bad.append(f"arena {a.id} on {key} ({a.used} bytes used)")
+    if bad:
+        raise RuntimeError(f"state arena guard words overwritten{' after ' + where if where else ''}: " + "; ".join(bad))

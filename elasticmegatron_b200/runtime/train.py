@@ -59,6 +59,10 @@ def train_step(ts, data_iter: Iterator, hetero_dp: Optional[bool] = None, return
     out = {"grad_norm": gnorm, "num_microbatches": n_mb, "update_successful": ok}
     if return_loss:
         out["loss"] = reduce_loss(ts, loss_sums)
+    if ts.pool.guard:
+        from .memory import check_guards
+
+        check_guards("train_step")
     return out
 
 
