@@ -28,6 +28,7 @@ import torch.distributed as dist
 from ..ops.native import ext
 from ..parallel.process_groups import ProcessGroupPool
 from ..planner.plan import KIND_OPT, ReshardPlan
+from . import validate
 
 TASK_DTYPE = np.dtype([
     ("src", np.uint64), ("dst", np.uint64), ("src_stride", np.uint64), ("dst_stride", np.uint64),
@@ -192,6 +193,8 @@ class NativeP2PEngine:
         ref = next(x for x in (dp, sp) if x is not None)
         el_param = ref.element_size()
         tasks = self._tasks(plan, rank, addrs, el_param)
+        if validate.enabled():
+            validate.validate_tasks(tasks, *validate.plan_regions(plan, addrs, el_param))
         dev = next(x for x in (dp, do, sp, so) if x is not None).device
         buf = torch.from_numpy(tasks.view(np.uint8).copy()).to(dev) if len(tasks) else torch.zeros(64, dtype=torch.uint8,
                                                                                                     device=dev)
