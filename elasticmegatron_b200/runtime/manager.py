@@ -26,6 +26,7 @@ import os
 import logging
 from typing import Callable, Dict, List, Optional, Union
 
+import numpy as np
 import torch
 import torch.distributed as dist
 
@@ -39,7 +40,7 @@ from ..utils.timers import DeviceTimer, HostTimer, max_over_ranks, nvtx_range
 from .data import DataloaderState
 from .training_state import TrainingState
 
-NVLINK_GBS = 770.0  # measured per-direction peer copy bandwidth on this pool's B200s
+NVLINK_GBS = 770.0  # measured per-direction peer copy bandwidth between two B200s over NVLink 5
 
 
 def default_setup_model_and_optimizer(strategy: ParallelStrategy, is_meta_device: bool = False) -> TrainingState:
@@ -209,11 +210,12 @@ class ElasticMegatronManager:
             return None
         ugroup = ProcessGroupPool.get(union)
         same_layout = src_s.layout_key() == dst_s.layout_key()
+        t_total = HostTimer(sync=False).__enter__()
         with HostTimer(sync=False) as t_build, nvtx_range("reshard/build"):
             dst = self._get_or_build(dst_s, is_meta_device)
         if src is not None and src.model_released:
             src.rebuild()
-        with nvtx_range("reshard/plan"):
+        with HostTimer(sync=False) as t_plan, nvtx_range("reshard/plan"):
             plan = self.plan(src_s, dst_s)
         if self._rank == 0 and os.environ.get("EMB_RESHARD_DEBUG", "0") != "0":
             # per-parameter send / receive plan (the reference's debug print, transfer/transfer.py:271-289)
@@ -227,11 +229,12 @@ class ElasticMegatronManager:
         else:
             with nvtx_range("reshard/transfer"):
                 ms, nbytes = self._transfer(plan, src, dst, ugroup, same_layout)
-        with nvtx_range("reshard/lr"):
+        with HostTimer(sync=False) as t_lr, nvtx_range("reshard/lr"):
             self._transfer_lr(src, dst, union)
-        if src is not None and src is not dst:
-            with nvtx_range("reshard/release"):
-                src.release()
+        with HostTimer(sync=False) as t_rel:
+            if src is not None and src is not dst:
+                with nvtx_range("reshard/release"):
+                    src.release()
         self.current = dst_s
         set_world_group(ProcessGroupPool.get(dst_s.ranks))
         if dst is not None and not is_meta_device:
@@ -240,15 +243,26 @@ class ElasticMegatronManager:
                 from .memory import check_guards
 
                 check_guards(f"reshard {src_s} -> {dst_s}")
-        mx = max_over_ranks([ms, nbytes / 1e9], group=ProcessGroupPool.get(union, "gloo")
+        t_total.__exit__(None, None, None)
+        # every phase's time is the MAX over the union ranks (the transfer's is device time)
+        mx = max_over_ranks([ms, nbytes / 1e9, t_build.elapsed, t_plan.elapsed, t_lr.elapsed, t_rel.elapsed,
+                             t_total.elapsed], group=ProcessGroupPool.get(union, "gloo")
                             if dist.is_initialized() else None)
-        roof = plan.nvlink_roofline_ms(NVLINK_GBS, 4, torch.finfo(get_args().model.torch_dtype).bits // 8)
+        el_param = torch.finfo(get_args().model.torch_dtype).bits // 8
+        roof = plan.nvlink_roofline_ms(NVLINK_GBS, 4, el_param)
+        links = plan.bytes_matrix(4, el_param)
+        np.fill_diagonal(links, 0)
         self.last_switch = {"src": str(src_s), "dst": str(dst_s), "engine": self.engine_name,
                             "transfer_ms": mx[0], "gbytes": mx[1],
                             "bandwidth_gbs": (mx[1] / (mx[0] / 1e3)) if mx[0] > 0 else None,
                             "nvlink_roofline_ms": roof,
                             "roofline_frac": (roof / mx[0]) if mx[0] > 0 else None,
-                            "build_ms": t_build.elapsed}
+                            "build_ms": mx[2], "plan_ms": mx[3], "lr_ms": mx[4], "release_ms": mx[5],
+                            "total_ms": mx[6],
+                            # bytes that cross links, per direction: [sender][receiver] in GB, and the busiest GPU
+                            "link_gb": (links / 1e9).round(4).tolist(),
+                            "max_egress_gb": float(links.sum(1).max(initial=0)) / 1e9,
+                            "max_ingress_gb": float(links.sum(0).max(initial=0)) / 1e9}
         if self._rank == 0 or logger is not None:
             log_json("reshard", logger, **self.last_switch)
         if save_ckpt and dst is not None:

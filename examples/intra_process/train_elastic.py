@@ -88,6 +88,7 @@ def main(argv=None):
     from elasticmegatron_b200.parallel.strategy import ParallelStrategy
     from elasticmegatron_b200.runtime.train import train_step
     from elasticmegatron_b200.runtime.training_state import TrainingState
+    from elasticmegatron_b200.utils.logging import log_json
 
     over = {"max_tensor_parallel_size": 8}
     if a.layers:
@@ -144,6 +145,9 @@ def main(argv=None):
                   f" | elapsed time per iteration (ms): {ms:.1f} | learning rate: {lr:.6E}"
                   f" | global batch size: {a.global_batch_size:5d} | lm loss: {out['loss']:.6E}"
                   f" | grad norm: {float(out['grad_norm']):.3f} | strategy: {mgr.current}", flush=True)
+            tokens = a.global_batch_size * cfg.seq_length
+            log_json("iteration", None, iteration=iteration, loss=out["loss"], ms=ms,
+                     tokens_per_s_per_gpu=tokens / (ms / 1e3) / mgr.current.world_size, strategy=str(mgr.current))
     if a.save and ts is not None:
         from elasticmegatron_b200.runtime.checkpoint import save_checkpoint
 

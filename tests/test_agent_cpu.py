@@ -1,4 +1,5 @@
 """Inter-process agent pieces and the two example programs, on CPU (gloo ranks, torchrun subprocesses)."""
+import json
 import os
 import re
 import subprocess
@@ -92,6 +93,18 @@ def test_examples_handoff_matches_intra_process_switch(tmp_path):
     for i in range(1, 7):
         assert abs(a[i] - b[i]) <= 1e-5 * abs(a[i]), (i, a[i], b[i])
     assert "successor exit code 0" in inter
+    # structured lines: one per iteration (tokens/s/GPU, strategy) and one per switch (phases, link bytes)
+    recs = [json.loads(ln) for ln in intra.splitlines() if ln.startswith('{"event"')]
+    its = [r for r in recs if r["event"] == "iteration"]
+    assert [r["iteration"] for r in its] == list(range(1, 7))
+    assert [r["strategy"].split("-")[0] for r in its] == ["ws2"] * 3 + ["ws1"] * 3
+    assert all(r["tokens_per_s_per_gpu"] > 0 for r in its)
+    sw = [r for r in recs if r["event"] == "reshard"]
+    assert len(sw) == 1 and (sw[0]["src"].split("-")[0], sw[0]["dst"].split("-")[0]) == ("ws2", "ws1")
+    for k in ("build_ms", "plan_ms", "transfer_ms", "lr_ms", "release_ms", "total_ms"):
+        assert sw[0][k] >= 0, k
+    assert sw[0]["total_ms"] >= sw[0]["transfer_ms"]
+    assert len(sw[0]["link_gb"]) == 2 and sw[0]["link_gb"][0][0] == 0 and sw[0]["max_egress_gb"] > 0
 
 
 def test_handoff_chain_scale_down_and_up(tmp_path):
