@@ -57,9 +57,9 @@ class RankGenerator:
         named = token.lower().split("-")
         for ax in named:
             assert ax in self.sizes, f"unknown axis {ax}"
+        # the named axes are enumerated in mesh order (first mesh axis fastest) whatever order the token spells
+        # them in, as Megatron does
         masked = [ax for ax in self.order if ax in named]
-        # named axes are enumerated in the order given by the token? Megatron enumerates the masked axes in
-        # mesh order (first mesh axis fastest), independent of how the token spells them.
         unmasked = [ax for ax in self.order if ax not in named]
         groups = []
         # outer loop over un-named axes with the first one fastest

@@ -97,3 +97,64 @@ def test_parse_round_trip():
         P.parse("tp2")
     with pytest.raises(ValueError):
         P.parse("ws4-xx2")
+
+
+def _divisors(n):
+    return [d for d in range(1, n + 1) if n % d == 0]
+
+
+def _oracle_groups(sizes, order, token):
+    """Megatron's documented mesh: rank = sum(coord * stride) with the first axis of ``order`` fastest; a group
+    of ``token`` is every rank that shares the coordinates of the axes the token does not name.  Ranks inside a
+    group and groups (by their lowest rank) come in ascending order."""
+    named = set(token.split("-"))
+    world = 1
+    for ax in order:
+        world *= sizes[ax]
+    groups = {}
+    for r in range(world):
+        rest, key = r, []
+        for ax in order:
+            rest, c = divmod(rest, sizes[ax])
+            if ax not in named:
+                key.append((ax, c))
+        groups.setdefault(tuple(key), []).append(r)
+    return sorted(groups.values())
+
+
+def _tokens(axes):
+    from itertools import combinations
+
+    return ["-".join(c) for k in range(1, len(axes) + 1) for c in combinations(axes, k)]
+
+
+def test_rank_meshes_all_factorizations_of_1_2_4_8():
+    """Dense (tp-cp-dp-pp) and expert (etp-ep-edp-pp) meshes of every strategy on 1, 2, 4 and 8 GPUs, every
+    group token, against the oracle above."""
+    order = ["tp", "cp", "ep", "dp", "pp"]
+    n = 0
+    for ws in (1, 2, 4, 8):
+        for tp in _divisors(ws):
+            for cp in _divisors(ws // tp):
+                for pp in _divisors(ws // (tp * cp)):
+                    dp = ws // (tp * cp * pp)
+                    s = ParallelStrategy(world_size=ws, tensor_model_parallel_size=tp, pipeline_model_parallel_size=pp,
+                                         context_parallel_size=cp, expert_tensor_parallel_size=1,
+                                         sequence_parallel=tp > 1,
+                                         expert_model_parallel_size=max(e for e in _divisors(ws // pp) if 8 % e == 0))
+                    dense = dict(tp=tp, cp=cp, ep=1, dp=dp, pp=pp)
+                    for tok in _tokens(["tp", "cp", "dp", "pp"]):
+                        assert s.all_groups(tok) == _oracle_groups(dense, order, tok), (ws, tp, cp, pp, tok)
+                        n += 1
+                    ep = s.expert_model_parallel_size
+                    expert = dict(tp=1, cp=1, ep=ep, dp=ws // (ep * pp), pp=pp)
+                    for tok in _tokens(["tp", "ep", "dp", "pp"]):
+                        assert s.all_groups(tok, True) == _oracle_groups(expert, order, tok), (ws, ep, pp, tok)
+                    # the expert mesh with ETP > 1 (no MoE resharding support, but the mesh itself)
+                    for etp in _divisors(ws // pp):
+                        for ep2 in _divisors(ws // (pp * etp)):
+                            sizes = dict(tp=etp, cp=1, ep=ep2, dp=ws // (etp * ep2 * pp), pp=pp)
+                            g = RankGenerator(tp=etp, ep=ep2, dp=sizes["dp"], pp=pp, cp=1)
+                            for tok in ("tp", "ep", "dp", "pp", "tp-ep", "ep-dp", "tp-ep-pp"):
+                                assert g.get_ranks(tok) == _oracle_groups(sizes, order, tok), (ws, etp, ep2, pp, tok)
+    assert n > 300
