@@ -8,7 +8,8 @@
   global batch is the same under every DP size (data continuity across switches; reference
   dataloader_state.py:127-157 resumes from ``consumed_train_samples`` the same way).
 * :func:`num_microbatches` - ``GBS / (MBS * DP)``, reconfigured on every switch; hetero-DP gives the
-  remainder to the lowest DP ranks (elastic_megatron/hetero_dp.py:126-188).
+  remainder, in units of ``alignment`` micro-batches, to the lowest DP ranks
+  (elastic_megatron/hetero_dp.py:126-188).
 * The iterator yields micro-batches in **pinned host memory**; the train step copies each to the device
   with ``non_blocking=True`` (the end-to-end path).
 """
@@ -32,7 +33,7 @@ class MockGPTDataset:
 
 
 def num_microbatches(global_batch_size: int, micro_batch_size: int, dp: int, dp_rank: int = 0,
-                     hetero: bool = False) -> int:
+                     hetero: bool = False, alignment: int = 1) -> int:
     per = micro_batch_size * dp
     if global_batch_size % per == 0:
         return global_batch_size // per
@@ -40,19 +41,25 @@ def num_microbatches(global_batch_size: int, micro_batch_size: int, dp: int, dp_
         raise ValueError(f"global batch {global_batch_size} not divisible by micro batch {micro_batch_size} x DP {dp}"
                          " (enable hetero-DP)")
     total_mb = global_batch_size // micro_batch_size
-    assert total_mb * micro_batch_size == global_batch_size, "GBS must divide by MBS"
-    base, extra = divmod(total_mb, dp)
-    return base + (1 if dp_rank < extra else 0)
+    if total_mb * micro_batch_size != global_batch_size or total_mb % alignment:
+        raise ValueError(f"global batch {global_batch_size} must divide by micro batch {micro_batch_size} x "
+                         f"alignment {alignment}")
+    units = total_mb // alignment
+    if units < dp:
+        raise ValueError(f"{units} units of {alignment} micro-batches cannot feed {dp} DP ranks")
+    base, extra = divmod(units, dp)
+    return (base + (1 if dp_rank < extra else 0)) * alignment
 
 
 class PretrainingSampler:
     """Sample indices for one DP rank, micro-batch by micro-batch, from ``consumed_samples`` on."""
 
     def __init__(self, total_samples: int, consumed_samples: int, micro_batch_size: int, dp_rank: int,
-                 dp_size: int, global_batch_size: Optional[int] = None):
+                 dp_size: int, global_batch_size: Optional[int] = None, alignment: int = 1):
         self.total, self.consumed = total_samples, consumed_samples
         self.mbs, self.r, self.dp = micro_batch_size, dp_rank, dp_size
         self.gbs = global_batch_size
+        self.alignment = alignment
 
     def __iter__(self) -> Iterator[List[int]]:
         i = self.consumed
@@ -62,10 +69,11 @@ class PretrainingSampler:
                 yield [(s + j) % self.total for j in range(self.mbs)]
                 i += self.mbs * self.dp
             else:
-                # hetero-DP: micro-batches of one global batch are dealt round-robin over DP ranks
+                # hetero-DP: units of ``alignment`` micro-batches of one global batch are dealt round-robin
+                # over DP ranks
                 n_mb = self.gbs // self.mbs
                 for m in range(n_mb):
-                    if m % self.dp == self.r:
+                    if (m // self.alignment) % self.dp == self.r:
                         s = i + m * self.mbs
                         yield [(s + j) % self.total for j in range(self.mbs)]
                 i += self.gbs
@@ -127,6 +135,8 @@ class DataloaderState:
         pos = None
         if s.context_parallel_size > 1:
             pos = cp_positions(ts.cfg.seq_length, s.context_parallel_size, ps.cp_rank)
+        from .hetero_dp import hetero_alignment
+
         sampler = PretrainingSampler(len(train_ds), consumed_samples, ts.train_cfg.micro_batch_size, ps.dp_rank,
-                                     ps.dp_size, ts.train_cfg.global_batch_size)
+                                     ps.dp_size, ts.train_cfg.global_batch_size, hetero_alignment())
         return DataIterator(train_ds, sampler, pos), None, None

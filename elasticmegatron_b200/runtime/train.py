@@ -28,11 +28,12 @@ def _act_shape(ts) -> tuple:
 def train_step(ts, data_iter: Iterator, hetero_dp: Optional[bool] = None, return_loss: bool = True) -> Dict:
     ps, tc, cfg = ts.ps, ts.train_cfg, ts.cfg
     s = ts.strategy
-    if hetero_dp is None:
-        from .hetero_dp import hetero_dp_enabled
+    from .hetero_dp import hetero_alignment, hetero_dp_enabled, process_outputs
 
+    if hetero_dp is None:
         hetero_dp = hetero_dp_enabled()
-    n_mb = num_microbatches(tc.global_batch_size, tc.micro_batch_size, s.data_parallel_size, ps.dp_rank, hetero_dp)
+    n_mb = num_microbatches(tc.global_batch_size, tc.micro_batch_size, s.data_parallel_size, ps.dp_rank, hetero_dp,
+                            hetero_alignment() if hetero_dp else 1)
     dev = ts.device
     needs_data = ps.is_first_stage or ps.is_last_stage
     host = [next(data_iter) for _ in range(n_mb)] if needs_data else [(None, None)] * n_mb
@@ -58,6 +59,8 @@ def train_step(ts, data_iter: Iterator, hetero_dp: Optional[bool] = None, return
                                 else tc.global_batch_size)
     out = {"grad_norm": gnorm, "num_microbatches": n_mb, "update_successful": ok}
     if return_loss:
+        if hetero_dp and ps.is_last_stage and loss_sums:
+            loss_sums = process_outputs(loss_sums)
         out["loss"] = reduce_loss(ts, loss_sums)
     if ts.pool.guard:
         from .memory import check_guards

@@ -221,7 +221,7 @@ def test_checkpoint_save_a_load_b_equals_live_reshard(tmp_path):
             assert a.keys() == b.keys() and all(torch.equal(a[k], b[k]) for k in a)
 
 
-def _hetero(rank, world, strat_idx):
+def _hetero(rank, world, strat_idx, alignment=1, gbs=6, mbs=2, hook=False):
     from elasticmegatron_b200.config import Args, ModelConfig, TrainConfig, set_args
     from elasticmegatron_b200 import apply_hetero_dp
     from elasticmegatron_b200.parallel.process_groups import create_all_groups
@@ -233,12 +233,13 @@ def _hetero(rank, world, strat_idx):
     cfg = ModelConfig(num_layers=2, hidden_size=64, num_attention_heads=4, ffn_hidden_size=128, vocab_size=500,
                       seq_length=32, params_dtype="fp32", max_tensor_parallel_size=2, make_vocab_size_divisible_by=8)
     # 3 micro-batches of 2 per global batch: DP2 splits them 2 + 1
-    set_args(Args(model=cfg, train=TrainConfig(micro_batch_size=2, global_batch_size=6, lr=1e-3, train_iters=20)))
-    apply_hetero_dp(True)
+    set_args(Args(model=cfg, train=TrainConfig(micro_batch_size=mbs, global_batch_size=gbs, lr=1e-3, train_iters=20)))
+    apply_hetero_dp(_double if hook else None, alignment=alignment)
     S = [ParallelStrategy(world_size=2, tensor_model_parallel_size=1, pipeline_model_parallel_size=1),
          ParallelStrategy(world_size=1, tensor_model_parallel_size=1, pipeline_model_parallel_size=1)]
-    if world == 4:  # DP2 x PP2: each pipeline runs 1F1B over its own number of micro-batches
+    if world == 4:  # DP2 x PP2: each pipeline runs 1F1B over its own number of micro-batches; DP4
         S.append(ParallelStrategy(world_size=4, tensor_model_parallel_size=1, pipeline_model_parallel_size=2))
+        S.append(ParallelStrategy(world_size=4, tensor_model_parallel_size=1, pipeline_model_parallel_size=1))
     create_all_groups(S)
     s = S[strat_idx]
     if rank >= s.world_size:
@@ -253,6 +254,49 @@ def test_hetero_dp_matches_single_rank():
     dp2 = run_distributed(_hetero, 2, 0)
     one = run_distributed(_hetero, 2, 1)
     np.testing.assert_allclose(dp2[0], one[0], rtol=2e-6)
+
+
+def _double(outputs):
+    return [2 * o for o in outputs]
+
+
+def test_hetero_microbatch_counts_and_sampler_with_alignment():
+    import pytest
+
+    from elasticmegatron_b200.runtime.data import PretrainingSampler, num_microbatches
+
+    for gbs, mbs, dp, al in [(10, 1, 4, 2), (36, 2, 5, 3), (6, 2, 2, 1), (30, 1, 8, 3), (7, 1, 3, 1)]:
+        counts = [num_microbatches(gbs, mbs, dp, r, True, al) for r in range(dp)]
+        assert sum(counts) * mbs == gbs and all(c % al == 0 and c > 0 for c in counts), (gbs, mbs, dp, al, counts)
+        assert counts == sorted(counts, reverse=True)
+        # the DP ranks' samplers together draw exactly the samples of each global batch, once
+        for consumed in (0, gbs * 3):
+            drawn = []
+            for r in range(dp):
+                it = iter(PretrainingSampler(10 ** 6, consumed, mbs, r, dp, gbs, al))
+                for _ in range(counts[r]):
+                    drawn += next(it)
+            assert sorted(drawn) == list(range(consumed, consumed + gbs)), (gbs, mbs, dp, al)
+    with pytest.raises(ValueError):
+        num_microbatches(10, 1, 4, 0, True, 3)  # 10 micro-batches are not units of 3
+    with pytest.raises(ValueError):
+        num_microbatches(6, 1, 4, 0, True, 2)  # 3 units for 4 ranks
+    from elasticmegatron_b200 import apply_hetero_dp
+
+    with pytest.raises(TypeError):
+        apply_hetero_dp(True)
+    apply_hetero_dp(enabled=False)
+
+
+def test_hetero_dp_alignment_and_output_hook():
+    """DP4 over 10 micro-batches of 1 in units of 2 (4 + 2 + 2 + 2) equals one rank; a hook that doubles the
+    per-micro-batch outputs doubles the reported loss and nothing else."""
+    one = run_distributed(_hetero, 2, 1, 2, 10, 1)
+    dp4 = run_distributed(_hetero, 4, 3, 2, 10, 1)
+    np.testing.assert_allclose(dp4[0], one[0], rtol=2e-6)
+    hooked = run_distributed(_hetero, 2, 0, 1, 6, 2, True)
+    plain = run_distributed(_hetero, 2, 0, 1, 6, 2)
+    np.testing.assert_allclose(hooked[0], [2 * x for x in plain[0]], rtol=1e-6)
 
 
 def test_hetero_dp_with_pipeline():
