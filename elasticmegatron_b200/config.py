@@ -114,7 +114,8 @@ class TrainConfig:
     grad_reduce_in_fp32: bool = True
     # memory
     recompute: bool = False
-    # context parallelism: "all_gather" (K/V gathered over the CP group) or "p2p" (K/V passed round a ring)
+    # context parallelism: "all_gather" (K/V gathered over the CP group), "p2p" (K/V passed round a ring) or
+    # "a2a" (Ulysses: all-to-all from a sequence split to a query-group split and back)
     cp_comm_type: str = "all_gather"
 
 

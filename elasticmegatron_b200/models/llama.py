@@ -26,7 +26,7 @@ from ..ops import functional as F_
 from ..ops import reference as ref
 from ..models.spec import LocalParam
 from .moe import MoELayer
-from ..parallel.context_parallel import CP_COMM_TYPES, cp_attention, cp_ring_attention
+from ..parallel.context_parallel import CP_COMM_TYPES, cp_attention, cp_ring_attention, cp_ulysses_attention
 
 
 class RotaryCache:
@@ -71,7 +71,11 @@ class GPTStage(nn.Module):
         self.mbs = micro_batch_size
         self.tp_group = pstate.group("tp") if self.tp > 1 else None
         self.cp_group = pstate.group("cp") if self.cp > 1 else None
-        self.cp_attention = cp_ring_attention if cp_comm_type == "p2p" else cp_attention
+        self.cp_attention = {"all_gather": cp_attention, "p2p": cp_ring_attention,
+                             "a2a": cp_ulysses_attention}[cp_comm_type]
+        if self.cp > 1 and cp_comm_type == "a2a" and (cfg.num_query_groups // self.tp) % self.cp:
+            raise ValueError(f"cp_comm_type a2a needs the query groups per TP rank "
+                             f"({cfg.num_query_groups // self.tp}) divisible by CP ({self.cp})")
         self.params_by_name: Dict[str, nn.Parameter] = {}
         for lp in params:
             p = nn.Parameter(views[lp.name], requires_grad=True)

@@ -1,6 +1,6 @@
 """Context parallelism: attention over a sequence split into 2*CP load-balanced chunks.
 
-CP rank ``r`` holds chunks ``r`` and ``2*CP-1-r`` (so every rank does the same amount of causal work).  Two
+CP rank ``r`` holds chunks ``r`` and ``2*CP-1-r`` (so every rank does the same amount of causal work).  Three
 ways to exchange keys and values over the CP group (Megatron's ``--cp-comm-type``):
 
 * ``"all_gather"`` (default, :func:`cp_attention`): K and V are all-gathered (reduce-scattered in backward);
@@ -10,6 +10,11 @@ ways to exchange keys and values over the CP group (Megatron's ``--cp-comm-type`
   step ``t``, so the exchange overlaps the attention.  Partial outputs are merged by their log-sum-exp; the
   backward pass sends the K/V blocks round again with their dK/dV accumulators, which end at their owners.
   No rank ever holds more than two K/V blocks.
+* ``"a2a"`` (:func:`cp_ulysses_attention`, DeepSpeed-Ulysses): an all-to-all trades the sequence split for a
+  split of the query groups, so each rank holds the WHOLE sequence of ``G / CP`` query groups (with their
+  K/V heads), runs one fused causal attention over it, and a second all-to-all trades back.  Needs the local
+  query-group count divisible by CP; moves 2 x (q + k + v + out) / CP of the activations per rank instead of
+  all of K/V.
 
 In the reference CP lives entirely in Megatron/TE (context_parallel_size is only carried and folded into the
 ZeRO group, parallel_strategy.py:131-147).
@@ -24,7 +29,7 @@ import torch.distributed as dist
 
 from ..ops import functional as F_
 
-CP_COMM_TYPES = ("all_gather", "p2p")
+CP_COMM_TYPES = ("all_gather", "p2p", "a2a")
 
 
 def _global_chunk_starts(s: int, cp: int):
@@ -91,7 +96,8 @@ class _Ring:
         self.group, self.nxt, self.prv = group, ranks[(cp_rank + 1) % cp], ranks[(cp_rank - 1) % cp]
 
     def start(self, send: torch.Tensor) -> Tuple[torch.Tensor, list]:
-        recv = torch.empty_like(send)
+        send = send.contiguous()
+        recv = torch.empty(send.shape, dtype=send.dtype, device=send.device)
         ops = [dist.P2POp(dist.isend, send, self.nxt, self.group), dist.P2POp(dist.irecv, recv, self.prv, self.group)]
         return recv, dist.batch_isend_irecv(ops)
 
@@ -211,3 +217,53 @@ def cp_ring_attention(qkv: torch.Tensor, hpg: int, group, cp_rank: int, cp: int)
     [s, b, G*hpg*d]).  Scores, softmax statistics and accumulators are fp32 whatever the input dtype; the
     math is plain tensor algebra, so the same code runs on the host and on the device."""
     return _RingAttnFn.apply(qkv, hpg, group, cp_rank, cp)
+
+
+# --------------------------------------------------------------------------------------------- ulysses
+class _AllToAll(torch.autograd.Function):
+    """Equal-split all-to-all over dim 0 (``[CP, ...]``: slot j goes to CP rank j, slot i comes from rank i).
+    Its adjoint is the same exchange, so the backward pass is one more all-to-all of the gradient.  Both
+    buffers are dense: the incoming gradient is often a permuted view, and a receive buffer shaped after it
+    with ``empty_like`` would keep its strides while the collective writes contiguous bytes."""
+
+    @staticmethod
+    def forward(ctx, x, group):
+        ctx.group = group
+        return _AllToAll._exchange(x, group)
+
+    @staticmethod
+    def backward(ctx, dy):
+        return _AllToAll._exchange(dy, ctx.group), None
+
+    @staticmethod
+    def _exchange(x, group):
+        x = x.contiguous()
+        out = torch.empty(x.shape, dtype=x.dtype, device=x.device)
+        dist.all_to_all_single(out, x, group=group)
+        return out
+
+
+def cp_ulysses_attention(qkv: torch.Tensor, hpg: int, group, cp_rank: int, cp: int) -> torch.Tensor:
+    """Causal attention with the CP split moved from the sequence to the query groups and back.
+
+    Same inputs and output as :func:`cp_attention`.  Query group slice ``j`` (``G / CP`` groups) of every
+    rank's two chunks goes to rank ``j``; rank ``j`` puts the ``2 * CP`` chunks in global order, attends over
+    the whole sequence with one fused causal call (grouped-query attention native to it) and sends each rank
+    its own two chunks back."""
+    s, b, G, w, d = qkv.shape
+    if G % cp:
+        raise ValueError(f"cp_comm_type a2a needs the local query groups ({G}) divisible by CP ({cp})")
+    gp, c, S = G // cp, s // 2, cp * s
+    x = qkv.reshape(s, b, cp, gp, w, d).permute(2, 0, 1, 3, 4, 5)  # [dest rank, s, b, gp, hpg+2, d]
+    y = _AllToAll.apply(x.contiguous(), group)  # [source rank, s, b, gp, hpg+2, d]
+    chunks = [y[g, :c] if g < cp else y[2 * cp - 1 - g, c:] for g in range(2 * cp)]
+    full = torch.cat(chunks, 0)  # [S, b, gp, hpg+2, d], global sequence order
+    q = full[:, :, :, :hpg].reshape(S, b, gp * hpg, d).permute(1, 2, 0, 3)
+    k = full[:, :, :, hpg].permute(1, 2, 0, 3)
+    v = full[:, :, :, hpg + 1].permute(1, 2, 0, 3)
+    o = torch.nn.functional.scaled_dot_product_attention(q, k, v, is_causal=True, enable_gqa=hpg > 1)
+    o = o.permute(2, 0, 1, 3).reshape(S, b, gp, hpg * d)
+    back = torch.stack([torch.cat([o[j * c:(j + 1) * c], o[(2 * cp - 1 - j) * c:(2 * cp - j) * c]], 0)
+                        for j in range(cp)])  # [dest rank, s, b, gp, hpg*d]
+    r = _AllToAll.apply(back, group)  # [query group slice, s, b, gp, hpg*d]
+    return r.permute(1, 2, 0, 3, 4).reshape(s, b, G * hpg * d)

@@ -46,8 +46,9 @@ def parse_args(argv=None):
     ap.add_argument("--lr-warmup-iters", type=int, default=2)
     ap.add_argument("--engine", default=None, choices=[None, "native", "torch", "reference"])
     ap.add_argument("--overlap-grad-reduce", action="store_true")
-    ap.add_argument("--cp-comm-type", default="all_gather", choices=["all_gather", "p2p"],
-                    help="context parallelism: gather K/V over the CP group, or pass it round a ring")
+    ap.add_argument("--cp-comm-type", default="all_gather", choices=["all_gather", "p2p", "a2a"],
+                    help="context parallelism: gather K/V over the CP group, pass it round a ring, or all-to-all "
+                         "to a query-group split (Ulysses)")
     ap.add_argument("--save", default=None, help="checkpoint directory written at the end")
     ap.add_argument("--save-around-reshard", action="store_true",
                     help="write before_reshard/ and after_reshard/ checkpoints at every switch (for compare_ckpt)")

@@ -92,9 +92,10 @@ def _ring_vs_gather(rank, world, gqa):
     import torch
     import torch.distributed as dist
 
-    from elasticmegatron_b200.parallel.context_parallel import cp_attention, cp_ring_attention
+    from elasticmegatron_b200.parallel.context_parallel import (cp_attention, cp_ring_attention,
+                                                                cp_ulysses_attention)
 
-    G, hpg, d, b, s = (2, 2, 16, 2, 12) if gqa else (4, 1, 16, 2, 12)
+    G, hpg, d, b, s = (4, 2, 16, 2, 12) if gqa else (4, 1, 16, 2, 12)
     gen = torch.Generator().manual_seed(7)
     # one global sequence; rank r holds global chunks r and 2*CP-1-r
     full = torch.randn(2 * world * (s // 2), b, G, hpg + 2, d, generator=gen, dtype=torch.float64)
@@ -105,33 +106,39 @@ def _ring_vs_gather(rank, world, gqa):
     mine, dmine = full[idx].float(), dfull[idx].float()
     out = {}
     res = []
-    for fn in (cp_attention, cp_ring_attention):
+    for fn in (cp_attention, cp_ring_attention, cp_ulysses_attention):
         x = mine.clone().requires_grad_()
         y = fn(x, hpg, dist.group.WORLD, rank, world)
         y.backward(dmine)
         res.append((y.detach(), x.grad))
-    out["fwd"] = (res[0][0] - res[1][0]).abs().max().item()
-    out["bwd"] = (res[0][1] - res[1][1]).abs().max().item()
-    # the whole-sequence oracle on every rank: plain causal attention of the global sequence
-    q = full[:, :, :, :hpg].permute(1, 2, 3, 0, 4)
-    k, v = full[:, :, :, hpg].permute(1, 2, 0, 3), full[:, :, :, hpg + 1].permute(1, 2, 0, 3)
+    out["fwd"] = max((res[0][0] - r[0]).abs().max().item() for r in res[1:])
+    out["bwd"] = max((res[0][1] - r[1]).abs().max().item() for r in res[1:])
+    # the whole-sequence oracle on every rank: plain causal attention of the global sequence (fp64), and its
+    # gradient for the loss sum over ranks of <out_r, dout_r> = <out, dfull>
+    F = full.clone().requires_grad_()
+    q = F[:, :, :, :hpg].permute(1, 2, 3, 0, 4)
+    k, v = F[:, :, :, hpg].permute(1, 2, 0, 3), F[:, :, :, hpg + 1].permute(1, 2, 0, 3)
     sc = torch.einsum("bghid,bgjd->bghij", q, k) / d ** 0.5
     n = sc.shape[-1]
     sc = sc.masked_fill(torch.ones(n, n, dtype=torch.bool).triu(1), float("-inf"))
     o = torch.einsum("bghij,bgjd->bghid", sc.softmax(-1), v).permute(3, 0, 1, 2, 4).reshape(n, b, -1)
-    out["oracle"] = (o[idx].float() - res[1][0]).abs().max().item()
+    (o * dfull).sum().backward()
+    out["oracle"] = max((o[idx].detach().float() - r[0]).abs().max().item() for r in res)
+    out["oracle_bwd"] = max((F.grad[idx].float() - r[1]).abs().max().item() for r in res)
     return out
 
 
-def test_ring_attention_matches_all_gather():
-    """cp_comm_type p2p (ring) against all_gather and against causal attention of the unsplit sequence."""
+def test_ring_and_ulysses_attention_match_all_gather():
+    """cp_comm_type p2p (ring) and a2a (Ulysses) against all_gather, and all three against causal attention
+    of the unsplit sequence (forward and gradients)."""
     for world in (2, 4):
         for gqa in (False, True):
             for r in run_distributed(_ring_vs_gather, world, gqa):
-                assert r["fwd"] < 1e-5 and r["bwd"] < 1e-5 and r["oracle"] < 1e-5, (world, gqa, r)
+                assert max(r.values()) < 1e-5, (world, gqa, r)
 
 
-def test_cp2_ring_equals_dp2():
+def test_cp2_ring_and_ulysses_equal_dp2():
     dp = run_distributed(_run, 2, [0, 0, 0], True)[0]
-    ring = run_distributed(_run, 2, [1, 1, 1], True, "p2p")[0]
-    np.testing.assert_allclose(dp, ring, rtol=1e-5)
+    for kind in ("p2p", "a2a"):
+        cp = run_distributed(_run, 2, [1, 1, 1], True, kind)[0]
+        np.testing.assert_allclose(dp, cp, rtol=1e-5, err_msg=kind)
