@@ -112,7 +112,7 @@ class TrainConfig:
     overlap_grad_reduce: bool = False
     ddp_bucket_size: Optional[int] = None
     grad_reduce_in_fp32: bool = True
-    # memory
+    # memory: recompute every transformer layer's activations in backward (keep only layer inputs)
     recompute: bool = False
     # context parallelism: "all_gather" (K/V gathered over the CP group), "p2p" (K/V passed round a ring) or
     # "a2a" (Ulysses: all-to-all from a sequence split to a query-group split and back)

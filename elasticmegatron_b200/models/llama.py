@@ -19,6 +19,7 @@ from __future__ import annotations
 from typing import Dict, List, Optional
 
 import torch
+import torch.utils.checkpoint
 from torch import nn
 
 from ..config import ModelConfig
@@ -58,7 +59,7 @@ def cp_positions(seq: int, cp: int, cp_rank: int) -> torch.Tensor:
 
 class GPTStage(nn.Module):
     def __init__(self, cfg: ModelConfig, pstate, params: List[LocalParam], views: Dict[str, torch.Tensor],
-                 micro_batch_size: int, cp_comm_type: str = "all_gather"):
+                 micro_batch_size: int, cp_comm_type: str = "all_gather", recompute: bool = False):
         super().__init__()
         if cp_comm_type not in CP_COMM_TYPES:
             raise ValueError(f"cp_comm_type must be one of {CP_COMM_TYPES}, got {cp_comm_type!r}")
@@ -69,6 +70,10 @@ class GPTStage(nn.Module):
         self.cp = s.context_parallel_size
         self.first, self.last = pstate.is_first_stage, pstate.is_last_stage
         self.mbs = micro_batch_size
+        # full activation recompute, one transformer layer per checkpoint (Megatron's --recompute-granularity
+        # full --recompute-method uniform --recompute-num-layers 1, which the reference's MoE launcher uses,
+        # run_moe.sh:101-105): only each layer's input is kept; backward replays the layer's forward
+        self.recompute = recompute
         self.tp_group = pstate.group("tp") if self.tp > 1 else None
         self.cp_group = pstate.group("cp") if self.cp > 1 else None
         self.cp_attention = {"all_gather": cp_attention, "p2p": cp_ring_attention,
@@ -119,8 +124,16 @@ class GPTStage(nn.Module):
         positions = cp_positions(cfg.seq_length, self.cp, self.ps.cp_rank if self.cp > 1 else 0)
         cos, sin = _ROPE.get(positions, cfg.head_dim, cfg.rotary_base, x.device)
         aux_total = None
+        recompute = self.recompute and torch.is_grad_enabled()
         for i in range(self.num_local_layers):
-            x, aux = self._layer(i, x, cos, sin, seq_local, b)
+            if recompute:
+                # early stop off: every rank replays the whole layer, so its collectives run in full and in
+                # the same order on all ranks of each group
+                with torch.utils.checkpoint.set_checkpoint_early_stop(False):
+                    x, aux = torch.utils.checkpoint.checkpoint(self._layer, i, x, cos, sin, seq_local, b,
+                                                               use_reentrant=False)
+            else:
+                x, aux = self._layer(i, x, cos, sin, seq_local, b)
             if aux is not None:
                 aux_total = aux if aux_total is None else aux_total + aux
         if not self.last:

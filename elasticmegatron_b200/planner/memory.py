@@ -6,7 +6,7 @@
   transformer layer and token: the layer input and the norm outputs (3 h), the fused QKV output (h + 2 kv),
   the attention output (h), the fc1 output and the SwiGLU output (2 f' + f', f' = ffn / TP), stored in the model
   dtype, divided by TP where sequence parallelism shards them; under 1F1B the first stage holds PP micro-batches
-  in flight;
+  in flight; with full recompute only each layer's input is kept, plus one layer's set during its replay;
 * switch: source and destination arenas coexist while the state moves (the source is released after).
 
 The reference has no estimator; its release / rebuild machinery exists because several layouts do not fit at
@@ -33,7 +33,7 @@ def state_bytes(cfg: ModelConfig, strategy, rank: int, overlap_grad_reduce: bool
     return out
 
 
-def activation_bytes(cfg: ModelConfig, strategy, micro_batch_size: int = 1) -> int:
+def activation_bytes(cfg: ModelConfig, strategy, micro_batch_size: int = 1, recompute: bool = False) -> int:
     tp, pp, cp = (strategy.tensor_model_parallel_size, strategy.pipeline_model_parallel_size,
                   strategy.context_parallel_size)
     h = cfg.hidden_size
@@ -44,6 +44,10 @@ def activation_bytes(cfg: ModelConfig, strategy, micro_batch_size: int = 1) -> i
     per_token = seq_sharded / tp + (h + 2 * kv) / tp + 3 * f / tp
     layers = cfg.num_layers // pp
     in_flight = pp  # 1F1B: the first stage holds PP micro-batches
+    if recompute:
+        # only each layer's input stays (sequence-sharded under SP), plus one layer's full set while it replays
+        layer_input = h / tp if strategy.sequence_parallel else h
+        return int((layer_input * layers * in_flight + per_token) * tokens * _dtype_bytes(cfg))
     return int(per_token * tokens * layers * in_flight * _dtype_bytes(cfg))
 
 
@@ -55,7 +59,7 @@ def layout_report(cfg: ModelConfig, strategy, train: Optional[TrainConfig] = Non
         st = state_bytes(cfg, strategy, r, train.overlap_grad_reduce, train.ddp_bucket_size)
         if worst is None or st["total"] > worst["total"]:
             worst = dict(st)
-    worst["activations"] = activation_bytes(cfg, strategy, train.micro_batch_size)
+    worst["activations"] = activation_bytes(cfg, strategy, train.micro_batch_size, train.recompute)
     worst["peak"] = worst["total"] + worst["activations"]
     return worst
 

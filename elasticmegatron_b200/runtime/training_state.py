@@ -59,7 +59,8 @@ class TrainingState:
             self._alloc_model()
             self._alloc_opt()
         views = self._param_views() if not is_meta_device else self._meta_views()
-        self.stage = GPTStage(self.cfg, self.ps, self.layout.params, views, tc.micro_batch_size, tc.cp_comm_type)
+        self.stage = GPTStage(self.cfg, self.ps, self.layout.params, views, tc.micro_batch_size, tc.cp_comm_type,
+                              tc.recompute)
         self.stage._training_state = self
         self.model = [self.stage]
         self.ddp = DistributedDataParallel(self.layout, self.ps, self.stage.params_by_name, self.param_flat,
@@ -130,7 +131,8 @@ class TrainingState:
             # gradient hooks afresh over the new arenas (the optimizer and scheduler objects survive)
             self.ddp.remove_hooks()
             self.stage = GPTStage(self.cfg, self.ps, self.layout.params, self._param_views(),
-                                  self.train_cfg.micro_batch_size, self.train_cfg.cp_comm_type)
+                                  self.train_cfg.micro_batch_size, self.train_cfg.cp_comm_type,
+                                  self.train_cfg.recompute)
             self.stage._training_state = self
             self.model = [self.stage]
             self.ddp = DistributedDataParallel(self.layout, self.ps, self.stage.params_by_name, self.param_flat,

@@ -82,3 +82,8 @@ def test_memory_estimate():
     assert set(ok) == {str(s1), str(s2)} and all("fits" in v for v in ok.values())
     two = fits(cfg, [P.parse("ws2"), P.parse("ws2-tp2")], 183 * 2**30)
     assert not any(v["fits"] for v in two.values())  # 13B on 2 GPUs: switching needs both layouts at once
+    from elasticmegatron_b200.planner.memory import activation_bytes
+
+    for spec in ("ws8", "ws8-tp4", "ws8-pp4", "ws8-tp2-pp2"):
+        full, rec = activation_bytes(cfg, P.parse(spec), 1), activation_bytes(cfg, P.parse(spec), 1, recompute=True)
+        assert rec < full / 4, (spec, full, rec)  # full recompute keeps one hidden vector per layer and token
