@@ -46,6 +46,8 @@ def parse_args(argv=None):
     ap.add_argument("--lr-warmup-iters", type=int, default=2)
     ap.add_argument("--engine", default=None, choices=[None, "native", "torch", "reference"])
     ap.add_argument("--overlap-grad-reduce", action="store_true")
+    ap.add_argument("--recompute", action="store_true",
+                    help="recompute every transformer layer's activations in backward (full, one layer each)")
     ap.add_argument("--cp-comm-type", default="all_gather", choices=["all_gather", "p2p", "a2a"],
                     help="context parallelism: gather K/V over the CP group, pass it round a ring, or all-to-all "
                          "to a query-group split (Ulysses)")
@@ -107,7 +109,7 @@ def main(argv=None):
                                                global_batch_size=a.global_batch_size, lr=a.lr, min_lr=a.min_lr,
                                                lr_warmup_iters=a.lr_warmup_iters, train_iters=a.train_iters,
                                                overlap_grad_reduce=a.overlap_grad_reduce,
-                                               cp_comm_type=a.cp_comm_type)))
+                                               cp_comm_type=a.cp_comm_type, recompute=a.recompute)))
     specs = a.strategies.split(",") if a.strategies else default_schedule(world)
     strategies = [ParallelStrategy.parse(s) for s in specs]
     uniq = list(dict.fromkeys(strategies))
