@@ -118,6 +118,18 @@ class TrainConfig:
     # "a2a" (Ulysses: all-to-all from a sequence split to a query-group split and back)
     cp_comm_type: str = "all_gather"
 
+    def __post_init__(self):
+        # Megatron flags kept for familiarity; the training core implements one setting of each
+        if not self.use_distributed_optimizer:
+            raise ValueError("the optimizer state is always sharded over the DP*CP ranks (ZeRO-1); for a replicated "
+                             "optimizer give the strategy num_distributed_optimizer_instances = DP*CP")
+        if not self.grad_reduce_in_fp32:
+            raise ValueError("gradients always accumulate and reduce in fp32 (main_grad)")
+        if self.lr_decay_style not in ("cosine", "linear", "constant"):
+            raise ValueError(f"lr_decay_style must be cosine, linear or constant, got {self.lr_decay_style!r}")
+        if self.cp_comm_type not in ("all_gather", "p2p", "a2a"):
+            raise ValueError(f"cp_comm_type must be all_gather, p2p or a2a, got {self.cp_comm_type!r}")
+
 
 @dataclass
 class Args:

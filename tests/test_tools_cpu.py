@@ -87,3 +87,16 @@ def test_memory_estimate():
     for spec in ("ws8", "ws8-tp4", "ws8-pp4", "ws8-tp2-pp2"):
         full, rec = activation_bytes(cfg, P.parse(spec), 1), activation_bytes(cfg, P.parse(spec), 1, recompute=True)
         assert rec < full / 4, (spec, full, rec)  # full recompute keeps one hidden vector per layer and token
+
+
+def test_train_config_rejects_unsupported_flags():
+    """Megatron flags whose other setting the training core does not implement fail loudly, not silently."""
+    import pytest
+
+    from elasticmegatron_b200.config import TrainConfig
+
+    TrainConfig(lr_decay_style="linear", cp_comm_type="a2a")
+    for kw in (dict(use_distributed_optimizer=False), dict(grad_reduce_in_fp32=False), dict(lr_decay_style="wsd"),
+               dict(cp_comm_type="ring")):
+        with pytest.raises(ValueError):
+            TrainConfig(**kw)
