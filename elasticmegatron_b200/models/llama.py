@@ -139,7 +139,10 @@ class GPTStage(nn.Module):
         if not self.last:
             return x, aux_total
         x = F_.rmsnorm(x, self.params_by_name["decoder.final_layernorm.weight"], cfg.norm_epsilon)
-        w_out = self.params_by_name["output_layer.weight"]
+        # untied, or the last stage's copy of a tied embedding; at PP=1 a tied head is the embedding itself
+        w_out = self.params_by_name.get("output_layer.weight")
+        if w_out is None:
+            w_out = self.params_by_name["embedding.word_embeddings.weight"]
         logits = F_.linear(x, w_out, self._mode("col"), self.tp_group)
         lab = labels.t().contiguous().view(-1)
         losses = F_.vocab_parallel_cross_entropy(logits, lab, self.vocab_start, self.tp_group)

@@ -46,6 +46,8 @@ class VParam:
     init: str = "normal"  # "normal" | "ones"
     # name of the model parameter (within a layer / stage) this virtual param lives in
     local_key: str = ""
+    # the word embedding also serves as the output layer (untie_embeddings_and_output_weights=False)
+    tied_head: bool = False
 
     @property
     def is_expert(self) -> bool:
@@ -95,7 +97,7 @@ def build_virtual_params(cfg: ModelConfig) -> List[VParam]:
         vps.append(VParam(index=len(vps), **kw))
 
     add(name="embedding.word_embeddings.weight", shape=(v, h), tp_dim=0, stage_kind=PRE,
-        local_key="embedding.word_embeddings.weight")
+        local_key="embedding.word_embeddings.weight", tied_head=not cfg.untie_embeddings_and_output_weights)
     for layer in range(cfg.num_layers):
         for p in _layer_params(cfg):
             name = p.pop("name", p["key"])
@@ -121,6 +123,10 @@ class LocalParam:
     sp_partial: bool
     # (virtual param, element offset of the virtual param's local shard inside this tensor)
     members: List[Tuple[VParam, int]] = field(default_factory=list)
+    # tied word embedding: its gradient is summed over the embedding group (first and last pipeline stage)
+    # before the DP reduction; ``replica`` marks the last stage's copy, which the gradient norm skips
+    tied: bool = False
+    replica: bool = False
 
     @property
     def numel(self) -> int:
@@ -136,6 +142,15 @@ def stage_of(vp: VParam, cfg: ModelConfig, pp: int) -> int:
     if vp.stage_kind == POST:
         return pp - 1
     return vp.layer_id // (cfg.num_layers // pp)
+
+
+def stages_of(vp: VParam, cfg: ModelConfig, pp: int) -> Tuple[int, ...]:
+    """Every pipeline stage that holds ``vp``: a tied word embedding is held by the first stage and, as the
+    output layer, by the last (Megatron keeps the same pair of copies and sums their gradients)."""
+    st = stage_of(vp, cfg, pp)
+    if vp.tied_head and pp > 1:
+        return (st, pp - 1)
+    return (st,)
 
 
 def tp_local_shape(vp: VParam, tp: int) -> Tuple[int, ...]:
@@ -154,7 +169,15 @@ def local_params(cfg: ModelConfig, vps: List[VParam], strategy, rank: int) -> Li
     per_stage = cfg.num_layers // pp
     out: List[LocalParam] = []
     stacked: Dict[Tuple[int, str], LocalParam] = {}
+    head_copy = None
     for vp in vps:
+        if vp.tied_head and pp > 1 and c["pp"] == pp - 1:
+            # the last stage's copy of the tied embedding, used as the output layer (after the final norm)
+            head_copy = LocalParam(name="output_layer.weight", key="output_layer.weight",
+                                   shape=tp_local_shape(vp, strategy.tensor_model_parallel_size), is_expert=False,
+                                   layer_local=None, weight_decay=vp.weight_decay, sp_partial=False,
+                                   members=[(vp, 0)], tied=True, replica=True)
+            continue
         if stage_of(vp, cfg, pp) != c["pp"]:
             continue
         if vp.is_expert:
@@ -185,7 +208,10 @@ def local_params(cfg: ModelConfig, vps: List[VParam], strategy, rank: int) -> Li
             ll = None
             name = vp.name
         out.append(LocalParam(name=name, key=vp.local_key, shape=shp, is_expert=False, layer_local=ll,
-                              weight_decay=vp.weight_decay, sp_partial=vp.sp_partial, members=[(vp, 0)]))
+                              weight_decay=vp.weight_decay, sp_partial=vp.sp_partial, members=[(vp, 0)],
+                              tied=vp.tied_head))
+    if head_copy is not None:
+        out.append(head_copy)
     return out
 
 

@@ -131,8 +131,12 @@ class DistributedDataParallel:
             bl = self.layout.dense if kind == "dense" else self.layout.expert
             names = [bl.params[j].name for j in bl.bucket_params[b]]
             ps = [self.params[n] for n in names]
-            # SP-partial params need a TP all-reduce first: keep their buckets for the end of backward
+            # SP-partial params need a TP all-reduce first, and tied-embedding copies a sum over the embedding
+            # group (and, at PP=1, report ready from both the embedding and the head): keep their buckets for
+            # the end of backward
             if self.sp and any(p._local_param.sp_partial for p in ps):
+                continue
+            if any(p._local_param.tied for p in ps):
                 continue
             for p in ps:
                 self._bucket_of[id(p)] = i
@@ -160,6 +164,13 @@ class DistributedDataParallel:
                 for t in parts:
                     t.copy_(flat[o:o + t.numel()])
                     o += t.numel()
+        tied = [p for p in self.params.values() if p._local_param.tied]
+        eg = self.ps.groups.get("embedding")
+        if tied and eg is not None and dist.get_world_size(eg) > 1:
+            # the first stage's word embedding and the last stage's output-layer copy of it: one gradient
+            # (Megatron's embedding-group all-reduce; the reference moves the pair with transfer.py:103-141)
+            for p in tied:
+                dist.all_reduce(p.main_grad, group=eg)
         views = self._bucket_views()
         for i, (kind, b, s, e, zi, g, ig) in enumerate(views):
             if i not in getattr(self, "_launched", set()):

@@ -39,6 +39,8 @@ def _segments(layout: RankLayout, tp_rank: int, instance: int) -> List[Tuple[int
         off = layout.offset_by_name[lp.name]
         vp = lp.members[0][0]
         dup = (not lp.is_expert) and vp.tp_dim is None and tp_rank != 0
+        # the last stage's copy of a tied embedding holds the same values and gradient as the first stage's
+        dup = dup or lp.replica
         spans.append((off, off + lp.numel, (bool(lp.weight_decay), (not dup) and instance == 0)))
     spans.sort()
     segs: List[Tuple[int, int, int, bool, bool]] = []

@@ -30,7 +30,7 @@ from typing import Dict, Iterable, List, Optional, Sequence, Tuple
 import numpy as np
 
 from ..config import ModelConfig, get_args
-from ..models.spec import VParam, stage_of, tp_col_offset, tp_row_blocks
+from ..models.spec import VParam, stages_of, tp_col_offset, tp_row_blocks
 from .layout import RankLayout, rank_layout, virtual_params
 
 KIND_OPT = 0
@@ -135,10 +135,10 @@ class _StrategyView:
         self.coords = [strategy.coords(r) for r in range(strategy.world_size)]
 
     def holders(self, vp: VParam) -> List[int]:
-        st = stage_of(vp, self.cfg, self.s.pipeline_model_parallel_size)
+        st = stages_of(vp, self.cfg, self.s.pipeline_model_parallel_size)
         out = []
         for r, c in enumerate(self.coords):
-            if c["pp"] != st:
+            if c["pp"] not in st:
                 continue
             if vp.is_expert and vp.expert_id // self.s.expert_num_per_ep_rank != c["ep"]:
                 continue
@@ -174,15 +174,16 @@ class _StrategyView:
         return _pieces(vp, tp, t, shp, ranges, bases)
 
     def replica_key(self, vp: VParam, r: int, kind: int):
-        """Ranks with equal keys hold identical data of ``vp`` at identical offsets."""
+        """Ranks with equal keys hold identical data of ``vp`` at identical offsets (the stage is part of the
+        key: the two copies of a tied embedding sit at different offsets of different layouts)."""
         c = self.coords[r]
         # a TP-replicated parameter (tp_dim None) is identical on every TP rank
         t = (c["etp"] if vp.is_expert else c["tp"]) if vp.tp_dim is not None else 0
         if kind == KIND_PARAM:
-            return (t,)
+            return (c["pp"], t)
         rl = self.layouts[r]
         z = rl.expert_shard_index if vp.is_expert else rl.dense_shard_index
-        return (t, z)
+        return (c["pp"], t, z)
 
 
 @dataclass

@@ -92,19 +92,26 @@ class ReferenceAlgorithmEngine:
 
     # ------------------------------------------------------------------ helpers
     @staticmethod
-    def _tp_groups(view, vp, holders, is_src: bool) -> Dict[int, List[int]]:
-        """Ranks holding each TP shard (instance 0 only), ordered by ZeRO shard index."""
-        out: Dict[int, List[int]] = {}
+    def _tp_groups(view, vp, holders, is_src: bool) -> Dict[tuple, List[int]]:
+        """Ranks holding each TP shard (instance 0 only), ordered by ZeRO shard index, keyed (stage, TP rank).
+
+        A tied embedding has a copy on the first and on the last stage: the source side reads the first
+        stage's, the destination side fills both (the reference re-broadcasts the word embedding to the last
+        stage over the embedding group, transfer/transfer.py:103-141)."""
+        if is_src and holders:
+            first = min(view.coords[r]["pp"] for r in holders)
+            holders = [r for r in holders if view.coords[r]["pp"] == first]
+        out: Dict[tuple, List[int]] = {}
         for r in holders:
             if view.layouts[r].instance != 0:
                 continue
             c = view.coords[r]
-            out.setdefault(c["etp"] if vp.is_expert else c["tp"], []).append(r)
+            out.setdefault((c["pp"], c["etp"] if vp.is_expert else c["tp"]), []).append(r)
         for t in out:
             out[t].sort(key=lambda r: (view.layouts[r].expert_shard_index if vp.is_expert
                                        else view.layouts[r].dense_shard_index, r))
         if vp.tp_dim is None and is_src:
-            out = {0: out.get(0, [])}
+            out = {k: v for k, v in out.items() if k[1] == 0}
         return out
 
     @staticmethod

@@ -19,10 +19,11 @@ from elasticmegatron_b200.planner.plan import apply_plan_reference, build_plan, 
 NAN = 12345.0
 
 
-def _cfg(moe=False):
+def _cfg(moe=False, tied=False):
     return ModelConfig(num_layers=4, hidden_size=64, num_attention_heads=8, num_query_groups=4, ffn_hidden_size=96,
                        vocab_size=300, params_dtype="fp32", max_tensor_parallel_size=4, make_vocab_size_divisible_by=8,
-                       num_experts=8 if moe else None, moe_ffn_hidden_size=48 if moe else None)
+                       num_experts=8 if moe else None, moe_ffn_hidden_size=48 if moe else None,
+                       untie_embeddings_and_output_weights=not tied)
 
 
 def _state(cfg, s, g, og, overlap, bucket):
@@ -73,6 +74,26 @@ def test_all_dense_pairs(overlap, bucket):
     strats = _dense_strategies()
     for a, b in itertools.permutations(strats, 2):
         _check_pair(cfg, a, b, overlap, bucket)
+
+
+def test_tied_embedding_pairs():
+    """A tied word embedding is held by the first stage and, as the output layer, by the last: every switch
+    writes both copies (including PP1 <-> PP>1, where the copy appears / disappears)."""
+    from elasticmegatron_b200.planner.layout import rank_layout
+
+    cfg = _cfg(tied=True)
+    set_args(Args(model=cfg, train=TrainConfig()))
+    strats = _dense_strategies()
+    for a, b in itertools.permutations(strats, 2):
+        _check_pair(cfg, a, b, True, 3000)
+    pp2 = ParallelStrategy(world_size=8, tensor_model_parallel_size=2, pipeline_model_parallel_size=2)
+    names = {r: [lp.name for lp in rank_layout(cfg, pp2, r).params] for r in range(8)}
+    first, last = pp2.coords(0)["pp"], pp2.coords(7)["pp"]
+    assert first == 0 and last == 1
+    assert "embedding.word_embeddings.weight" in names[0] and "output_layer.weight" not in names[0]
+    assert names[7][-1] == "output_layer.weight" and "embedding.word_embeddings.weight" not in names[7]
+    pp1 = ParallelStrategy(world_size=8, tensor_model_parallel_size=2, pipeline_model_parallel_size=1)
+    assert "output_layer.weight" not in [lp.name for lp in rank_layout(cfg, pp1, 0).params]
 
 
 def test_moe_ep_pairs():
