@@ -48,8 +48,6 @@ def run_distributed(fn, world: int, *args, timeout: float = 600.0, backend: str 
     for p in procs:
         p.start()
     results = {}
-    import queue as _q
-
     try:
         for _ in range(world):
             rank, status, res = q.get(timeout=timeout)

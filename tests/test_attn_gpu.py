@@ -1,6 +1,4 @@
 """Native flash attention against the fp32 PyTorch reference on the fused QKV layout."""
-import math
-
 import pytest
 import torch
 

@@ -1,7 +1,6 @@
 """Inter-process hand-off on CPU/gloo: a 2-rank job exports its state in place, a separate 1-rank job adopts it
 (pulling its own layout straight out of the old processes' shared memory) and continues training; the loss
 equals an in-process reshard of the same schedule."""
-import os
 import tempfile
 
 import numpy as np

@@ -14,7 +14,7 @@ from elasticmegatron_b200.config import Args, ModelConfig, TrainConfig, set_args
 from elasticmegatron_b200.parallel.strategy import ParallelStrategy
 from elasticmegatron_b200.planner.layout import rank_layout
 from elasticmegatron_b200.planner.materialize import init_global_params, scatter_to_rank
-from elasticmegatron_b200.planner.plan import apply_plan_reference, build_plan, KIND_OPT, KIND_PARAM
+from elasticmegatron_b200.planner.plan import apply_plan_reference, build_plan, KIND_OPT
 
 NAN = 12345.0
 

@@ -76,10 +76,7 @@ def test_k1_emulated_ranks():
 
 
 def _two_gpu(rank, world):
-    import os
-
     import torch
-    import torch.distributed as dist
 
     torch.cuda.set_device(rank)
     from elasticmegatron_b200.config import Args, ModelConfig, TrainConfig, set_args
