@@ -32,6 +32,8 @@ class ModelConfig:
     seq_length: int = 512
     rotary_base: float = 10000.0
     norm_epsilon: float = 1e-5
+    # "RMSNorm" (Llama) or "LayerNorm" (Megatron's default, with a bias per norm: the reference's demo model)
+    normalization: str = "RMSNorm"
     init_method_std: float = 0.02
     untie_embeddings_and_output_weights: bool = True
     # MoE
@@ -51,6 +53,8 @@ class ModelConfig:
             self.moe_ffn_hidden_size = self.ffn_hidden_size
         assert self.hidden_size % self.num_attention_heads == 0
         assert self.num_attention_heads % self.num_query_groups == 0
+        if self.normalization not in ("RMSNorm", "LayerNorm"):
+            raise ValueError(f"normalization must be RMSNorm or LayerNorm, got {self.normalization!r}")
 
     @property
     def head_dim(self) -> int:
@@ -82,13 +86,14 @@ class ModelConfig:
 
     def num_params(self) -> int:
         h, f, v = self.hidden_size, self.ffn_hidden_size, self.padded_vocab_size
-        per_layer = self.qkv_rows * h + h * h + 2 * h
+        norm = 2 * h if self.normalization == "LayerNorm" else h  # weight (+ bias)
+        per_layer = self.qkv_rows * h + h * h + 2 * norm
         if self.is_moe:
             per_layer += self.num_experts * (3 * self.moe_ffn_hidden_size * h) + self.num_experts * h
         else:
             per_layer += 3 * f * h
         emb = v * h * (2 if self.untie_embeddings_and_output_weights else 1)
-        return self.num_layers * per_layer + emb + h
+        return self.num_layers * per_layer + emb + norm
 
 
 @dataclass
@@ -189,6 +194,9 @@ PRESETS = {
                        vocab_size=32000, seq_length=4096),
     "llama3-8b": dict(num_layers=32, hidden_size=4096, num_attention_heads=32, num_query_groups=8,
                       ffn_hidden_size=14336, vocab_size=128256, seq_length=8192, rotary_base=500000.0),
+    # the reference demo's default model (run_e2e_demo.sh:25-31, MODEL_SIZE=tiny): Megatron's LayerNorm, MHA
+    "demo-tiny": dict(num_layers=4, hidden_size=4096, num_attention_heads=32, ffn_hidden_size=11008,
+                      vocab_size=32000, seq_length=4096, normalization="LayerNorm"),
     "mixtral-8x7b": dict(num_layers=32, hidden_size=4096, num_attention_heads=32, num_query_groups=8,
                          ffn_hidden_size=14336, vocab_size=32000, seq_length=4096, num_experts=8,
                          moe_router_topk=2, moe_aux_loss_coeff=1e-2, rotary_base=1e6),

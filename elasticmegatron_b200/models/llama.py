@@ -98,6 +98,14 @@ class GPTStage(nn.Module):
     def _p(self, layer: int, key: str) -> nn.Parameter:
         return self.params_by_name[f"decoder.layers.{layer}.{key}"]
 
+    def _norm(self, x: torch.Tensor, weight_name: str) -> torch.Tensor:
+        """RMSNorm (native kernel), or LayerNorm with the bias stored next to the weight."""
+        w = self.params_by_name[weight_name]
+        if self.cfg.normalization == "LayerNorm":
+            b = self.params_by_name[weight_name[:-len("weight")] + "bias"]
+            return F_.layernorm(x, w, b, self.cfg.norm_epsilon)
+        return F_.rmsnorm(x, w, self.cfg.norm_epsilon)
+
     def rebind(self, views: Dict[str, torch.Tensor]) -> None:
         """Point every parameter at a new arena (after a release / rebuild)."""
         for n, p in self.params_by_name.items():
@@ -138,7 +146,7 @@ class GPTStage(nn.Module):
                 aux_total = aux if aux_total is None else aux_total + aux
         if not self.last:
             return x, aux_total
-        x = F_.rmsnorm(x, self.params_by_name["decoder.final_layernorm.weight"], cfg.norm_epsilon)
+        x = self._norm(x, "decoder.final_layernorm.weight")
         # untied, or the last stage's copy of a tied embedding; at PP=1 a tied head is the embedding itself
         w_out = self.params_by_name.get("output_layer.weight")
         if w_out is None:
@@ -153,7 +161,7 @@ class GPTStage(nn.Module):
         G_loc = cfg.num_query_groups // self.tp
         hpg, d = cfg.heads_per_group, cfg.head_dim
         res = x
-        h = F_.rmsnorm(x, self._p(i, "self_attention.linear_qkv.layer_norm_weight"), cfg.norm_epsilon)
+        h = self._norm(x, f"decoder.layers.{i}.self_attention.linear_qkv.layer_norm_weight")
         qkv = F_.linear(h, self._p(i, "self_attention.linear_qkv.weight"), self._mode("col"), self.tp_group)
         qkv = qkv.view(seq_local, b, G_loc, hpg + 2, d)
         qkv = F_.rope_qkv(qkv, cos, sin, hpg + 1)
@@ -166,10 +174,10 @@ class GPTStage(nn.Module):
         x = res + o
         aux = None
         if self.moe is not None:
-            h = F_.rmsnorm(x, self._p(i, "pre_mlp_layernorm.weight"), cfg.norm_epsilon)
+            h = self._norm(x, f"decoder.layers.{i}.pre_mlp_layernorm.weight")
             o, aux = self.moe[i](h)
         else:
-            h = F_.rmsnorm(x, self._p(i, "mlp.linear_fc1.layer_norm_weight"), cfg.norm_epsilon)
+            h = self._norm(x, f"decoder.layers.{i}.mlp.linear_fc1.layer_norm_weight")
             h = F_.linear(h, self._p(i, "mlp.linear_fc1.weight"), self._mode("col"), self.tp_group)
             h = F_.swiglu(h)
             o = F_.linear(h, self._p(i, "mlp.linear_fc2.weight"), self._mode("row"), self.tp_group)

@@ -43,7 +43,7 @@ class VParam:
     expert_id: Optional[int] = None
     sp_partial: bool = False  # grad is a partial sum across TP ranks under sequence parallelism
     weight_decay: bool = True
-    init: str = "normal"  # "normal" | "ones"
+    init: str = "normal"  # "normal" | "ones" | "zeros"
     # name of the model parameter (within a layer / stage) this virtual param lives in
     local_key: str = ""
     # the word embedding also serves as the output layer (untie_embeddings_and_output_weights=False)
@@ -61,11 +61,20 @@ class VParam:
         return n
 
 
+def _norm_bias(cfg: ModelConfig, key: str) -> List[dict]:
+    """LayerNorm's bias next to a norm weight (TransformerEngine / Megatron names); none under RMSNorm."""
+    if cfg.normalization != "LayerNorm":
+        return []
+    bkey = key[:-len("weight")] + "bias"
+    return [dict(key=bkey, shape=(cfg.hidden_size,), sp_partial=True, weight_decay=False, init="zeros")]
+
+
 def _layer_params(cfg: ModelConfig) -> List[dict]:
     h = cfg.hidden_size
     out = [
         dict(key="self_attention.linear_qkv.layer_norm_weight", shape=(h,), sp_partial=True, weight_decay=False,
              init="ones"),
+        *_norm_bias(cfg, "self_attention.linear_qkv.layer_norm_weight"),
         dict(key="self_attention.linear_qkv.weight", shape=(cfg.qkv_rows, h), tp_dim=0),
         dict(key="self_attention.linear_proj.weight", shape=(h, cfg.num_attention_heads * cfg.head_dim), tp_dim=1),
     ]
@@ -73,6 +82,7 @@ def _layer_params(cfg: ModelConfig) -> List[dict]:
         f = cfg.moe_ffn_hidden_size
         out.append(dict(key="pre_mlp_layernorm.weight", shape=(h,), sp_partial=True, weight_decay=False,
                         init="ones"))
+        out += _norm_bias(cfg, "pre_mlp_layernorm.weight")
         out.append(dict(key="mlp.router.weight", shape=(cfg.num_experts, h), sp_partial=True))
         for e in range(cfg.num_experts):
             out.append(dict(key="mlp.experts.linear_fc1.weight", shape=(2 * f, h), tp_dim=0, tp_kind="swiglu",
@@ -83,6 +93,7 @@ def _layer_params(cfg: ModelConfig) -> List[dict]:
         f = cfg.ffn_hidden_size
         out.append(dict(key="mlp.linear_fc1.layer_norm_weight", shape=(h,), sp_partial=True, weight_decay=False,
                         init="ones"))
+        out += _norm_bias(cfg, "mlp.linear_fc1.layer_norm_weight")
         out.append(dict(key="mlp.linear_fc1.weight", shape=(2 * f, h), tp_dim=0, tp_kind="swiglu"))
         out.append(dict(key="mlp.linear_fc2.weight", shape=(h, f), tp_dim=1))
     return out
@@ -105,6 +116,9 @@ def build_virtual_params(cfg: ModelConfig) -> List[VParam]:
             add(name=f"decoder.layers.{layer}.{name}", layer_id=layer, stage_kind=LAYER, local_key=key, **p)
     add(name="decoder.final_layernorm.weight", shape=(h,), stage_kind=POST, sp_partial=True, weight_decay=False,
         init="ones", local_key="decoder.final_layernorm.weight")
+    if cfg.normalization == "LayerNorm":
+        add(name="decoder.final_layernorm.bias", shape=(h,), stage_kind=POST, sp_partial=True, weight_decay=False,
+            init="zeros", local_key="decoder.final_layernorm.bias")
     if cfg.untie_embeddings_and_output_weights:
         add(name="output_layer.weight", shape=(v, h), tp_dim=0, stage_kind=POST, local_key="output_layer.weight")
     return vps

@@ -247,6 +247,13 @@ def rmsnorm(x, w, eps):
     return RMSNormFn.apply(x, w, eps)
 
 
+def layernorm(x, w, b, eps):
+    """Megatron's LayerNorm (weight and bias) over the last dimension.  It runs the library kernel on both
+    host and device (as attention does by default); the weight and bias gradients reach ``main_grad``
+    through the data-parallel layer's accumulation hook."""
+    return torch.nn.functional.layer_norm(x, (x.shape[-1],), w, b, eps)
+
+
 # ------------------------------------------------------------------------------------------ SwiGLU
 class SwiGLUFn(torch.autograd.Function):
     @staticmethod

@@ -90,6 +90,8 @@ def init_global_params(cfg: ModelConfig, seed: int = 0, dtype=torch.float32) -> 
         g = torch.Generator().manual_seed(seed * 1_000_003 + vp.index)
         if vp.init == "ones":
             out[vp.index] = torch.ones(vp.shape, dtype=dtype)
+        elif vp.init == "zeros":
+            out[vp.index] = torch.zeros(vp.shape, dtype=dtype)
         else:
             out[vp.index] = torch.randn(vp.shape, generator=g, dtype=torch.float32).mul_(
                 cfg.init_method_std).to(dtype)

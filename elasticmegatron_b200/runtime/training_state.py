@@ -188,6 +188,8 @@ class TrainingState:
                 v = P[off:off + lp.numel]
                 if vp.init == "ones":
                     v.fill_(1.0)
+                elif vp.init == "zeros":
+                    v.zero_()
                 else:
                     gen = torch.Generator(device=P.device)
                     gen.manual_seed(seed * 7919 + vp.index * 131 + (c["etp"] if lp.is_expert else c["tp"]) * 17
