@@ -21,6 +21,7 @@ its optimizer arena ``[dense shards | expert shards]``.
 """
 from __future__ import annotations
 
+import bisect
 from dataclasses import dataclass, field
 from typing import Dict, List, Optional, Tuple
 
@@ -114,6 +115,8 @@ class RankLayout:
     # virtual-param index -> (arena offset of its local shard, local shard shape)
     vp_loc: Dict[int, Tuple[int, Tuple[int, ...]]] = field(default_factory=dict)
     offset_by_name: Dict[str, int] = field(default_factory=dict)
+    _owned: Optional[List[Tuple[int, int, int]]] = field(default=None, repr=False, compare=False)
+    _owned_starts: Optional[List[int]] = field(default=None, repr=False, compare=False)
 
     def __post_init__(self):
         for i, lp in enumerate(self.dense.params):
@@ -140,12 +143,29 @@ class RankLayout:
         return self.offset_by_name[lp.name]
 
     def owned(self) -> List[Tuple[int, int, int]]:
-        """(arena_start, arena_end, opt_offset) of every owned optimizer slice (dense then expert)."""
-        out = list(self.dense.owned_ranges(self.dense_shard_index))
-        if self.expert is not None:
-            base_p, base_o = self.dense.numel, self.dense.opt_numel
-            out += [(s + base_p, e + base_p, o + base_o)
-                    for s, e, o in self.expert.owned_ranges(self.expert_shard_index)]
+        """(arena_start, arena_end, opt_offset) of every owned optimizer slice (dense then expert), in arena
+        order; computed once per layout (layouts are cached, and the planner asks per parameter)."""
+        if self._owned is None:
+            out = list(self.dense.owned_ranges(self.dense_shard_index))
+            if self.expert is not None:
+                base_p, base_o = self.dense.numel, self.dense.opt_numel
+                out += [(s + base_p, e + base_p, o + base_o)
+                        for s, e, o in self.expert.owned_ranges(self.expert_shard_index)]
+            self._owned = out
+            self._owned_starts = [s for s, _, _ in out]
+        return list(self._owned)
+
+    def owned_overlapping(self, a: int, b: int) -> List[Tuple[int, int, int]]:
+        """The owned slices that intersect the arena range ``[a, b)`` (binary search; slices are disjoint and
+        sorted)."""
+        self.owned()
+        i = max(0, bisect.bisect_right(self._owned_starts, a) - 1)
+        out = []
+        while i < len(self._owned) and self._owned[i][0] < b:
+            s, e, o = self._owned[i]
+            if e > a:
+                out.append((s, e, o))
+            i += 1
         return out
 
 

@@ -165,7 +165,7 @@ class _StrategyView:
         for x in shp:
             n *= x
         ranges, bases = [], []
-        for s, e, o in rl.owned():
+        for s, e, o in rl.owned_overlapping(P, P + n):
             lo, hi = max(s, P), min(e, P + n)
             if lo < hi:
                 ranges.append((lo - P, hi - P))

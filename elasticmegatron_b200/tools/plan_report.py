@@ -5,7 +5,9 @@
 
 Runs the planner on the host only (no GPU, no processes).  The roofline is max over GPUs of max(egress, ingress)
 bytes that cross NVLink divided by ``--link-gbs`` (default: the measured 770 GB/s per direction of B200 peer
-copies); the JSON line at the end holds the same figures.
+copies); the JSON line at the end holds the same figures, plus the host cost of a first switch between the
+pair: building the plan (``plan_ms``, layouts not cached) and the slowest rank's transfer task table
+(``tasks_ms_max``, with stand-in addresses).  Later switches between the same pair reuse both.
 """
 from __future__ import annotations
 
@@ -27,8 +29,23 @@ def report(model: str, src: str, dst: str, layers=None, link_gbs: float = 770.0,
         over["num_layers"] = layers
     cfg = preset(model, **over)
     set_args(Args(model=cfg, train=TrainConfig(overlap_grad_reduce=True)))
+    import time
+
+    from ..planner import layout as _layout
+    from ..transfer.native_engine import NativeP2PEngine
+
     a, b = ParallelStrategy.parse(src), ParallelStrategy.parse(dst)
+    _layout._RL_CACHE.clear()
+    t0 = time.perf_counter()
     plan = build_plan(a, b, cfg, overlap_grad_reduce=True, ddp_bucket_size=None)
+    plan_ms = (time.perf_counter() - t0) * 1e3
+    n = max(a.world_size, b.world_size)
+    addrs = {r: tuple((1 << 40) * (4 * r + j + 1) for j in range(4)) for r in range(n)}  # stand-ins, never used
+    eng, tasks_ms = NativeP2PEngine(), 0.0
+    for r in range(n):
+        t0 = time.perf_counter()
+        eng._tasks(plan, r, addrs, 2)
+        tasks_ms = max(tasks_ms, (time.perf_counter() - t0) * 1e3)
     dt = 4
     m = plan.bytes_matrix(dt, 2)
     local = int(np.trace(m))
@@ -37,7 +54,7 @@ def report(model: str, src: str, dst: str, layers=None, link_gbs: float = 770.0,
            "nvlink_bytes": int(m.sum()), "local_bytes": local,
            "max_egress_bytes": int(m.sum(1).max(initial=0)), "max_ingress_bytes": int(m.sum(0).max(initial=0)),
            "roofline_ms": plan.nvlink_roofline_ms(link_gbs, dt, 2), "link_gbs": link_gbs,
-           "bytes_matrix_gb": (m / 1e9).round(3).tolist()}
+           "bytes_matrix_gb": (m / 1e9).round(3).tolist(), "plan_ms": plan_ms, "tasks_ms_max": tasks_ms}
     from ..planner.memory import layout_report, switch_peak_bytes
 
     out["memory_gb"] = {"src": {k: v / 1e9 for k, v in layout_report(cfg, a).items()},
@@ -62,7 +79,8 @@ def main(argv=None) -> int:
     print(f"{r['src']} -> {r['dst']} ({r['model']}): {r['copies']} copies, "
           f"{r['nvlink_bytes'] / 1e9:.2f} GB over NVLink, {r['local_bytes'] / 1e9:.2f} GB local; "
           f"busiest GPU sends {r['max_egress_bytes'] / 1e9:.2f} GB / receives {r['max_ingress_bytes'] / 1e9:.2f} GB; "
-          f"NVLink roofline {r['roofline_ms']:.2f} ms at {r['link_gbs']:.0f} GB/s")
+          f"NVLink roofline {r['roofline_ms']:.2f} ms at {r['link_gbs']:.0f} GB/s; host: plan {r['plan_ms']:.0f} ms, "
+          f"task table {r['tasks_ms_max']:.0f} ms (slowest rank)")
     mem = r["memory_gb"]
     print(f"per-GPU memory (largest rank): source {mem['src']['peak']:.1f} GB (state {mem['src']['total']:.1f} + "
           f"activations ~{mem['src']['activations']:.1f}), destination {mem['dst']['peak']:.1f} GB; during the "
