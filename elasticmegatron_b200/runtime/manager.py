@@ -66,7 +66,13 @@ class ElasticMegatronManager:
         self.strategies = [ParallelStrategy.from_any(s) for s in parallel_strategy_list]
         assert len(set(self.strategies)) == len(self.strategies), "duplicate strategies"
         backend = dist.get_backend() if dist.is_initialized() else "gloo"
-        create_all_groups(self.strategies, backend)
+        pairs = []
+        if use_p2p_to_collective and dist.is_initialized():
+            # P2P as a broadcast needs a group per rank pair; the reference builds all N(N-1)/2 of them up front
+            # (distributed/elastic_process_group.py:235-245), collectively here like every other group
+            n = dist.get_world_size()
+            pairs = [(i, j) for i in range(n) for j in range(i + 1, n)]
+        create_all_groups(self.strategies, backend, extra=pairs)
         if training_state is None and model is not None:
             training_state = model[0]._training_state
         self._states: Dict[ParallelStrategy, Optional[TrainingState]] = {s: None for s in self.strategies}

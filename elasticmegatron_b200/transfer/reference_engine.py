@@ -133,7 +133,11 @@ class ReferenceAlgorithmEngine:
             from ..parallel.process_groups import ProcessGroupPool
 
             buf = t.contiguous()
-            self.broadcast_fn(buf, src, ProcessGroupPool.get(sorted((src, dst))))
+            pair = ProcessGroupPool.get(sorted((src, dst)))
+            if pair is None:
+                raise RuntimeError(f"no process group for ranks {{{src}, {dst}}}: construct the manager with "
+                                   "use_p2p_to_collective=True on every rank so the pair groups exist")
+            self.broadcast_fn(buf, src, pair)
             if rank == dst and buf.data_ptr() != t.data_ptr():
                 t.copy_(buf)
             if rank == src:

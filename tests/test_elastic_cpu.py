@@ -107,7 +107,7 @@ def test_bitwise_round_trip():
     assert all(run_distributed(_roundtrip, 2))
 
 
-def _engine_losses(rank, world, engine):
+def _engine_losses(rank, world, engine, strats=None):
     from elasticmegatron_b200.parallel.process_groups import create_all_groups
     from elasticmegatron_b200.parallel.strategy import ParallelStrategy
     from elasticmegatron_b200.runtime.manager import ElasticMegatronManager
@@ -115,7 +115,8 @@ def _engine_losses(rank, world, engine):
     from elasticmegatron_b200.runtime.training_state import TrainingState
 
     _setup()
-    S = [ParallelStrategy(**s) for s in STRATS]
+    strats = strats or STRATS
+    S = [ParallelStrategy.from_any(s) for s in strats]
     create_all_groups(S)
     ts = TrainingState(S[0])
     ts.init_weights(0)
@@ -127,7 +128,7 @@ def _engine_losses(rank, world, engine):
             calls["send"] += 1
             dist.send(t, dst)
 
-        mgr = ElasticMegatronManager(STRATS, training_state=ts, send_fn=send_fn)
+        mgr = ElasticMegatronManager(strats, training_state=ts, send_fn=send_fn)
     elif engine == "p2p_as_collective":
         import torch.distributed as dist
 
@@ -135,13 +136,13 @@ def _engine_losses(rank, world, engine):
             calls["bcast"] += 1
             dist.broadcast(t, src=src, group=group)
 
-        mgr = ElasticMegatronManager(STRATS, training_state=ts, broadcast_fn=bcast, use_p2p_to_collective=True)
+        mgr = ElasticMegatronManager(strats, training_state=ts, broadcast_fn=bcast, use_p2p_to_collective=True)
     else:
-        mgr = ElasticMegatronManager(STRATS, training_state=ts, engine=engine)
+        mgr = ElasticMegatronManager(strats, training_state=ts, engine=engine)
     train_step(ts, mgr.build_iterators(0)[0])
     losses = []
     for i in (1, 2, 0):
-        ts = mgr.reshard(STRATS[i])
+        ts = mgr.reshard(strats[i])
         losses.append(train_step(ts, mgr.build_iterators(8)[0])["loss"])
     if engine in ("injected", "p2p_as_collective"):
         assert mgr.engine_name == "reference" and calls["send" if engine == "injected" else "bcast"] > 0
@@ -160,6 +161,11 @@ def test_injected_communicator_and_p2p_as_collective():
     c = run_distributed(_engine_losses, 2, "p2p_as_collective")
     np.testing.assert_allclose(a[0], b[0], rtol=1e-6)
     np.testing.assert_allclose(a[0], c[0], rtol=1e-6)
+    # four ranks: the broadcasts run on two-rank groups that are not the world (all six pairs exist)
+    four = ["ws4", "ws4-tp2-pp2", "ws4-tp2"]
+    a4 = run_distributed(_engine_losses, 4, "torch", four)
+    c4 = run_distributed(_engine_losses, 4, "p2p_as_collective", four)
+    np.testing.assert_allclose(a4[0], c4[0], rtol=1e-6)
 
 
 def _ckpt(rank, world, root):
