@@ -198,6 +198,11 @@ class ElasticMegatronManager:
 
     def reshard(self, new_parallel_strategy, logger: Optional[logging.Logger] = None, is_meta_device: bool = False,
                 save_ckpt: bool = False, ckpt_dir: Optional[str] = None) -> Optional[TrainingState]:
+        # meta mode (or inside build_nccl_connection_context): build the destination's state and the switch's
+        # mappings / task tables, move no data, and leave every live state alone - neither the source is
+        # released nor a released state rebuilt (the reference turns release / rebuild into no-ops for its fake
+        # transfers, elastic_manager.py:268-304)
+        is_meta_device = is_meta_device or self._warm_only
         assert not (is_meta_device and save_ckpt), "Can't save checkpoint in meta device"
         dst_s = ParallelStrategy.from_any(new_parallel_strategy)
         assert dst_s in self._states, f"strategy {dst_s} was not declared at construction"
@@ -219,7 +224,7 @@ class ElasticMegatronManager:
         t_total = HostTimer(sync=False).__enter__()
         with HostTimer(sync=False) as t_build, nvtx_range("reshard/build"):
             dst = self._get_or_build(dst_s, is_meta_device)
-        if src is not None and src.model_released:
+        if src is not None and src.model_released and not is_meta_device:
             src.rebuild()
         with HostTimer(sync=False) as t_plan, nvtx_range("reshard/plan"):
             plan = self.plan(src_s, dst_s)
@@ -238,7 +243,7 @@ class ElasticMegatronManager:
         with HostTimer(sync=False) as t_lr, nvtx_range("reshard/lr"):
             self._transfer_lr(src, dst, union)
         with HostTimer(sync=False) as t_rel:
-            if src is not None and src is not dst:
+            if src is not None and src is not dst and not is_meta_device:
                 with nvtx_range("reshard/release"):
                     src.release()
         self.current = dst_s

@@ -1,0 +1,93 @@
+"""The reference-API entry points of the manager and the training state on gloo ranks, each checked by its
+effect: ``register`` (a custom state builder and dataset provider are the ones used), ``get_data_parallel_group``,
+``global_barrier_by_gloo``, meta-device switches (they leave the live state untouched) followed by
+``clear_meta_state``, ``release`` / ``rebuild`` (arenas return to the pool and come back),
+``update_model_weight`` (parameters regenerated from the fp32 master and all-gathered over DP) and
+``refresh_config``."""
+from dist_utils import run_distributed
+
+
+def _api(rank, world):
+    import torch
+    import torch.distributed as dist
+
+    from elasticmegatron_b200.config import Args, ModelConfig, TrainConfig, set_args
+    from elasticmegatron_b200.parallel.process_groups import create_all_groups
+    from elasticmegatron_b200.parallel.strategy import ParallelStrategy
+    from elasticmegatron_b200.runtime.data import MockGPTDataset
+    from elasticmegatron_b200.runtime.manager import ElasticMegatronManager
+    from elasticmegatron_b200.runtime.train import train_step
+    from elasticmegatron_b200.runtime.training_state import TrainingState
+
+    cfg = ModelConfig(num_layers=2, hidden_size=64, num_attention_heads=4, ffn_hidden_size=128, vocab_size=500,
+                      seq_length=32, params_dtype="fp32", max_tensor_parallel_size=2, make_vocab_size_divisible_by=8)
+    set_args(Args(model=cfg, train=TrainConfig(micro_batch_size=2, global_batch_size=8, lr=1e-3)))
+    out = {}
+    built = []
+
+    def setup(strategy, is_meta_device=False):
+        built.append((str(strategy), is_meta_device))
+        return TrainingState(strategy, is_meta_device=is_meta_device)
+
+    provided = []
+
+    def provider():
+        provided.append(1)
+        return MockGPTDataset(1 << 20, cfg.seq_length, cfg.vocab_size, seed=99), None, None
+
+    ElasticMegatronManager.register(setup, provider)
+    specs = ["ws2", "ws2-tp2", "ws1"]
+    S = [ParallelStrategy.parse(s) for s in specs]
+    create_all_groups(S)
+    ts = TrainingState(S[0])
+    ts.init_weights(0)
+    mgr = ElasticMegatronManager(specs, training_state=ts, engine="torch")
+
+    # data comes from the registered provider
+    ids, _ = next(iter(mgr.build_iterators(0)[0]))
+    want = MockGPTDataset(1 << 20, cfg.seq_length, cfg.vocab_size, seed=99)[rank * 2][:-1]
+    out["provider"] = bool(provided) and torch.equal(ids[0], want)
+
+    # groups and the host barrier
+    g = mgr.get_data_parallel_group("ws2")
+    out["dp_group"] = g is not None and dist.get_world_size(g) == 2
+    g1 = mgr.get_data_parallel_group("ws1")
+    out["dp_idle"] = (g1 is None) if rank == 1 else True
+    mgr.global_barrier_by_gloo()
+
+    train_step(ts, mgr.build_iterators(0)[0])
+    # meta-device switches there and back: the registered builder makes a meta state, no data moves and the
+    # live state is neither released nor changed
+    before_p, before_o = ts.param_flat.clone(), ts.opt_flat.clone()
+    mgr.reshard("ws2-tp2", is_meta_device=True)
+    out["meta_built"] = ("ws2-tp2-pp1-cp1-dp1-ep1-etp2-inst1-sp", True) in built
+    back = mgr.reshard("ws2", is_meta_device=True)
+    out["live_kept"] = (back is ts and not ts.model_released and torch.equal(ts.param_flat, before_p)
+                        and torch.equal(ts.opt_flat, before_o))
+    mgr.clear_meta_state("ws2-tp2")
+    # a real switch and back: the registered builder builds the cleared state again, for real
+    tp = mgr.reshard("ws2-tp2")
+    out["real_built"] = ("ws2-tp2-pp1-cp1-dp1-ep1-etp2-inst1-sp", False) in built and not tp.is_meta_device
+    back = mgr.reshard("ws2")
+    out["round_trip"] = torch.equal(back.param_flat, before_p) and torch.equal(back.opt_flat, before_o)
+
+    # release returns the arenas to the pool; rebuild takes arenas back (contents are refilled by a switch)
+    tp.release()
+    out["released"] = tp.model_released and tp.optimizer_released and tp.param_arena is None
+    tp.rebuild()
+    out["rebuilt"] = (not tp.model_released) and tp.param_flat.numel() == tp.layout.param_numel
+    tp.release()
+
+    # update_model_weight: parameters regenerated from the fp32 master of each shard, then all-gathered
+    good = back.param_flat.clone()
+    back.param_flat.zero_()
+    back.update_model_weight()
+    out["update_model_weight"] = torch.equal(back.param_flat, good)
+    out["refresh_config"] = back.refresh_config(back.model, back.optimizer) is None
+    ElasticMegatronManager.register(None, None)
+    return out
+
+
+def test_reference_api_entry_points():
+    for res in run_distributed(_api, 2):
+        assert all(res.values()), res
