@@ -198,6 +198,10 @@ class ElasticMegatronManager:
 
     def reshard(self, new_parallel_strategy, logger: Optional[logging.Logger] = None, is_meta_device: bool = False,
                 save_ckpt: bool = False, ckpt_dir: Optional[str] = None) -> Optional[TrainingState]:
+        """Switch to ``new_parallel_strategy``; returns this rank's state under it (None on idle ranks).
+
+        ``logger`` receives the switch's JSON record (default: rank 0 prints it); ``save_ckpt`` writes Megatron
+        checkpoints of both sides into ``<ckpt_dir>/before_reshard`` and ``<ckpt_dir>/after_reshard``."""
         # meta mode (or inside build_nccl_connection_context): build the destination's state and the switch's
         # mappings / task tables, move no data, and leave every live state alone - neither the source is
         # released nor a released state rebuilt (the reference turns release / rebuild into no-ops for its fake
@@ -211,7 +215,9 @@ class ElasticMegatronManager:
         if save_ckpt and src is not None:
             from .checkpoint import save_checkpoint
 
-            save_checkpoint(src, ckpt_dir or "before_reshard")
+            # the reference writes the two sides of a switch to before_reshard / after_reshard (its
+            # convert-and-compare check reads both); ``ckpt_dir`` is the root that holds them
+            save_checkpoint(src, os.path.join(ckpt_dir or ".", "before_reshard"))
         if dst_s == src_s:
             return src
         union = union_ranks(src_s, dst_s)
@@ -279,7 +285,7 @@ class ElasticMegatronManager:
         if save_ckpt and dst is not None:
             from .checkpoint import save_checkpoint
 
-            save_checkpoint(dst, ckpt_dir or "after_reshard")
+            save_checkpoint(dst, os.path.join(ckpt_dir or ".", "after_reshard"))
         return dst
 
     def recover(self, new_parallel_strategy, failed_ranks, logger: Optional[logging.Logger] = None):

@@ -91,3 +91,66 @@ def _api(rank, world):
 def test_reference_api_entry_points():
     for res in run_distributed(_api, 2):
         assert all(res.values()), res
+
+
+def _ckpt_and_logger(rank, world, root):
+    import json
+    import logging
+
+    from elasticmegatron_b200.config import Args, ModelConfig, TrainConfig, get_args, set_args
+    from elasticmegatron_b200.parallel.process_groups import create_all_groups
+    from elasticmegatron_b200.parallel.strategy import ParallelStrategy
+    from elasticmegatron_b200.runtime.manager import ElasticMegatronManager
+    from elasticmegatron_b200.runtime.train import train_step
+    from elasticmegatron_b200.runtime.training_state import TrainingState
+
+    cfg = ModelConfig(num_layers=2, hidden_size=64, num_attention_heads=4, ffn_hidden_size=128, vocab_size=500,
+                      seq_length=32, params_dtype="fp32", max_tensor_parallel_size=2, make_vocab_size_divisible_by=8)
+    set_args(Args(model=cfg, train=TrainConfig(micro_batch_size=2, global_batch_size=8, lr=1e-3)))
+    S = [ParallelStrategy.parse(s) for s in ("ws2", "ws2-tp2")]
+    create_all_groups(S)
+    ts = TrainingState(S[0])
+    ts.init_weights(0)
+    mgr = ElasticMegatronManager(S, training_state=ts, engine="torch")
+    train_step(ts, mgr.build_iterators(0)[0])
+    get_args().iteration = 1
+
+    records = []
+
+    class _Keep(logging.Handler):
+        def emit(self, rec):
+            records.append(rec.getMessage())
+
+    log = logging.getLogger(f"switch-test-{rank}")
+    log.addHandler(_Keep())
+    log.setLevel(logging.INFO)
+    log.propagate = False
+    mgr.reshard("ws2-tp2", logger=log, save_ckpt=True, ckpt_dir=root)
+    rec = [json.loads(m) for m in records if m.startswith("{")]
+    return len(rec) == 1 and rec[0]["event"] == "reshard" and rec[0]["dst"].startswith("ws2-tp2")
+
+
+def test_reshard_saves_both_sides_and_logs_to_the_logger(tmp_path):
+    """``reshard(save_ckpt=True, ckpt_dir=...)`` writes the source layout to before_reshard/ and the destination
+    to after_reshard/; converting the first offline to the destination layout gives the second exactly (the
+    reference's convert-and-compare check).  The switch record goes to the given logger on every rank."""
+    import os
+
+    from elasticmegatron_b200.config import Args, ModelConfig, TrainConfig, set_args
+    from elasticmegatron_b200.parallel.strategy import ParallelStrategy
+    from elasticmegatron_b200.runtime.checkpoint import convert_checkpoint
+    from elasticmegatron_b200.tools.compare_ckpt import compare
+
+    assert all(run_distributed(_ckpt_and_logger, 2, str(tmp_path)))
+    before, after = tmp_path / "before_reshard", tmp_path / "after_reshard"
+    ib = next(d for d in os.listdir(before) if d.startswith("iter_"))
+    ia = next(d for d in os.listdir(after) if d.startswith("iter_"))
+    assert sorted(os.listdir(before / ib)) == ["mp_rank_00"]
+    assert sorted(os.listdir(after / ia)) == ["mp_rank_00", "mp_rank_01"]
+    cfg = ModelConfig(num_layers=2, hidden_size=64, num_attention_heads=4, ffn_hidden_size=128, vocab_size=500,
+                      seq_length=32, params_dtype="fp32", max_tensor_parallel_size=2, make_vocab_size_divisible_by=8)
+    set_args(Args(model=cfg, train=TrainConfig(micro_batch_size=2, global_batch_size=8, lr=1e-3)))
+    conv = tmp_path / "converted"
+    convert_checkpoint(str(before), str(conv), ParallelStrategy.parse("ws2-tp2"))
+    ic = next(d for d in os.listdir(conv) if d.startswith("iter_"))
+    assert compare(str(conv / ic), str(after / ia), 0.0) == []
