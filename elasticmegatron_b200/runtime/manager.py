@@ -57,7 +57,7 @@ class ElasticMegatronManager:
     def __init__(self, parallel_strategy_list: List[Union[Dict, ParallelStrategy, str]], model=None, optimizer=None,
                  opt_param_scheduler=None, send_fn: Optional[Callable] = None, recv_fn: Optional[Callable] = None,
                  broadcast_fn: Optional[Callable] = None, use_p2p_to_collective: Optional[bool] = None,
-                 training_state: Optional[TrainingState] = None, engine: Optional[str] = None, warmup: bool = True):
+                 training_state: Optional[TrainingState] = None, engine: Optional[str] = None):
         """``send_fn`` / ``recv_fn`` / ``broadcast_fn`` / ``use_p2p_to_collective`` keep the reference's
         injectable communicator (elastic_manager.py:41-58): when any is given, switches run the reference's
         transfer schedule through those functions; otherwise ``engine`` picks the transfer engine

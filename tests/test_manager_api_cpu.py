@@ -84,6 +84,10 @@ def _api(rank, world):
     back.update_model_weight()
     out["update_model_weight"] = torch.equal(back.param_flat, good)
     out["refresh_config"] = back.refresh_config(back.model, back.optimizer) is None
+    # the reference's constructor form: the live model (and its optimizer / scheduler) instead of the state
+    m2 = ElasticMegatronManager(specs, model=back.model, optimizer=back.optimizer,
+                                opt_param_scheduler=back.opt_param_scheduler, engine="torch")
+    out["model_ctor"] = m2.training_state is back
     ElasticMegatronManager.register(None, None)
     return out
 
