@@ -227,9 +227,12 @@ class ElasticMegatronManager:
             return None
         ugroup = ProcessGroupPool.get(union)
         same_layout = src_s.layout_key() == dst_s.layout_key()
+        # same layout (the strategies differ only in sequence parallelism): the destination takes over the
+        # source's arenas - nothing is allocated and nothing moves
+        adopt = same_layout and src is not None and not is_meta_device
         t_total = HostTimer(sync=False).__enter__()
         with HostTimer(sync=False) as t_build, nvtx_range("reshard/build"):
-            dst = self._get_or_build(dst_s, is_meta_device)
+            dst = self._get_or_build(dst_s, is_meta_device or adopt)
         if src is not None and src.model_released and not is_meta_device:
             src.rebuild()
         with HostTimer(sync=False) as t_plan, nvtx_range("reshard/plan"):
@@ -237,7 +240,10 @@ class ElasticMegatronManager:
         if self._rank == 0 and os.environ.get("EMB_RESHARD_DEBUG", "0") != "0":
             # per-parameter send / receive plan (the reference's debug print, transfer/transfer.py:271-289)
             print(plan.describe(), flush=True)
-        if is_meta_device:
+        if adopt:
+            dst.adopt(src)
+            ms, nbytes = 0.0, 0
+        elif is_meta_device:
             # meta mode: no data moves; only pre-build state / connections (reference "fake transfer")
             ms, nbytes = 0.0, 0
             if hasattr(self.engine, "warmup"):
@@ -245,7 +251,7 @@ class ElasticMegatronManager:
                     self.engine.warmup(plan, self._rank, src, dst, ugroup)
         else:
             with nvtx_range("reshard/transfer"):
-                ms, nbytes = self._transfer(plan, src, dst, ugroup, same_layout)
+                ms, nbytes = self._transfer(plan, src, dst, ugroup)
         with HostTimer(sync=False) as t_lr, nvtx_range("reshard/lr"):
             self._transfer_lr(src, dst, union)
         with HostTimer(sync=False) as t_rel:
@@ -348,7 +354,7 @@ class ElasticMegatronManager:
             if hasattr(self.engine, "warmup"):
                 self.engine.warmup(plan, self._rank, src_state, dst_state, ugroup)
             return 0.0
-        ms, _ = self._transfer(plan, src_state, dst_state, ugroup, src_s.layout_key() == dst_s.layout_key())
+        ms, _ = self._transfer(plan, src_state, dst_state, ugroup)
         return ms
 
     def redundant_backup(self, src_state: Optional[TrainingState], dst_state: Optional[TrainingState],
@@ -388,7 +394,7 @@ class ElasticMegatronManager:
         return ParallelStrategy.from_any(strategy)
 
     # ------------------------------------------------------------------ internals
-    def _transfer(self, plan, src, dst, ugroup, same_layout: bool):
+    def _transfer(self, plan, src, dst, ugroup):
         eng = self.engine
         if hasattr(eng, "reset_counters"):
             eng.reset_counters()

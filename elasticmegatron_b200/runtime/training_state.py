@@ -126,6 +126,10 @@ class TrainingState:
         if not self.model_released:
             return
         self._alloc_model()
+        self._bind_model_arenas()
+
+    def _bind_model_arenas(self) -> None:
+        """Point the model, DDP and optimizer at the current param / grad arenas."""
         if self.is_meta_device:
             # meta parameters cannot be re-pointed at device memory in place: build the stage and its
             # gradient hooks afresh over the new arenas (the optimizer and scheduler objects survive)
@@ -154,6 +158,23 @@ class TrainingState:
     def release(self):
         self.release_model()
         self.release_optimizer()
+
+    def adopt(self, other: "TrainingState") -> None:
+        """Take over ``other``'s arenas instead of copying them; ``other`` ends released.
+
+        Valid when both layouts are the same (strategies that differ only in sequence parallelism: the layout
+        does not depend on it), so every parameter, gradient and optimizer element already sits at its offset
+        under this strategy."""
+        lo, ls = other.layout, self.layout
+        assert (lo.offset_by_name == ls.offset_by_name and lo.param_numel == ls.param_numel
+                and lo.owned() == ls.owned()), "adopt needs identical layouts"
+        self.release()
+        self.param_arena, self.grad_arena, self.opt_arena = other.param_arena, other.grad_arena, other.opt_arena
+        other.param_arena = other.grad_arena = other.opt_arena = None
+        other.model_released = other.optimizer_released = True
+        self._bind_model_arenas()
+        self.optimizer.bind(self.param_flat, self.grad_flat, self.opt_flat)
+        self.optimizer_released = False
 
     def rebuild(self):
         self.rebuild_model()

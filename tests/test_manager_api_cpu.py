@@ -158,3 +158,42 @@ def test_reshard_saves_both_sides_and_logs_to_the_logger(tmp_path):
     convert_checkpoint(str(before), str(conv), ParallelStrategy.parse("ws2-tp2"))
     ic = next(d for d in os.listdir(conv) if d.startswith("iter_"))
     assert compare(str(conv / ic), str(after / ia), 0.0) == []
+
+
+def _sp_switch(rank, world, specs):
+    from elasticmegatron_b200.config import Args, ModelConfig, TrainConfig, set_args
+    from elasticmegatron_b200.parallel.process_groups import create_all_groups
+    from elasticmegatron_b200.parallel.strategy import ParallelStrategy
+    from elasticmegatron_b200.runtime.manager import ElasticMegatronManager
+    from elasticmegatron_b200.runtime.train import train_step
+    from elasticmegatron_b200.runtime.training_state import TrainingState
+
+    cfg = ModelConfig(num_layers=2, hidden_size=64, num_attention_heads=4, ffn_hidden_size=128, vocab_size=500,
+                      seq_length=32, params_dtype="fp32", max_tensor_parallel_size=2, make_vocab_size_divisible_by=8)
+    set_args(Args(model=cfg, train=TrainConfig(micro_batch_size=2, global_batch_size=8, lr=1e-3)))
+    S = [ParallelStrategy.parse(s) for s in dict.fromkeys(specs)]
+    create_all_groups(S)
+    ts = TrainingState(S[0])
+    ts.init_weights(0)
+    mgr = ElasticMegatronManager(S, training_state=ts, engine="torch")
+    ptr, allocated = ts.param_flat.data_ptr(), ts.pool.allocated_bytes
+    losses, moved, same_arenas = [], [], True
+    for i, s in enumerate(specs):
+        if i and s != specs[i - 1]:
+            ts = mgr.reshard(s)
+            moved.append(mgr.last_switch["gbytes"])
+            same_arenas &= ts.param_flat.data_ptr() == ptr and ts.pool.allocated_bytes == allocated
+        losses.append(train_step(ts, mgr.build_iterators(8 * i)[0])["loss"])
+    return losses, moved, same_arenas
+
+
+def test_sp_only_switch_hands_over_the_arenas():
+    """Strategies that differ only in sequence parallelism share a layout: a switch between them hands the
+    arenas over (no copy, no allocation) and training continues as if nothing happened."""
+    import numpy as np
+
+    base = run_distributed(_sp_switch, 2, ["ws2-tp2"] * 4)
+    sw = run_distributed(_sp_switch, 2, ["ws2-tp2", "ws2-tp2-nosp", "ws2-tp2-nosp", "ws2-tp2"])
+    np.testing.assert_allclose(sw[0][0], base[0][0], rtol=1e-5)
+    for losses, moved, same in sw:
+        assert moved == [0.0, 0.0] and same, (moved, same)
