@@ -54,7 +54,9 @@ def report(model: str, src: str, dst: str, layers=None, link_gbs: float = 770.0,
            "nvlink_bytes": int(m.sum()), "local_bytes": local,
            "max_egress_bytes": int(m.sum(1).max(initial=0)), "max_ingress_bytes": int(m.sum(0).max(initial=0)),
            "roofline_ms": plan.nvlink_roofline_ms(link_gbs, dt, 2), "link_gbs": link_gbs,
-           "bytes_matrix_gb": (m / 1e9).round(3).tolist(), "plan_ms": plan_ms, "tasks_ms_max": tasks_ms}
+           "bytes_matrix_gb": (m / 1e9).round(3).tolist(), "plan_ms": plan_ms, "tasks_ms_max": tasks_ms,
+           # same layout (only SP differs): the manager hands the arenas over instead of running the plan
+           "handover": a.layout_key() == b.layout_key()}
     from ..planner.memory import layout_report, switch_peak_bytes
 
     out["memory_gb"] = {"src": {k: v / 1e9 for k, v in layout_report(cfg, a).items()},
@@ -81,6 +83,9 @@ def main(argv=None) -> int:
           f"busiest GPU sends {r['max_egress_bytes'] / 1e9:.2f} GB / receives {r['max_ingress_bytes'] / 1e9:.2f} GB; "
           f"NVLink roofline {r['roofline_ms']:.2f} ms at {r['link_gbs']:.0f} GB/s; host: plan {r['plan_ms']:.0f} ms, "
           f"task table {r['tasks_ms_max']:.0f} ms (slowest rank)")
+    if r["handover"]:
+        print("same layout (the strategies differ only in sequence parallelism): a switch hands the arenas over; "
+              "nothing is copied")
     mem = r["memory_gb"]
     print(f"per-GPU memory (largest rank): source {mem['src']['peak']:.1f} GB (state {mem['src']['total']:.1f} + "
           f"activations ~{mem['src']['activations']:.1f}), destination {mem['dst']['peak']:.1f} GB; during the "
