@@ -10,7 +10,7 @@ row and plane counts.  A wrong table writes into whatever memory the addresses n
 
 The reference has no equivalent: it issues one blocking NCCL call per (parameter, tensor, peer) and relies
 on the call order (transfer/transfer.py:196-197).  This stands in for a sanitizer's bounds check on the
-transfer, which is closed on this pool.
+transfer where no memory sanitizer can run.
 """
 from __future__ import annotations
 
