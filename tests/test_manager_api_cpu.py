@@ -158,6 +158,11 @@ def test_reshard_saves_both_sides_and_logs_to_the_logger(tmp_path):
     convert_checkpoint(str(before), str(conv), ParallelStrategy.parse("ws2-tp2"))
     ic = next(d for d in os.listdir(conv) if d.startswith("iter_"))
     assert compare(str(conv / ic), str(after / ia), 0.0) == []
+    # the same check through the command line the README gives
+    from elasticmegatron_b200.tools import convert_ckpt
+
+    assert convert_ckpt.main([str(before), str(tmp_path / "cli"), "--world-size", "2", "--tp", "2",
+                              "--compare", str(after)]) == 0
 
 
 def _sp_switch(rank, world, specs):
