@@ -2,6 +2,8 @@
 # Dense Llama-style model, one 8-GPU node, online switches between strategies every 2 iterations.
 # Analogue of the reference's run_e2e_demo.sh (model, seq 4096, MBS 1, GBS 32, ZeRO-1, bf16, mock data).
 #   NPROC=8 MODEL=llama2-7b bash examples/intra_process/run_e2e_demo.sh
+#   MODEL=demo-tiny bash examples/intra_process/run_e2e_demo.sh   # the reference demo's own default model
+#                                                                 # (4 layers, hidden 4096, LayerNorm)
 set -euo pipefail
 HERE="$(cd "$(dirname "${BASH_SOURCE[0]}")" && pwd)"
 NPROC="${NPROC:-8}"
