@@ -352,14 +352,7 @@ __global__ void dq_cast_kernel(const float* __restrict__ dq, __nv_bfloat16* __re
   }
 }
 
-static int* err_flag() {
-  static int* f = nullptr;
-  if (!f) {
-    EMB_CUDA_CHECK(cudaMalloc(&f, sizeof(int)));
-    EMB_CUDA_CHECK(cudaMemset(f, 0, sizeof(int)));
-  }
-  return f;
-}
+static int* err_flag() { return device_err_flag(kErrAttnBwd); }
 
 static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;

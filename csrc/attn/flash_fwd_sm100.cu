@@ -351,14 +351,7 @@ static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   return fn;
 }
 
-static int* err_flag() {
-  static int* f = nullptr;
-  if (!f) {
-    EMB_CUDA_CHECK(cudaMalloc(&f, sizeof(int)));
-    EMB_CUDA_CHECK(cudaMemset(f, 0, sizeof(int)));
-  }
-  return f;
-}
+static int* err_flag() { return device_err_flag(kErrAttnFwd); }
 
 // {d, slot, b, s} view of the fused QKV activation with 128-row x 64-column boxes.
 CUtensorMap qkv_map(const at::Tensor& qkv) {

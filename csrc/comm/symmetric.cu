@@ -50,18 +50,7 @@ __global__ void sym_barrier_kernel(SigPtrs sig, int me, int tp, uint32_t epoch, 
   __syncthreads();
 }
 
-int* comm_err_flag() {
-  static int* f = nullptr;
-  static int dev_of = -1;
-  int dev;
-  cudaGetDevice(&dev);
-  if (!f || dev_of != dev) {
-    EMB_CUDA_CHECK(cudaMalloc(&f, sizeof(int)));
-    EMB_CUDA_CHECK(cudaMemset(f, 0, sizeof(int)));
-    dev_of = dev;
-  }
-  return f;
-}
+int* comm_err_flag() { return device_err_flag(kErrComm); }
 
 }  // namespace
 

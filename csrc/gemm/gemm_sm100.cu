@@ -825,18 +825,7 @@ static CUtensorMap make_map(const void* base, int64_t rows, int64_t cols, int64_
   return m;
 }
 
-static int* err_flag() {
-  static int* f = nullptr;
-  static int dev_of = -1;
-  int dev;
-  cudaGetDevice(&dev);
-  if (!f || dev_of != dev) {
-    EMB_CUDA_CHECK(cudaMalloc(&f, sizeof(int)));
-    EMB_CUDA_CHECK(cudaMemset(f, 0, sizeof(int)));
-    dev_of = dev;
-  }
-  return f;
-}
+static int* err_flag() { return device_err_flag(kErrGemm); }
 
 }  // namespace gk
 

@@ -5,6 +5,7 @@
 #include <cuda_bf16.h>
 #include <cstdint>
 #include <atomic>
+#include <mutex>
 
 #include <c10/cuda/CUDAStream.h>
 #include <ATen/ATen.h>
@@ -23,6 +24,27 @@ inline void count_launch(long long n = 1) { launch_counter().fetch_add(n, std::m
   } while (0)
 
 #define EMB_LAUNCH_CHECK() EMB_CUDA_CHECK(cudaGetLastError())
+
+// Device-side error words of the kernels with bounded waits: one zero-initialised int per (device, slot),
+// allocated on first use on each device and kept until exit, so a timeout or abort code recorded on one
+// device is never dropped when another device becomes current.
+enum ErrSlot { kErrGemm = 0, kErrAttnFwd = 1, kErrAttnBwd = 2, kErrComm = 3, kErrSlots = 8 };
+constexpr int kMaxDevices = 64;
+inline int* device_err_flag(int slot) {
+  static std::mutex mu;
+  static int* flags[kMaxDevices] = {};
+  int dev = 0;
+  EMB_CUDA_CHECK(cudaGetDevice(&dev));
+  TORCH_CHECK(dev >= 0 && dev < kMaxDevices && slot >= 0 && slot < kErrSlots, "device_err_flag: bad device/slot");
+  std::lock_guard<std::mutex> g(mu);
+  if (!flags[dev]) {
+    int* f = nullptr;
+    EMB_CUDA_CHECK(cudaMalloc(&f, kErrSlots * sizeof(int)));
+    EMB_CUDA_CHECK(cudaMemset(f, 0, kErrSlots * sizeof(int)));
+    flags[dev] = f;
+  }
+  return flags[dev] + slot;
+}
 
 inline cudaStream_t cur_stream() { return c10::cuda::getCurrentCUDAStream().stream(); }
 

@@ -12,7 +12,7 @@
 // Contract:
 //   * dy, x: [T, H] bf16 row-major; w: [H] bf16; rstd: [T] fp32 (from the forward pass);
 //     dx: [T, H] bf16 output; dw: [H] fp32 output, overwritten (accumulate == 0) or added to (!= 0).
-//   * H must be a multiple of 8 and at most 32768; the scratch holds grid * H floats with
+//   * T must be at most INT_MAX (2^31 - 1) rows; H must be a multiple of 8 and at most 32768; the scratch holds grid * H floats with
 //     grid = min(T, 2 * SMs, EMB_NOALLOC_SCRATCH_FLOATS / H), so every supported size fits.
 //   * The first call on a device looks up the device address of the scratch array (cudaGetSymbolAddress)
 //     with that device current; make that first call before any stream capture on the device.

@@ -321,6 +321,7 @@ at::Tensor rope_fwd(at::Tensor qkv, at::Tensor cosv, at::Tensor sinv, int64_t nr
 // weight-gradient partials go to a fixed file-scope device array instead of a per-call allocation.
 #include "../include/noalloc.h"
 
+#include <climits>
 #include <cstdio>
 #include <mutex>
 
@@ -329,7 +330,6 @@ namespace {
 
 static __device__ __align__(256) float g_noalloc_scratch[EMB_NOALLOC_SCRATCH_FLOATS];
 
-constexpr int kMaxDevices = 64;
 float* g_scratch_ptr[kMaxDevices] = {nullptr};
 std::mutex g_scratch_mu;
 
@@ -356,9 +356,10 @@ cudaError_t scratch_for_current_device(float** out) {
 extern "C" int emb_rmsnorm_bwd_noalloc(const void* dy, const void* x, const void* w, const float* rstd, void* dx,
                                        float* dw, int64_t T, int64_t H, int accumulate, cudaStream_t stream) {
   using namespace emb;
-  if (T < 0 || H <= 0 || H % 8 != 0 || H > 8 * 4 * 1024 || H > EMB_NOALLOC_SCRATCH_FLOATS) {
+  if (T < 0 || T > INT_MAX || H <= 0 || H % 8 != 0 || H > 8 * 4 * 1024 || H > EMB_NOALLOC_SCRATCH_FLOATS) {
     std::fprintf(stderr,
-                 "emb_rmsnorm_bwd_noalloc: unsupported shape T=%lld H=%lld (need H %% 8 == 0, 0 < H <= 32768)\n",
+                 "emb_rmsnorm_bwd_noalloc: unsupported shape T=%lld H=%lld (need 0 <= T <= INT_MAX, H %% 8 == 0, "
+                 "0 < H <= 32768)\n",
                  (long long)T, (long long)H);
     return EMB_NOALLOC_EBADSIZE;
   }

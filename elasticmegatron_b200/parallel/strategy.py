@@ -62,7 +62,7 @@ class ParallelStrategy:
         assert self.world_size % self.total_model_size == 0
         self.data_parallel_size = self.world_size // self.total_model_size
         if tp == 1 and self.sequence_parallel:
-            raise ValueError("Sequence parallel is not supported with tensor model parallel size 1")
+            raise ValueError("sequence_parallel=True needs tensor_model_parallel_size > 1 (SP splits the sequence over the TP group)")
         if self.sequence_parallel is None:
             self.sequence_parallel = tp > 1
         if self.ranks is None:

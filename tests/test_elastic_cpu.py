@@ -200,6 +200,17 @@ def _ckpt(rank, world, root):
     return bool(ok)
 
 
+def _same_optim(a, b):
+    """Two distrib_optim.pt dicts hold the same keys and bitwise-equal tensors."""
+    import torch
+
+    if isinstance(a, dict):
+        return isinstance(b, dict) and a.keys() == b.keys() and all(_same_optim(a[k], b[k]) for k in a)
+    if isinstance(a, torch.Tensor):
+        return isinstance(b, torch.Tensor) and torch.equal(a, b)
+    return a == b
+
+
 def test_checkpoint_save_a_load_b_equals_live_reshard(tmp_path):
     import os
 
@@ -224,7 +235,7 @@ def test_checkpoint_save_a_load_b_equals_live_reshard(tmp_path):
         for sub in os.listdir(conv / "iter_0000002"):
             a = torch.load(conv / "iter_0000002" / sub / "distrib_optim.pt")
             b = torch.load(tmp_path / f"live_{i}" / "iter_0000002" / sub / "distrib_optim.pt")
-            assert a.keys() == b.keys() and all(torch.equal(a[k], b[k]) for k in a)
+            assert _same_optim(a, b)
 
 
 def _hetero(rank, world, strat_idx, alignment=1, gbs=6, mbs=2, hook=False):
@@ -381,3 +392,60 @@ def test_reference_step_level_api_matches_reshard():
     a = run_distributed(_step_api, 2, False)
     b = run_distributed(_step_api, 2, True)
     np.testing.assert_allclose(a[0], b[0], rtol=1e-7)
+
+
+def _moe_ckpt(rank, world, root):
+    """Save a trained MoE state under EP4, then load it into fresh states under EP4, EP2*TP2 and EP2*PP2: each must
+    equal the live resharded state bit for bit (every expert shard written once, in its own directory)."""
+    import torch
+
+    from elasticmegatron_b200.parallel.process_groups import create_all_groups
+    from elasticmegatron_b200.parallel.strategy import ParallelStrategy
+    from elasticmegatron_b200.runtime.checkpoint import load_checkpoint, save_checkpoint
+    from elasticmegatron_b200.runtime.manager import ElasticMegatronManager
+    from elasticmegatron_b200.runtime.train import train_step
+    from elasticmegatron_b200.runtime.training_state import TrainingState
+
+    _setup(moe=True)
+    S = [ParallelStrategy(**s) for s in MOE4]
+    create_all_groups(S)
+    ts = TrainingState(S[0])
+    ts.init_weights(0)
+    mgr = ElasticMegatronManager(MOE4, training_state=ts, engine="torch")
+    it = mgr.build_iterators(0)[0]
+    train_step(ts, it)
+    train_step(ts, it)
+    save_checkpoint(ts, root, iteration=2, consumed_samples=16)
+    same = TrainingState(S[0])
+    load_checkpoint(same, root)
+    ok = [torch.equal(same.param_flat, ts.param_flat) and torch.equal(same.opt_flat, ts.opt_flat)]
+    for i in (1, 2):
+        live = mgr.reshard(MOE4[i])
+        fresh = TrainingState(S[i])
+        load_checkpoint(fresh, root)
+        ok.append(torch.equal(live.param_flat, fresh.param_flat) and torch.equal(live.opt_flat, fresh.opt_flat))
+    return ok
+
+
+def test_moe_checkpoint_every_expert_shard_round_trips(tmp_path):
+    import os
+
+    import pytest as _pytest
+
+    res = run_distributed(_moe_ckpt, 4, str(tmp_path))
+    assert all(all(r) for r in res), res
+    it = tmp_path / "iter_0000002"
+    assert sorted(os.listdir(it)) == ["mp_rank_00_000", "mp_rank_00_001", "mp_rank_00_002", "mp_rank_00_003"]
+    import torch
+
+    for sub in sorted(os.listdir(it)):
+        opt = torch.load(it / sub / "distrib_optim.pt", weights_only=False)
+        assert opt["buckets_coalesced"] is True and 1 in opt
+        assert (0 in opt) == (sub == "mp_rank_00_000")  # dense state once, with ep 0
+    # a missing expert directory is an error, not silently zero state
+    from elasticmegatron_b200.runtime.checkpoint import read_global_state
+
+    _setup(moe=True)
+    os.rename(it / "mp_rank_00_002", tmp_path / "moved_away")
+    with _pytest.raises(FileNotFoundError, match="mp_rank_00_002"):
+        read_global_state(str(tmp_path), 2)
