@@ -41,6 +41,7 @@ torch::Tensor attn_bwd(torch::Tensor dO, torch::Tensor qkv, torch::Tensor o, tor
                        bool causal);
 int64_t attn_bwd_error_flag();
 int64_t gemm_error_flag();
+std::vector<int64_t> gemm_debug_counters();
 void gemm_rs(torch::Tensor a, torch::Tensor b, bool trans_a, bool trans_b, torch::Tensor peers, int64_t my_slot,
              int64_t rows_per_rank);
 torch::Tensor rs_reduce(torch::Tensor stage, int64_t tp, int64_t rows, int64_t n);
@@ -105,6 +106,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("attn_bwd_error_flag", &attn_bwd_error_flag);
   m.def("attn_error_flag", &attn_error_flag);
   m.def("gemm_error_flag", &gemm_error_flag);
+  m.def("gemm_debug_counters", &gemm_debug_counters);
   m.def("gemm_rs", &gemm_rs);
   m.def("rs_reduce", &rs_reduce);
   m.def("gemm_ag", &gemm_ag);

@@ -22,6 +22,8 @@
 // host checks, and the waiting role stops issuing work (no trap).
 #include <cudaTypedefs.h>
 
+#include <cstdlib>
+
 #include "../include/common.cuh"
 
 namespace emb {
@@ -64,6 +66,24 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* e
   for (uint32_t i = 0; i < WAIT_LIMIT; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
     if (i > 64) __nanosleep(32);
+  }
+  atomicExch(err, code);
+  return false;
+}
+__device__ __forceinline__ uint64_t gtimer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+// Bounded wait for the roles on the main loop's critical path (TMA producer, MMA issuer): polls without
+// __nanosleep, whose wake-up granularity otherwise lands in the producer -> MMA -> commit -> producer ring on
+// every stage.  Gives up after ~4 s of wall clock (read every 4096 polls), recording `code` in *err.
+__device__ __forceinline__ bool mbar_wait_hot(uint64_t* bar, uint32_t parity, int* err, int code) {
+  if (mbar_try_wait(bar, parity)) return true;
+  uint64_t t0 = gtimer_ns();
+  for (uint32_t i = 1;; ++i) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((i & 4095) == 0 && gtimer_ns() - t0 > 4000000000ull) break;
   }
   atomicExch(err, code);
   return false;
@@ -133,6 +153,10 @@ struct Params {
   int* err;
   int split_tail;  // 2-SM kernel: run the last partial wave as 256 x 128 half tiles when they fit in one wave
   int no_store;    // 2-SM kernel, measurement only: read the accumulators but write no output
+  int c_tma;       // 2-SM kernel: C is written (or add-reduced) through the tensor map tmC, one 32-row block per
+                   // epilogue warp and bulk operation (else row by row)
+  int probe;       // 2-SM kernel, measurement only: bit 0 issues no MMAs, bit 1 loads no operands (the
+                   // pipeline's barriers still run), isolating the main loop's feed from its math
   // grouped GEMM (1-SM kernel; MoE experts).  group_mode 1: A rows come in per-group segments padded to BM,
   // group_info[m tile] = group of that tile (-1: skip); B holds every group's matrix stacked along its row
   // coordinate, group g's rows start at g * group_b_stride.  group_mode 2 (weight gradient): group g reduces
@@ -254,7 +278,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         for (int kb = ti.kb0; kb < ti.kb1; ++kb, ++it) {
           const int s = it % STAGES;
           const uint32_t ph = (it / STAGES) & 1;
-          if (!mbar_wait(&empty[s], ph ^ 1, p.err, 1) || *abort_flag) { ok = false; *abort_flag = 1; break; }
+          if (!mbar_wait_hot(&empty[s], ph ^ 1, p.err, 1) || *abort_flag) { ok = false; *abort_flag = 1; break; }
           mbar_expect_tx(&full[s], STAGE_BYTES);
           uint8_t* a_dst = sA + s * A_STAGE_BYTES;
           uint8_t* b_dst = sB + s * B_STAGE_BYTES;
@@ -289,14 +313,14 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         const int buf = local & 1;
         const uint32_t tph = (local >> 1) & 1;
         ++local;
-        if (!mbar_wait(&tempty[buf], tph ^ 1, p.err, 2) || *abort_flag) { ok = false; *abort_flag = 1; break; }
+        if (!mbar_wait_hot(&tempty[buf], tph ^ 1, p.err, 2) || *abort_flag) { ok = false; *abort_flag = 1; break; }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + buf * BN;
         for (int kb = ti.kb0; kb < ti.kb1; ++kb, ++it) {
           const int s = it % STAGES;
           const uint32_t ph = (it / STAGES) & 1;
-          if (!mbar_wait(&full[s], ph, p.err, 3) || *abort_flag) { ok = false; *abort_flag = 1; break; }
-          tc_fence_after();
+          if (!mbar_wait_hot(&full[s], ph, p.err, 3) || *abort_flag) { ok = false; *abort_flag = 1; break; }
+          // (no tcgen05 fence here: the TMA -> MMA hand-off is ordered by the mbarrier alone)
           const uint32_t a_addr = smem_u32(sA + s * A_STAGE_BYTES);
           const uint32_t b_addr = smem_u32(sB + s * B_STAGE_BYTES);
 #pragma unroll
@@ -404,17 +428,41 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 //   tempty[b] - leader only; all 8 epilogue warps of the pair arrive (remote arrive from the peer).
 // TMA loads never use cluster multicast.
 namespace gk2 {
-constexpr int BM = 256, BN = 256, BK = 64, STAGES = 5;
-constexpr int A_HALF = 128 * BK * 2;  // 16 KiB per CTA
-constexpr int B_HALF = 128 * BK * 2;  // 16 KiB per CTA
-constexpr int STAGE_BYTES = A_HALF + B_HALF;
+// Cycle counters of the main-loop roles (probe bit 2, measurement only), read by gemm_debug_counters().
+__device__ unsigned long long g_dbg[16];
+__device__ __forceinline__ unsigned long long clk() {
+  unsigned long long c;
+  asm volatile("mov.u64 %0, %%clock64;" : "=l"(c));
+  return c;
+}
+constexpr int BM = 256, BN = 256;
+// K depth of a pipeline stage: 64 (5 stages of 32 KiB per CTA) or 128 (3 stages of 64 KiB, half as many
+// barrier round trips and MMA-issue loop iterations per unit of tensor work).
+template <int BK_>
+struct Cfg {
+  static constexpr int BK = BK_;
+  static constexpr int STAGES = BK_ == 64 ? 5 : 3;
+  static constexpr int A_HALF = 128 * BK_ * 2;  // per CTA
+  static constexpr int B_HALF = 128 * BK_ * 2;
+  static constexpr int STAGE_BYTES = A_HALF + B_HALF;
+  static constexpr int EPI_BUFS = BK_ == 64 ? 2 : 1;
+};
 constexpr int TMEM_COLS = 512;
 constexpr int NUM_THREADS = 192;
 constexpr int NUM_THREADS_AG = 256;  // + 2 copy warps for the all-gather prologue
 constexpr int AG_UNIT_ROWS = 32;     // rows per pushed unit (one readiness flag each)
 constexpr int EPI_STRIDE = 144;  // 128-byte rows padded to 144 B: a warp's 16-byte writes hit 4-way banks
-constexpr int EPI_BYTES = 2 * 128 * EPI_STRIDE;  // double-buffered epilogue staging
-constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + EPI_BYTES + 1024 + 256;
+// Epilogue staging: two 16 KiB buffers of four 32-row x 128-byte warp blocks (tensor-map path), which also hold
+// EPI_BUFS padded 128-row buffers for the row-by-row path.
+template <int BK_>
+constexpr int epi_bytes() {
+  return Cfg<BK_>::EPI_BUFS * 128 * EPI_STRIDE > 32768 ? Cfg<BK_>::EPI_BUFS * 128 * EPI_STRIDE : 32768;
+}
+template <int BK_>
+constexpr int smem_bytes() {
+  return Cfg<BK_>::STAGES * Cfg<BK_>::STAGE_BYTES + epi_bytes<BK_>() + 1024 + 256;
+}
+static_assert(smem_bytes<64>() <= 232448 && smem_bytes<128>() <= 232448, "2-SM GEMM shared memory");
 
 __device__ __forceinline__ uint32_t cluster_rank() {
   uint32_t r;
@@ -474,10 +522,14 @@ __device__ __forceinline__ bool wait_epoch(const uint32_t* flag, uint32_t epoch,
   return false;
 }
 
-template <bool AG>
+template <bool AG, int BK_>
 __global__ void __launch_bounds__(AG ? NUM_THREADS_AG : NUM_THREADS, 1)
-    gemm2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, gk::Params p) {
+    gemm2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                 const __grid_constant__ CUtensorMap tmC, gk::Params p) {
   using namespace gk;
+  constexpr int BK = BK_, STAGES = Cfg<BK_>::STAGES, A_HALF = Cfg<BK_>::A_HALF, B_HALF = Cfg<BK_>::B_HALF;
+  constexpr int STAGE_BYTES = Cfg<BK_>::STAGE_BYTES, EPI_BUFS = Cfg<BK_>::EPI_BUFS;
+  constexpr int EPI_BYTES = epi_bytes<BK_>();
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
@@ -544,10 +596,12 @@ __global__ void __launch_bounds__(AG ? NUM_THREADS_AG : NUM_THREADS, 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
+  const bool timing = (p.probe & 4) != 0;
   if (warp == 0) {
     if (lane == 0) {
       int it = 0;
       bool ok = true;
+      unsigned long long t_begin = timing ? clk() : 0, t_wait = 0, t_issue = 0;
       for (int u = cluster_id; u < num_units && ok; u += num_clusters) {
         const int t = unit_tile(u), hf = unit_half(u);
         const int m0 = tile_m(t) * BM + 128 * rank;
@@ -567,57 +621,95 @@ __global__ void __launch_bounds__(AG ? NUM_THREADS_AG : NUM_THREADS, 1)
         for (int kb = 0; kb < nk; ++kb, ++it) {
           const int s = it % STAGES;
           const uint32_t ph = (it / STAGES) & 1;
-          if (!mbar_wait(&empty[s], ph ^ 1, p.err, 11) || *abort_flag) { ok = false; *abort_flag = 1; break; }
+          const unsigned long long t0 = timing ? clk() : 0;
+          if (!mbar_wait_hot(&empty[s], ph ^ 1, p.err, 11) || *abort_flag) { ok = false; *abort_flag = 1; break; }
+          const unsigned long long t1 = timing ? clk() : 0;
+          t_wait += t1 - t0;
           const uint32_t bar = mapa(smem_u32(&full[s]), 0);
+          if (p.probe & 2) {
+            if (leader) mbar_arrive(&full[s]);
+            continue;
+          }
           if (leader) mbar_expect_tx(&full[s], 2 * STAGE_BYTES);
           uint8_t* a_dst = sA + s * A_HALF;
           uint8_t* b_dst = sB + s * B_HALF;
           const int k0 = kb * BK;
-          if (!p.a_mn) {
-            tma_load_2d_pair(a_dst, &tmA, bar, k0, m0);
-          } else {
-            tma_load_2d_pair(a_dst, &tmA, bar, m0, k0);
-            tma_load_2d_pair(a_dst + 8192, &tmA, bar, m0 + 64, k0);
+          // K-major: 64-wide K panels of 128 rows, 16 KiB apart.  MN-major: 64-wide M (N) panels of BK K-rows,
+          // BK * 128 bytes apart, each loaded as 64 x 64 boxes.
+#pragma unroll
+          for (int h = 0; h < BK / 64; ++h) {
+            if (!p.a_mn) {
+              tma_load_2d_pair(a_dst + h * 16384, &tmA, bar, k0 + 64 * h, m0);
+            } else {
+              tma_load_2d_pair(a_dst + h * 8192, &tmA, bar, m0, k0 + 64 * h);
+              tma_load_2d_pair(a_dst + BK * 128 + h * 8192, &tmA, bar, m0 + 64, k0 + 64 * h);
+            }
+            if (!p.b_mn) {
+              tma_load_2d_pair(b_dst + h * 16384, &tmB, bar, k0 + 64 * h, n0);
+            } else {
+              tma_load_2d_pair(b_dst + h * 8192, &tmB, bar, n0, k0 + 64 * h);
+              tma_load_2d_pair(b_dst + BK * 128 + h * 8192, &tmB, bar, n0 + 64, k0 + 64 * h);
+            }
           }
-          if (!p.b_mn) {
-            tma_load_2d_pair(b_dst, &tmB, bar, k0, n0);
-          } else {
-            tma_load_2d_pair(b_dst, &tmB, bar, n0, k0);
-            tma_load_2d_pair(b_dst + 8192, &tmB, bar, n0 + 64, k0);
-          }
+          if (timing) t_issue += clk() - t1;
         }
+      }
+      if (timing && leader) {
+        atomicAdd(&g_dbg[4], t_wait);
+        atomicAdd(&g_dbg[5], t_issue);
+        atomicAdd(&g_dbg[6], clk() - t_begin);
       }
     }
   } else if (warp == 1) {
     if (leader && lane == 0) {
       const uint32_t idesc_full = make_idesc2(p.a_mn, p.b_mn);
       const uint32_t idesc_half = make_idesc2(p.a_mn, p.b_mn, BN / 2);
-      const uint32_t a_lbo = p.a_mn ? 8192 : 16, a_step = p.a_mn ? 2048 : 32;
-      const uint32_t b_lbo = p.b_mn ? 8192 : 16, b_step = p.b_mn ? 2048 : 32;
+      // descriptors of stage 0 at k-step 0; a k-step / stage advances the 14-bit start-address field only
+      const uint64_t a_desc0 = smem_desc(smem_u32(sA), p.a_mn ? BK * 128 : 16, 1024);
+      const uint64_t b_desc0 = smem_desc(smem_u32(sB), p.b_mn ? BK * 128 : 16, 1024);
+      auto kstep = [&](bool mn, int k) -> uint32_t {  // byte offset of k-step k (16 deep) inside a stage
+        return mn ? (uint32_t)k * 2048u : (uint32_t)(k >> 2) * 16384u + (uint32_t)(k & 3) * 32u;
+      };
       int it = 0, local = 0;
       bool ok = true;
+      unsigned long long t_begin = timing ? clk() : 0, t_wf = 0, t_is = 0, t_wt = 0, nkb = 0;
       for (int u = cluster_id; u < num_units && ok; u += num_clusters, ++local) {
         const uint32_t idesc = unit_half(u) >= 0 ? idesc_half : idesc_full;
         const int buf = local & 1;
         const uint32_t tph = (local >> 1) & 1;
-        if (!mbar_wait(&tempty[buf], tph ^ 1, p.err, 12) || *abort_flag) { ok = false; *abort_flag = 1; break; }
+        const unsigned long long ta = timing ? clk() : 0;
+        if (!mbar_wait_hot(&tempty[buf], tph ^ 1, p.err, 12) || *abort_flag) { ok = false; *abort_flag = 1; break; }
+        if (timing) t_wt += clk() - ta;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + buf * BN;
         for (int kb = 0; kb < nk; ++kb, ++it) {
           const int s = it % STAGES;
           const uint32_t ph = (it / STAGES) & 1;
-          if (!mbar_wait(&full[s], ph, p.err, 13) || *abort_flag) { ok = false; *abort_flag = 1; break; }
-          tc_fence_after();
-          const uint32_t a_addr = smem_u32(sA + s * A_HALF);
-          const uint32_t b_addr = smem_u32(sB + s * B_HALF);
+          const unsigned long long t0 = timing ? clk() : 0;
+          if (!mbar_wait_hot(&full[s], ph, p.err, 13) || *abort_flag) { ok = false; *abort_flag = 1; break; }
+          const unsigned long long t1 = timing ? clk() : 0;
+          t_wf += t1 - t0;
+          // (no tcgen05 fence here: the TMA -> MMA hand-off is ordered by the mbarrier alone)
+          const uint64_t a_s = a_desc0 + (uint64_t)((s * A_HALF) >> 4);
+          const uint64_t b_s = b_desc0 + (uint64_t)((s * B_HALF) >> 4);
+          if (!(p.probe & 1)) {
 #pragma unroll
-          for (int k = 0; k < BK / 16; ++k) {
-            mma_pair(d_tmem, smem_desc(a_addr + k * a_step, a_lbo, 1024), smem_desc(b_addr + k * b_step, b_lbo, 1024),
-                     idesc, (kb | k) != 0);
+            for (int k = 0; k < BK / 16; ++k) {
+              mma_pair(d_tmem, a_s + (kstep(p.a_mn, k) >> 4), b_s + (kstep(p.b_mn, k) >> 4), idesc, (kb | k) != 0);
+            }
           }
           commit_pair(&empty[s]);
+          if (timing) { t_is += clk() - t1; ++nkb; }
         }
         if (ok) commit_pair(&tfull[buf]);
+      }
+      if (timing) {
+        atomicAdd(&g_dbg[0], t_wf);
+        atomicAdd(&g_dbg[1], t_is);
+        atomicAdd(&g_dbg[2], t_wt);
+        atomicAdd(&g_dbg[3], clk() - t_begin);
+        atomicAdd(&g_dbg[9], nkb);
+        atomicAdd(&g_dbg[10], 1ull);
       }
     }
   } else if (AG && warp >= 6) {
@@ -666,16 +758,77 @@ __global__ void __launch_bounds__(AG ? NUM_THREADS_AG : NUM_THREADS, 1)
     const int row_in_half = quarter * 32 + lane;
     int local = 0;
     uint32_t epi_n = 0;  // bulk groups issued by this thread (selects the staging buffer)
+    unsigned long long e_begin = timing ? clk() : 0, e_wait = 0;
     for (int u = cluster_id; u < num_units; u += num_clusters, ++local) {
       const int t = unit_tile(u), hf = unit_half(u);
       const int buf = local & 1;
       const uint32_t tph = (local >> 1) & 1;
+      const unsigned long long ta = timing ? clk() : 0;
       if (!mbar_wait(&tfull[buf], tph, p.err, 14) || *abort_flag) { *abort_flag = 1; break; }
+      if (timing) e_wait += clk() - ta;
       tc_fence_after();
       const int row = tile_m(t) * BM + 128 * rank + row_in_half;
       const int n0 = tile_n(t) * BN + (hf > 0 ? BN / 2 : 0);
       const int n_chunks = (hf >= 0 ? BN / 2 : BN) / 32;
       const bool row_ok = row < p.M;
+      if (p.c_tma && !p.no_store) {
+        // Each warp stages its 32 rows x 128 bytes (32 fp32 or 64 bf16 columns) in a 128-byte-swizzled block
+        // (16-byte chunk j of row r at chunk j ^ (r & 7): conflict-free writes) and one lane hands the block to
+        // the TMA unit: a tensor store, or an fp32 add-reduction into C for the accumulating weight gradient.
+        // Out-of-range rows / columns are clipped by the tensor map.
+        const int row0 = tile_m(t) * BM + 128 * rank + quarter * 32;
+        const int cols = p.out_fp32 ? 32 : 64;
+        const int steps = (hf >= 0 ? BN / 2 : BN) / cols;
+#pragma unroll 1
+        for (int c = 0; c < steps; ++c) {
+          uint32_t r[64];
+          // (a half tile's MMA ran with N = 128 into columns [0, 128) of the buffer, whichever half it is)
+          const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + buf * BN + c * cols;
+          TMEM_LD_32(taddr, r);
+          if (!p.out_fp32) TMEM_LD_32(taddr + 32, (r + 32));
+          asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+          uint8_t* wbuf = sEpi + (epi_n & 1) * 16384 + quarter * 4096;
+          if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+          __syncwarp();
+          uint8_t* myrow = wbuf + lane * 128;
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            uint4 v;
+            if (p.out_fp32) {
+              v = make_uint4(r[4 * j], r[4 * j + 1], r[4 * j + 2], r[4 * j + 3]);
+            } else {
+              float f[8];
+#pragma unroll
+              for (int q = 0; q < 8; ++q) f[q] = __uint_as_float(r[8 * j + q]);
+              v = pack8(f);
+            }
+            *reinterpret_cast<uint4*>(myrow + ((j ^ (lane & 7)) << 4)) = v;
+          }
+          asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+          __syncwarp();
+          if (lane == 0) {
+            const int x = n0 + c * cols;
+            if (p.accumulate) {
+              asm volatile(
+                  "cp.reduce.async.bulk.tensor.2d.global.shared::cta.add.tile.bulk_group [%0, {%1, %2}], [%3];" ::"l"(
+                      reinterpret_cast<uint64_t>(&tmC)),
+                  "r"(x), "r"(row0), "r"(smem_u32(wbuf))
+                  : "memory");
+            } else {
+              asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];" ::"l"(
+                               reinterpret_cast<uint64_t>(&tmC)),
+                           "r"(x), "r"(row0), "r"(smem_u32(wbuf))
+                           : "memory");
+            }
+            asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+          }
+          ++epi_n;
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) remote_arrive(mapa(smem_u32(&tempty[buf]), 0));
+        continue;
+      }
 #pragma unroll 1
       for (int c = 0; c < n_chunks; ++c) {
         uint32_t r[32];
@@ -706,8 +859,12 @@ __global__ void __launch_bounds__(AG ? NUM_THREADS_AG : NUM_THREADS, 1)
         if (ncols == 32 && ((reinterpret_cast<uintptr_t>(gdst) & 15) == 0)) {
           // stage the row chunk in shared memory and hand it to the bulk-copy engine: a plain store, or an
           // fp32 add-reduction into C (the wgrad accumulate), without the read-modify-write round trip
-          uint8_t* srow = sEpi + (epi_n & 1) * (128 * EPI_STRIDE) + row_in_half * EPI_STRIDE;
-          asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+          uint8_t* srow = sEpi + (epi_n % EPI_BUFS) * (128 * EPI_STRIDE) + row_in_half * EPI_STRIDE;
+          if constexpr (EPI_BUFS == 2) {
+            asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+          } else {
+            asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+          }
           uint32_t bytes;
           if (p.out_fp32) {
 #pragma unroll
@@ -786,6 +943,10 @@ __global__ void __launch_bounds__(AG ? NUM_THREADS_AG : NUM_THREADS, 1)
       if (lane == 0) remote_arrive(mapa(smem_u32(&tempty[buf]), 0));
     }
     asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+    if (timing && leader && warp == 2 && lane == 0) {
+      atomicAdd(&g_dbg[7], e_wait);
+      atomicAdd(&g_dbg[8], clk() - e_begin);
+    }
   }
 
   tc_fence_before();
@@ -828,6 +989,56 @@ static CUtensorMap make_map(const void* base, int64_t rows, int64_t cols, int64_
 static int* err_flag() { return device_err_flag(kErrGemm); }
 
 }  // namespace gk
+
+// Output through a tensor map in the 2-SM kernel (EMB_GEMM_C_TMA=0 selects the row-by-row epilogue).
+static bool c_tma_enabled() {
+  static bool on = [] {
+    const char* e = std::getenv("EMB_GEMM_C_TMA");
+    return !(e && std::atoi(e) == 0);
+  }();
+  return on;
+}
+
+// Stage depth of the 2-SM kernel unless a variant asks otherwise (EMB_GEMM_BK=64 or 128 overrides).
+static int gemm2_default_bk() {
+  static int bk = [] {
+    const char* e = std::getenv("EMB_GEMM_BK");
+    return (e && std::atoi(e) == 64) ? 64 : 128;
+  }();
+  return bk;
+}
+
+namespace gk2 {
+// Launch the 2-SM kernel on `clusters` CTA pairs with stage depth `bk` (64 or 128); sets the kernel's
+// shared-memory limit on each device the first time it is used there.
+template <bool AG>
+static void launch(int bk, const CUtensorMap& tA, const CUtensorMap& tB, const CUtensorMap& tC, const gk::Params& p,
+                   int clusters) {
+  static bool attr_set[2][kMaxDevices] = {};
+  int dev = 0;
+  EMB_CUDA_CHECK(cudaGetDevice(&dev));
+  const int which = bk == 128 ? 1 : 0;
+  auto kern = which ? gemm2_kernel<AG, 128> : gemm2_kernel<AG, 64>;
+  const int smem = which ? smem_bytes<128>() : smem_bytes<64>();
+  if (!attr_set[which][dev]) {
+    EMB_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    attr_set[which][dev] = true;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(2 * clusters, 1, 1);
+  cfg.blockDim = dim3(AG ? NUM_THREADS_AG : NUM_THREADS, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = cur_stream();
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  EMB_CUDA_CHECK(cudaLaunchKernelEx(&cfg, kern, tA, tB, tC, p));
+}
+}  // namespace gk2
 
 static bool ok_2d(const at::Tensor& t) {
   return t.dim() == 2 && t.stride(1) == 1 && t.stride(0) % 8 == 0 && (reinterpret_cast<uintptr_t>(t.data_ptr()) % 16) == 0;
@@ -883,33 +1094,40 @@ at::Tensor gemm_tc(at::Tensor a, at::Tensor b, bool trans_a, bool trans_b, c10::
   const int64_t tiles2 = ((M + 255) / 256) * ((N + 255) / 256);
   // variant: 0 auto, 1 one-SM tiles, 2 two-SM tiles, 3 two-SM tiles without the tail split (for comparison)
   // variant 9: variant 2 without output stores (epilogue cost measurement; the result is not written)
-  const bool pair = variant == 2 || variant == 3 || variant == 9 || (variant <= 0 && tiles2 >= num_sms() / 2);
+  // variants 10 / 11 / 12: variant 9 without MMAs / without operand loads / without either (main-loop probes)
+  // variants 13 / 14: variant 2 / 11 with per-role cycle counters (gemm_debug_counters)
+  // variants 4 / 5: variant 2 with 64-deep / 128-deep stages (variant 2 itself uses the default depth);
+  // variant 15: variant 13 with 128-deep stages
+  const bool pair = (variant >= 2 && variant <= 5) || (variant >= 9 && variant <= 15) ||
+                    (variant <= 0 && tiles2 >= num_sms() / 2);
+  const int bk = variant == 4 ? 64 : (variant == 5 || variant == 15) ? 128
+                 : (variant >= 9 && variant <= 14) ? 64 : gemm2_default_bk();
+  if (variant == 15) variant = 13;
+  if (variant == 4 || variant == 5) variant = 2;
   p.split_tail = variant == 3 ? 0 : 1;
-  p.no_store = variant == 9 ? 1 : 0;
+  p.no_store = (variant >= 9 && variant != 13) ? 1 : 0;
+  p.probe = variant == 13 ? 4 : variant == 14 ? 6 : (variant >= 10 ? variant - 9 : 0);
   if (pair) {
     // 2-SM clusters: each CTA loads a 128-row half of the A tile and of the B tile
     CUtensorMap tA2 = a_mn ? tA : make_map(a.data_ptr(), M, K, a.stride(0), 64, 128);
     CUtensorMap tB2 = b_mn ? tB : make_map(b.data_ptr(), N, K, b.stride(0), 64, 128);
-    static bool attr2 = false;
-    if (!attr2) {
-      EMB_CUDA_CHECK(cudaFuncSetAttribute(gk2::gemm2_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                          gk2::SMEM_BYTES));
-      attr2 = true;
+    // C through a tensor map when its rows are 16-byte aligned: 32-row boxes of 128 bytes, 128-byte swizzle
+    CUtensorMap tC = tA2;
+    const int esz = p.out_fp32 ? 4 : 2;
+    if (((uintptr_t)C.data_ptr() % 16) == 0 && (C.stride(0) * esz) % 16 == 0 && p.no_store == 0) {
+      cuuint64_t dims[2] = {(cuuint64_t)N, (cuuint64_t)M};
+      cuuint64_t strides[1] = {(cuuint64_t)(C.stride(0) * esz)};
+      cuuint32_t box[2] = {(cuuint32_t)(128 / esz), 32};
+      cuuint32_t estr[2] = {1, 1};
+      CUresult r = get_encode()(&tC, p.out_fp32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
+                                C.data_ptr(), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                                CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+      TORCH_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled(C) failed: ", (int)r);
+      p.c_tma = c_tma_enabled() ? 1 : 0;
     }
     const int clusters = (int)std::min<int64_t>(tiles2, num_sms() / 2);
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(2 * clusters, 1, 1);
-    cfg.blockDim = dim3(gk2::NUM_THREADS, 1, 1);
-    cfg.dynamicSmemBytes = gk2::SMEM_BYTES;
-    cfg.stream = cur_stream();
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = 2;
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    EMB_CUDA_CHECK(cudaLaunchKernelEx(&cfg, gk2::gemm2_kernel<false>, tA2, tB2, p));
+    gk2::launch<false>(bk, tA2, tB2, tC, p, clusters);
   } else {
     static bool attr_set = false;
     if (!attr_set) {
@@ -1058,27 +1276,9 @@ void gemm_rs(at::Tensor a, at::Tensor b, bool trans_a, bool trans_b, at::Tensor 
   p.rows_per_rank = (int)rows_per_rank;
   p.my_slot = (int)my_slot;
   for (int64_t i = 0; i < tp; ++i) p.peer_out[i] = reinterpret_cast<void*>(pc.data_ptr<int64_t>()[i]);
-  static bool attr2 = false;
-  if (!attr2) {
-    EMB_CUDA_CHECK(cudaFuncSetAttribute(gk2::gemm2_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                        gk2::SMEM_BYTES));
-    attr2 = true;
-  }
   const int64_t tiles2 = ((M + 255) / 256) * ((N + 255) / 256);
   const int clusters = (int)std::min<int64_t>(tiles2, num_sms() / 2);
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(2 * clusters, 1, 1);
-  cfg.blockDim = dim3(gk2::NUM_THREADS, 1, 1);
-  cfg.dynamicSmemBytes = gk2::SMEM_BYTES;
-  cfg.stream = cur_stream();
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = 2;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  EMB_CUDA_CHECK(cudaLaunchKernelEx(&cfg, gk2::gemm2_kernel<false>, tA, tB, p));
+  gk2::launch<false>(gemm2_default_bk(), tA, tB, tA /* unused */, p, clusters);
   count_launch();
 }
 
@@ -1131,27 +1331,9 @@ at::Tensor gemm_ag(at::Tensor local, at::Tensor b, bool trans_b, at::Tensor peer
     TORCH_CHECK((reinterpret_cast<uintptr_t>(p.ag_dst[i]) & 15) == 0 && (reinterpret_cast<uintptr_t>(p.ag_flags[i]) & 3) == 0,
                 "gemm_ag: misaligned peer buffer");
   }
-  static bool attr = false;
-  if (!attr) {
-    EMB_CUDA_CHECK(cudaFuncSetAttribute(gk2::gemm2_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                        gk2::SMEM_BYTES));
-    attr = true;
-  }
   const int64_t tiles2 = ((M + 255) / 256) * ((N + 255) / 256);
   const int clusters = (int)std::min<int64_t>(tiles2, num_sms() / 2);
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(2 * clusters, 1, 1);
-  cfg.blockDim = dim3(gk2::NUM_THREADS_AG, 1, 1);
-  cfg.dynamicSmemBytes = gk2::SMEM_BYTES;
-  cfg.stream = cur_stream();
-  cudaLaunchAttribute attr2[1];
-  attr2[0].id = cudaLaunchAttributeClusterDimension;
-  attr2[0].val.clusterDim.x = 2;
-  attr2[0].val.clusterDim.y = 1;
-  attr2[0].val.clusterDim.z = 1;
-  cfg.attrs = attr2;
-  cfg.numAttrs = 1;
-  EMB_CUDA_CHECK(cudaLaunchKernelEx(&cfg, gk2::gemm2_kernel<true>, tA, tB, p));
+  gk2::launch<true>(gemm2_default_bk(), tA, tB, tA /* unused */, p, clusters);
   count_launch();
   return C;
 }
@@ -1174,6 +1356,15 @@ int64_t gemm_error_flag() {
   int v = 0;
   EMB_CUDA_CHECK(cudaMemcpy(&v, gk::err_flag(), sizeof(int), cudaMemcpyDeviceToHost));
   return v;
+}
+
+// Role cycle counters of the last timed GEMM launches (variants 13 / 14), then reset.
+std::vector<int64_t> gemm_debug_counters() {
+  unsigned long long h[16];
+  EMB_CUDA_CHECK(cudaMemcpyFromSymbol(h, gk2::g_dbg, sizeof(h)));
+  unsigned long long z[16] = {0};
+  EMB_CUDA_CHECK(cudaMemcpyToSymbol(gk2::g_dbg, z, sizeof(z)));
+  return std::vector<int64_t>(h, h + 16);
 }
 
 void gemm_clear_error() { EMB_CUDA_CHECK(cudaMemset(gk::err_flag(), 0, sizeof(int))); }
