@@ -40,7 +40,7 @@ from ..utils.timers import DeviceTimer, HostTimer, max_over_ranks, nvtx_range
 from .data import DataloaderState
 from .training_state import TrainingState
 
-NVLINK_GBS = 770.0  # measured per-direction peer copy bandwidth between two B200s over NVLink 5
+from ..utils.links import NVLINK_NOMINAL_GBS, measured_link_gbs
 
 
 def default_setup_model_and_optimizer(strategy: ParallelStrategy, is_meta_device: bool = False) -> TrainingState:
@@ -272,14 +272,21 @@ class ElasticMegatronManager:
                              t_total.elapsed], group=ProcessGroupPool.get(union, "gloo")
                             if dist.is_initialized() else None)
         el_param = torch.finfo(get_args().model.torch_dtype).bits // 8
-        roof = plan.nvlink_roofline_ms(NVLINK_GBS, 4, el_param)
+        roof = plan.nvlink_roofline_ms(NVLINK_NOMINAL_GBS, 4, el_param)
+        meas = measured_link_gbs()
+        roof_m = plan.nvlink_roofline_ms(meas, 4, el_param) if meas else None
         links = plan.bytes_matrix(4, el_param)
         np.fill_diagonal(links, 0)
         self.last_switch = {"src": str(src_s), "dst": str(dst_s), "engine": self.engine_name,
                             "transfer_ms": mx[0], "gbytes": mx[1],
                             "bandwidth_gbs": (mx[1] / (mx[0] / 1e3)) if mx[0] > 0 else None,
+                            # roofline: busiest GPU's NVLink bytes per direction at the nominal 900 GB/s, and at
+                            # the peer-copy rate measured in this job (utils/links.py) when there is one
                             "nvlink_roofline_ms": roof,
                             "roofline_frac": (roof / mx[0]) if mx[0] > 0 else None,
+                            "measured_link_gbs": meas,
+                            "nvlink_roofline_ms_measured": roof_m,
+                            "roofline_frac_measured": (roof_m / mx[0]) if (roof_m is not None and mx[0] > 0) else None,
                             "build_ms": mx[2], "plan_ms": mx[3], "lr_ms": mx[4], "release_ms": mx[5],
                             "total_ms": mx[6],
                             # bytes that cross links, per direction: [sender][receiver] in GB, and the busiest GPU

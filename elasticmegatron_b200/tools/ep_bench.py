@@ -12,7 +12,7 @@ rank, weighted sum over the k choices).  The expert MLP itself is left out; the 
   local re-layout into the padded expert layout, and the same three steps back).
 
 Timed with CUDA events on the compute stream after warm-up, MAX over ranks.  Roofline: max over GPUs of the
-bytes that must cross NVLink (rows leaving or entering the GPU, both movements) / 770 GB/s.
+bytes that must cross NVLink (rows leaving or entering the GPU, both movements) / the link rate (nominal 900 GB/s per direction).
 """
 from __future__ import annotations
 
@@ -33,7 +33,7 @@ def main():
     ap.add_argument("--topk", type=int, default=2)
     ap.add_argument("--iters", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
-    ap.add_argument("--link-gbs", type=float, default=770.0)
+    ap.add_argument("--link-gbs", type=float, default=900.0, help="link rate per direction (nominal NVLink 5: 900 GB/s; pass a measured rate to compare)")
     a = ap.parse_args()
     local = int(os.environ.get("LOCAL_RANK", "0"))
     torch.cuda.set_device(local)

@@ -4,7 +4,7 @@
     python -m elasticmegatron_b200.tools.plan_report --model mixtral-8x7b --layers 2 ws8-ep8 ws8-tp2-ep4-etp1 --params
 
 Runs the planner on the host only (no GPU, no processes).  The roofline is max over GPUs of max(egress, ingress)
-bytes that cross NVLink divided by ``--link-gbs`` (default: the measured 770 GB/s per direction of B200 peer
+bytes that cross NVLink divided by ``--link-gbs`` (default: the nominal 900 GB/s per direction of B200 peer
 copies); the JSON line at the end holds the same figures, plus the host cost of a first switch between the
 pair: building the plan (``plan_ms``, layouts not cached) and the slowest rank's transfer task table
 (``tasks_ms_max``, with stand-in addresses).  Later switches between the same pair reuse both.
@@ -18,7 +18,7 @@ import sys
 import numpy as np
 
 
-def report(model: str, src: str, dst: str, layers=None, link_gbs: float = 770.0, params: bool = False,
+def report(model: str, src: str, dst: str, layers=None, link_gbs: float = 900.0, params: bool = False,
            max_params=None) -> dict:
     from ..config import Args, TrainConfig, preset, set_args
     from ..parallel.strategy import ParallelStrategy
@@ -73,7 +73,7 @@ def main(argv=None) -> int:
     ap.add_argument("dst")
     ap.add_argument("--model", default="llama2-7b")
     ap.add_argument("--layers", type=int, default=None)
-    ap.add_argument("--link-gbs", type=float, default=770.0)
+    ap.add_argument("--link-gbs", type=float, default=900.0, help="link rate per direction (nominal NVLink 5: 900 GB/s; pass a measured rate to compare)")
     ap.add_argument("--params", action="store_true", help="also print the per-parameter plan")
     ap.add_argument("--max-params", type=int, default=None)
     a = ap.parse_args(argv)

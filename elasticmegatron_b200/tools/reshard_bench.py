@@ -57,7 +57,7 @@ def main():
     ap.add_argument("--pairs", default="all", help="'all' or a comma list like tp1pp1-tp4pp1")
     ap.add_argument("--alternate", type=int, default=20, help="TP1*DP8 <-> TP4*DP2 switches (0 = skip)")
     ap.add_argument("--iters", type=int, default=3)
-    ap.add_argument("--link-gbs", type=float, default=770.0)
+    ap.add_argument("--link-gbs", type=float, default=900.0, help="link rate per direction (nominal NVLink 5: 900 GB/s; pass a measured rate to compare)")
     ap.add_argument("--out", default=None)
     ap.add_argument("--mode", default="push", choices=["pull", "push"], help="native engine: who runs each copy")
     args = ap.parse_args()

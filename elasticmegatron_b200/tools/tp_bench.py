@@ -11,7 +11,7 @@ compute stream after warm-up, the MAX over ranks of
 * ``nccl``: NCCL ``all_gather_into_tensor`` / ``reduce_scatter_tensor`` around the same tcgen05 GEMM;
 * ``gemm``: the GEMM alone (the compute floor).
 
-The roofline of a fused op is max(FLOPs / measured bf16 GEMM peak, bytes crossing NVLink per GPU / 770 GB/s).
+The roofline of a fused op is max(FLOPs / measured bf16 GEMM peak, bytes crossing NVLink per GPU / the link rate (nominal 900 GB/s per direction)).
 Activations are larger than L2 for the default shapes (tokens = 4096).
 """
 from __future__ import annotations
@@ -48,7 +48,7 @@ def main():
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--peak-tflops", type=float, default=None)
-    ap.add_argument("--link-gbs", type=float, default=770.0)
+    ap.add_argument("--link-gbs", type=float, default=900.0, help="link rate per direction (nominal NVLink 5: 900 GB/s; pass a measured rate to compare)")
     a = ap.parse_args()
 
     local = int(os.environ.get("LOCAL_RANK", "0"))

@@ -101,3 +101,94 @@ def validate_tasks(tasks: np.ndarray, src_regions: List[Region], dst_regions: Li
             errors.append(f"tasks {idx[prev]} and {idx[k]} both write destination byte {s[k]:#x}")
     if errors:
         raise ValueError(f"{len(errors)} invalid transfer task(s):\n  " + "\n  ".join(errors))
+
+
+# ---------------------------------------------------------------------------------------------------- checksums
+_P1, _P2, _P3, _P4 = 0x9E3779B97F4A7C15, 0xC2B2AE3D27D4EB4F, 0x165667B19E3779F9, 0x27D4EB2F165667C5
+_CHUNK = 1 << 22
+
+
+def _wrap64(x: int) -> int:
+    x &= (1 << 64) - 1
+    return x - (1 << 64) if x >= 1 << 63 else x
+
+
+def _piece_sum(arena, piece, tag: int) -> "torch.Tensor":
+    """Sum over one piece of ``bits(value) * w(tag, global row, global col)`` in wrapping int64 arithmetic:
+    exact and independent of summation order, so any layout of the same global state gives the same value."""
+    import torch
+
+    rows, cols = piece.gr1 - piece.gr0, piece.gc1 - piece.gc0
+    ibits = torch.int16 if arena.element_size() == 2 else torch.int32
+    dev = arena.device
+    gc = torch.arange(piece.gc0, piece.gc1, device=dev, dtype=torch.int64) * _wrap64(_P2)
+    total = torch.zeros((), dtype=torch.int64, device=dev)
+    step = max(1, _CHUNK // max(cols, 1))
+    for r0 in range(0, rows, step):
+        r1 = min(rows, r0 + step)
+        blk = arena.as_strided((r1 - r0, cols), (piece.ld, 1), piece.off(piece.gr0 + r0, piece.gc0))
+        b = blk.view(ibits).to(torch.int64)
+        gr = torch.arange(piece.gr0 + r0, piece.gr0 + r1, device=dev, dtype=torch.int64) * _wrap64(_P1)
+        w = gr[:, None] + gc[None, :] + _wrap64(tag * _P3)
+        w = (w ^ (w >> 31)) * _wrap64(_P4)
+        w = w ^ (w >> 29)
+        total += (b * (w | 1)).sum()
+    return total
+
+
+def state_checksum(ts, group=None) -> Tuple[int, int]:
+    """Layout-independent, position-sensitive checksums ``(params, optimizer state)`` of the whole model state
+    of ``ts``'s strategy (a collective over its ranks when ``group`` is given).
+
+    Every global element of every parameter is counted once: from the lowest rank of its first pipeline stage
+    that holds its TP piece, and its fp32 master / exp_avg / exp_avg_sq from the optimizer-instance-0 rank that
+    owns it.  The bits of each value are weighted by a hash of (parameter, plane, global row, global column) and
+    summed with int64 wrap-around, so two strategies holding the same state bit for bit give equal checksums,
+    and a value moved to the wrong place or changed in any bit changes them.  Used after timed switches to
+    check the moved bytes against the planner's index maps (the oracle)."""
+    import torch
+    import torch.distributed as dist
+
+    from ..config import get_args
+    from ..models.spec import stages_of
+    from ..planner.layout import virtual_params
+    from ..planner.plan import _StrategyView
+
+    args = get_args()
+    cfg, tc = args.model, args.train
+    s, r = ts.strategy, ts.rank
+    view = _StrategyView(cfg, s, tc.overlap_grad_reduce, tc.ddp_bucket_size)
+    zc = [s.zero_coords(q) for q in range(s.world_size)]
+    P, O = ts.param_flat, ts.opt_flat
+    acc_p = torch.zeros((), dtype=torch.int64, device=P.device)
+    acc_o = torch.zeros((), dtype=torch.int64, device=P.device)
+    for vp in virtual_params(cfg):
+        hold = view.holders(vp)
+        if r not in hold:
+            continue
+        first = min(stages_of(vp, cfg, s.pipeline_model_parallel_size))
+        if view.coords[r]["pp"] != first:
+            continue
+        tkey = lambda q: (view.coords[q]["etp"] if vp.is_expert else view.coords[q]["tp"]) if vp.tp_dim is not None else 0
+        mine = tkey(r)
+        if min(q for q in hold if view.coords[q]["pp"] == first and tkey(q) == mine) == r:
+            for pc in view.param_pieces(vp, r):
+                acc_p += _piece_sum(P, pc, 4 * vp.index)
+        # optimizer state: one owner per (TP piece, ZeRO shard) among instance-0 ranks (TP-replicated parameters
+        # keep a copy of their sharded state on every TP rank)
+        def okey(q):
+            zq = zc[q]
+            inst = zq["expert_instance"] if vp.is_expert else zq["dense_instance"]
+            return (tkey(q), zq["expert_shard"] if vp.is_expert else zq["dense_shard"]) if inst == 0 else None
+
+        if okey(r) is not None and min(q for q in hold if view.coords[q]["pp"] == first and okey(q) == okey(r)) == r:
+            for pc in view.opt_pieces(vp, r):
+                for plane in range(3):
+                    acc_o += _piece_sum(O[plane], pc, 4 * vp.index + 1 + plane)
+    out = torch.stack([acc_p, acc_o])
+    if group is not None and dist.is_initialized():
+        if dist.get_backend(group) == "nccl" and out.device.type != "cuda":
+            out = out.cuda()
+        dist.all_reduce(out, group=group)
+    a, b = out.tolist()
+    return int(a), int(b)

@@ -449,3 +449,39 @@ def test_moe_checkpoint_every_expert_shard_round_trips(tmp_path):
     os.rename(it / "mp_rank_00_002", tmp_path / "moved_away")
     with _pytest.raises(FileNotFoundError, match="mp_rank_00_002"):
         read_global_state(str(tmp_path), 2)
+
+
+def _checksums(rank, world):
+    from elasticmegatron_b200.parallel.process_groups import ProcessGroupPool, create_all_groups
+    from elasticmegatron_b200.parallel.strategy import ParallelStrategy
+    from elasticmegatron_b200.runtime.manager import ElasticMegatronManager
+    from elasticmegatron_b200.runtime.train import train_step
+    from elasticmegatron_b200.runtime.training_state import TrainingState
+    from elasticmegatron_b200.transfer.validate import state_checksum
+
+    _setup()
+    S = [ParallelStrategy(**s) for s in STRATS[:3]]
+    create_all_groups(S)
+    ts = TrainingState(S[0])
+    ts.init_weights(0)
+    mgr = ElasticMegatronManager(STRATS[:3], training_state=ts, engine="torch")
+    train_step(ts, mgr.build_iterators(0)[0])
+    world_g = ProcessGroupPool.get(list(range(world)))
+    sums = [state_checksum(ts, world_g)]
+    for i in (1, 2, 0):
+        ts = mgr.reshard(STRATS[i])
+        sums.append(state_checksum(ts, world_g))
+    # a single flipped bit in one optimizer value changes the checksum
+    if rank == 1:
+        v = ts.opt_flat.view(-1)[5:6].view(__import__("torch").int32)
+        v ^= 1
+    sums.append(state_checksum(ts, world_g))
+    return sums
+
+
+def test_state_checksum_is_layout_invariant_and_position_sensitive():
+    res = run_distributed(_checksums, 2)
+    sums = res[0]
+    assert res[0] == res[1]
+    assert sums[0] == sums[1] == sums[2] == sums[3], sums
+    assert sums[4][0] == sums[0][0] and sums[4][1] != sums[0][1]
