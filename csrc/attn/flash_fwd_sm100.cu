@@ -5,16 +5,21 @@
 // o [s, b, H, d] bf16 and the per-row log-sum-exp lse [b, H, s] fp32 (natural log of the scaled scores) for
 // the backward pass.
 //
-// One CTA = one (128-row query tile, batch, head); 192 threads:
-//   warp 0      - TMA: Q once (2 boxes of 128 x 64), then K_j and V_j into 2-deep rings;
-//   warp 1      - TMEM owner (512 columns: S0, S1, O) and MMA issuer (one thread):
-//                 S_j = Q K_j^T (M=128, N=128, K=128) into S[j % 2], and O_j = P_j V_j (P from shared memory,
-//                 V as an MN-major operand) one step behind, so S_{j+1} is computed while row j is in softmax;
-//   warps 2..5  - one thread per query row: read S_j from TMEM (two passes: max, then exp2), online-softmax
-//                 statistics in registers, P_j written as bf16 into a 128-byte-swizzled K-major tile (the
-//                 layout the MMA reads), then the previous O tile folded into a 128-float register
-//                 accumulator with its rescale factor.  The final O / l is stored straight from registers.
-// Causal masking only touches the diagonal tile (equal 128 tiles for queries and keys).
+// One CTA = two 128-row query tiles (Q0 = rows [256 p, 256 p + 128), Q1 = the next 128) of one (batch, head);
+// both share every K / V tile the CTA loads.  384 threads:
+//   warp 0        - TMA: Q0 and Q1 once, then K_j and V_j into 2-deep rings;
+//   warp 1        - TMEM owner (512 columns: S0 | S1 | O0 | O1, 128 fp32 columns each) and MMA issuer (one
+//                   thread), in the order  PV0(j), S0(j+1), PV1(j), S1(j+1):  while softmax group 0 works on
+//                   S0(j+1) the tensor core runs tile 1's work and vice versa (ping-pong);
+//   warps 4..7    - softmax group 0 (one thread per row of Q0 = TMEM lane), warps 8..11 - group 1 (Q1):
+//                   read the row of S from TMEM, online max with a lazy rescale (the running max moves only when
+//                   a row's max grows by more than 2^8; then that warp rescales its O rows in TMEM), p = 2^(s*c - m)
+//                   summed in fp32 and written back as packed bf16 INTO the S columns, from where the PV MMA reads
+//                   P as its A operand (tcgen05.mma with A in tensor memory): no shared-memory round trip for P.
+//                   After the last tile the group divides O by the row sum and stores o and lse.
+// Ordering relies on the tensor pipe executing one thread's MMAs in issue order: the commit after S_i(j+1)
+// also covers PV_i(j), so a softmax group that sees S_i(j+1) may rescale O_i, and S_i(j+1) (which overwrites
+// P_i(j)) is issued only after PV_i(j).  Causal masking touches only the diagonal tile of each query tile.
 // All mbarrier waits are bounded (error flag + early exit); no TMA multicast.
 #include <cudaTypedefs.h>
 
@@ -25,8 +30,9 @@ namespace fa {
 
 constexpr int D = 128, BQ = 128, BKV = 128;
 constexpr int TILE_BYTES = 128 * 128 * 2;  // one 128 x 128 bf16 tile = two 16 KiB swizzle panels
-constexpr int SMEM_BYTES = 7 * TILE_BYTES + 1024 + 256;
-constexpr uint32_t WAIT_LIMIT = 1u << 26;
+constexpr int SMEM_BYTES = 6 * TILE_BYTES + 1024 + 256;
+constexpr int NUM_THREADS = 384;
+constexpr float RESCALE_THRESHOLD = 8.0f;  // log2 units: P values stay below 2^8 between rescales
 
 __device__ __forceinline__ uint32_t su32(const void* p) { return static_cast<uint32_t>(__cvta_generic_to_shared(p)); }
 __device__ __forceinline__ void bar_init(uint64_t* b, uint32_t n) {
@@ -38,16 +44,28 @@ __device__ __forceinline__ void bar_expect(uint64_t* b, uint32_t bytes) {
 __device__ __forceinline__ void bar_arrive(uint64_t* b) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(su32(b)) : "memory");
 }
+__device__ __forceinline__ bool bar_try(uint64_t* b, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(su32(b)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+__device__ __forceinline__ uint64_t gtimer() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+// Bounded wait without sleeping (every wait here is on the pipeline's critical path): gives up after ~4 s of
+// wall clock, recording `code` in *err.
 __device__ __forceinline__ bool bar_wait(uint64_t* b, uint32_t parity, int* err, int code) {
-  for (uint32_t i = 0; i < WAIT_LIMIT; ++i) {
-    uint32_t ok;
-    asm volatile(
-        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
-        : "=r"(ok)
-        : "r"(su32(b)), "r"(parity)
-        : "memory");
-    if (ok) return true;
-    if (i > 64) __nanosleep(64);
+  if (bar_try(b, parity)) return true;
+  const uint64_t t0 = gtimer();
+  for (uint32_t i = 1;; ++i) {
+    if (bar_try(b, parity)) return true;
+    if ((i & 4095) == 0 && gtimer() - t0 > 4000000000ull) break;
   }
   atomicExch(err, code);
   return false;
@@ -70,14 +88,26 @@ __host__ __device__ constexpr uint32_t idesc(bool b_mn) {
   return (1u << 4) | (1u << 7) | (1u << 10) | ((b_mn ? 1u : 0u) << 16) | ((uint32_t)(128 >> 3) << 17) |
          ((uint32_t)(128 >> 4) << 24);
 }
-__device__ __forceinline__ void mma(uint32_t d, uint64_t a, uint64_t b, uint32_t id, uint32_t acc) {
+// A and B from shared memory
+__device__ __forceinline__ void mma_ss(uint32_t d, uint64_t a, uint64_t b, uint32_t id, uint32_t acc) {
   asm volatile(
       "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(d),
       "l"(a), "l"(b), "r"(id), "r"(acc));
 }
+// A from tensor memory (128 lanes x 16 bf16 packed in 8 columns), B from shared memory
+__device__ __forceinline__ void mma_ts(uint32_t d, uint32_t a_tmem, uint64_t b, uint32_t id, uint32_t acc) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n}\n" ::"r"(d),
+      "r"(a_tmem), "l"(b), "r"(id), "r"(acc));
+}
 __device__ __forceinline__ void commit(uint64_t* bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(su32(bar))
                : "memory");
+}
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
 }
 
 #define FA_TMEM_LD_32(taddr, r)                                                                                     \
@@ -89,6 +119,28 @@ __device__ __forceinline__ void commit(uint64_t* bar) {
         "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),     \
         "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])                   \
       : "r"(taddr))
+#define FA_TMEM_ST_32(taddr, r)                                                                                     \
+  asm volatile(                                                                                                     \
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18," \
+      "%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),                                     \
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]), \
+      "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]),  \
+      "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]),   \
+      "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])                                                                \
+      : "memory")
+#define FA_TMEM_LD_16(taddr, r)                                                                                     \
+  asm volatile(                                                                                                     \
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"      \
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]), \
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])                    \
+      : "r"(taddr))
+#define FA_TMEM_ST_16(taddr, r)                                                                                     \
+  asm volatile(                                                                                                     \
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"( \
+          taddr),                                                                                                   \
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]), \
+      "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])                                       \
+      : "memory")
 
 struct Params {
   __nv_bfloat16* o;
@@ -99,61 +151,52 @@ struct Params {
   int* err;
 };
 
-// Smem K-major 128 x 128 bf16 tile with 128-byte swizzle: two 64-column panels of 16 KiB.
-__device__ __forceinline__ uint32_t swz_off(int row, int col) {
-  const int panel = col >> 6, c = col & 63;
-  const int g = (c >> 3) ^ (row & 7);
-  return panel * 16384 + row * 128 + g * 16 + (c & 7) * 2;
-}
-
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(NUM_THREADS, 1)
     flash_fwd_kernel(const __grid_constant__ CUtensorMap tm, Params p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* sQ = sm;
-  uint8_t* sK = sm + TILE_BYTES;      // [2]
-  uint8_t* sV = sm + 3 * TILE_BYTES;  // [2]
-  uint8_t* sP = sm + 5 * TILE_BYTES;  // [2]
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + 7 * TILE_BYTES);
-  uint64_t* q_full = bars;
-  uint64_t* k_full = bars + 1;   // [2]
-  uint64_t* k_empty = bars + 3;  // [2]
-  uint64_t* v_full = bars + 5;   // [2]
-  uint64_t* v_empty = bars + 7;  // [2]
-  uint64_t* s_full = bars + 9;   // [2]
-  uint64_t* s_empty = bars + 11; // [2]
-  uint64_t* p_full = bars + 13;  // [2]
-  uint64_t* p_empty = bars + 15; // [2]
-  uint64_t* o_full = bars + 17;
-  uint64_t* o_empty = bars + 18;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 20);
+  uint8_t* sQ = sm;                   // [2]: Q0, Q1
+  uint8_t* sK = sm + 2 * TILE_BYTES;  // [2]
+  uint8_t* sV = sm + 4 * TILE_BYTES;  // [2]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + 6 * TILE_BYTES);
+  uint64_t* q_full = bars;        // [2]
+  uint64_t* k_full = bars + 2;    // [2]
+  uint64_t* k_empty = bars + 4;   // [2]
+  uint64_t* v_full = bars + 6;    // [2]
+  uint64_t* v_empty = bars + 8;   // [2]
+  uint64_t* s_full = bars + 10;   // [2] per query tile
+  uint64_t* p_full = bars + 12;   // [2] per query tile
+  uint64_t* o_final = bars + 14;  // [2] per query tile
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int nq = p.s / BQ;
-  const int qt = nq - 1 - blockIdx.x;  // heavy (late) query tiles first
+  const int npairs = (p.s / BQ + 1) / 2;
+  const int pr = npairs - 1 - (int)blockIdx.y;  // heavy (late) query tiles first
   const int H = p.G * p.hpg;
-  const int bh = blockIdx.y;
+  const int bh = blockIdx.x;
   const int bidx = bh / H, h = bh % H;
   const int g = h / p.hpg, hj = h % p.hpg;
   const int slots = p.hpg + 2;
   const int q_slot = g * slots + hj, k_slot = g * slots + p.hpg, v_slot = g * slots + p.hpg + 1;
-  const int nkv = p.causal ? qt + 1 : p.s / BKV;
+  const int qt0 = 2 * pr, qt1 = 2 * pr + 1;
+  const int nkv = p.s / BKV;
+  const bool has1 = qt1 < nkv;              // an odd tile count leaves the last CTA one query tile
+  const int n0 = p.causal ? qt0 + 1 : nkv;  // KV tiles query tile 0 needs
+  const int n1 = has1 ? (p.causal ? qt1 + 1 : nkv) : 0;  // ... tile 1
+  const int nl = n1 > n0 ? n1 : n0;         // KV tiles the CTA loads
 
   if (threadIdx.x == 0) {
-    bar_init(q_full, 1);
     for (int i = 0; i < 2; ++i) {
+      bar_init(&q_full[i], 1);
       bar_init(&k_full[i], 1);
       bar_init(&k_empty[i], 1);
       bar_init(&v_full[i], 1);
       bar_init(&v_empty[i], 1);
       bar_init(&s_full[i], 1);
-      bar_init(&s_empty[i], 4);
       bar_init(&p_full[i], 4);
-      bar_init(&p_empty[i], 1);
+      bar_init(&o_final[i], 1);
     }
-    bar_init(o_full, 1);
-    bar_init(o_empty, 4);
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tm)) : "memory");
@@ -168,11 +211,15 @@ __global__ void __launch_bounds__(192, 1)
   const uint32_t tmem = *tmem_slot;
 
   if (warp == 0) {
+    // ------------------------------------------------------------------ TMA producer
     if (lane == 0) {
-      bar_expect(q_full, TILE_BYTES);
-      tma4(sQ, &tm, q_full, 0, q_slot, bidx, qt * BQ);
-      tma4(sQ + 16384, &tm, q_full, 64, q_slot, bidx, qt * BQ);
-      for (int j = 0; j < nkv; ++j) {
+      for (int i = 0; i < (has1 ? 2 : 1); ++i) {
+        bar_expect(&q_full[i], TILE_BYTES);
+        const int row = (i ? qt1 : qt0) * BQ;
+        tma4(sQ + i * TILE_BYTES, &tm, &q_full[i], 0, q_slot, bidx, row);
+        tma4(sQ + i * TILE_BYTES + 16384, &tm, &q_full[i], 64, q_slot, bidx, row);
+      }
+      for (int j = 0; j < nl; ++j) {
         const int st = j & 1;
         const uint32_t ph = (j >> 1) & 1;
         if (!bar_wait(&k_empty[st], ph ^ 1, p.err, 21) || *abort_flag) { *abort_flag = 1; break; }
@@ -186,149 +233,173 @@ __global__ void __launch_bounds__(192, 1)
       }
     }
   } else if (warp == 1) {
+    // ------------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       const uint32_t id_qk = idesc(false), id_pv = idesc(true);
-      bool ok = bar_wait(q_full, 0, p.err, 23) && !*abort_flag;
-      const uint32_t q_addr = su32(sQ);
-      auto pv = [&](int jj) -> bool {
-        const int st = jj & 1;
-        const uint32_t ph = (jj >> 1) & 1;
-        if (!bar_wait(&v_full[st], ph, p.err, 24) || !bar_wait(&p_full[st], ph, p.err, 25) ||
-            !bar_wait(o_empty, (jj & 1) ^ 1, p.err, 26) || *abort_flag)
-          return false;
-        fence_after();
-        const uint32_t pa = su32(sP + st * TILE_BYTES), va = su32(sV + st * TILE_BYTES);
-#pragma unroll
-        for (int k = 0; k < 8; ++k) {
-          // A = P (K-major over the key index), B = V as MN-major (rows = keys, 64-wide d panels 16 KiB apart)
-          mma(tmem + 256, desc(pa + (k >> 2) * 16384 + (k & 3) * 32, 16, 1024), desc(va + k * 2048, 16384, 1024),
-              id_pv, k != 0);
-        }
-        commit(&v_empty[st]);
-        commit(&p_empty[st]);
-        commit(o_full);
-        return true;
-      };
-      for (int j = 0; j < nkv && ok; ++j) {
-        const int st = j & 1;
-        const uint32_t ph = (j >> 1) & 1;
-        if (!bar_wait(&k_full[st], ph, p.err, 27) || !bar_wait(&s_empty[st], ph ^ 1, p.err, 28) || *abort_flag) {
-          ok = false;
-          break;
-        }
-        fence_after();
-        const uint32_t ka = su32(sK + st * TILE_BYTES);
+      bool ok = true;
+      // S_i(j) = Q_i K_j^T into columns [128 i, 128 i + 128)
+      auto qk = [&](int i, int j) {
+        const uint32_t qa = su32(sQ + i * TILE_BYTES), ka = su32(sK + (j & 1) * TILE_BYTES);
 #pragma unroll
         for (int k = 0; k < 8; ++k) {
           const uint32_t off = (k >> 2) * 16384 + (k & 3) * 32;
-          mma(tmem + st * 128, desc(q_addr + off, 16, 1024), desc(ka + off, 16, 1024), id_qk, k != 0);
+          mma_ss(tmem + i * 128, desc(qa + off, 16, 1024), desc(ka + off, 16, 1024), id_qk, k != 0);
         }
-        commit(&k_empty[st]);
-        commit(&s_full[st]);
-        if (j >= 1) ok = pv(j - 1);
+        commit(&s_full[i]);
+      };
+      // O_i += P_i(j) V_j: P from the first 64 columns of S_i (packed bf16), V as an MN-major B operand
+      auto pv = [&](int i, int j) {
+        const uint32_t va = su32(sV + (j & 1) * TILE_BYTES);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          mma_ts(tmem + 256 + i * 128, tmem + i * 128 + k * 8, desc(va + k * 2048, 16384, 1024), id_pv,
+                 (j | k) != 0);
+        }
+      };
+      auto wait_k = [&](int j) -> bool {
+        return bar_wait(&k_full[j & 1], (j >> 1) & 1, p.err, 23) && !*abort_flag;
+      };
+      ok = bar_wait(&q_full[0], 0, p.err, 24) && (!has1 || bar_wait(&q_full[1], 0, p.err, 24)) && wait_k(0);
+      if (ok) {
+        fence_after();
+        qk(0, 0);
+        if (has1) qk(1, 0);
+        commit(&k_empty[0]);
       }
-      if (ok) ok = pv(nkv - 1);
-      if (!ok) *abort_flag = 1;
+      for (int j = 0; j < nl && ok; ++j) {
+        const uint32_t ph = j & 1;
+        if (!bar_wait(&v_full[j & 1], (j >> 1) & 1, p.err, 25)) { ok = false; break; }
+        if (j < n0) {
+          if (!bar_wait(&p_full[0], ph, p.err, 26) || *abort_flag) { ok = false; break; }
+          fence_after();
+          pv(0, j);
+          if (j + 1 < n0) {
+            if (!wait_k(j + 1)) { ok = false; break; }
+            qk(0, j + 1);
+          }
+        }
+        if (j < n1) {
+          if (!bar_wait(&p_full[1], ph, p.err, 27) || *abort_flag) { ok = false; break; }
+          fence_after();
+          pv(1, j);
+        }
+        commit(&v_empty[j & 1]);
+        if (j + 1 < nl) {
+          if (!wait_k(j + 1)) { ok = false; break; }
+          if (j + 1 < n1) qk(1, j + 1);
+          commit(&k_empty[(j + 1) & 1]);
+        }
+      }
+      if (ok) {
+        commit(&o_final[0]);
+        if (has1) commit(&o_final[1]);
+      } else {
+        *abort_flag = 1;
+      }
     }
-  } else {
-    // ------------------------------------------------------------------ softmax / correction warps
-    const int quarter = warp & 3;
-    const int row = quarter * 32 + lane;  // row of the query tile == TMEM lane
+  } else if (warp >= 4) {
+    // ------------------------------------------------------------------ softmax groups
+    const int grp = (warp - 4) >> 2;  // query tile
+    const int quarter = warp & 3;     // TMEM lane quarter
+    const int row = quarter * 32 + lane;
+    const int qt = grp ? qt1 : qt0;
+    const int n = grp ? n1 : n0;
+    const bool active = grp == 0 || has1;
     const int qpos = qt * BQ + row;
     const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
-    float oacc[D];
-#pragma unroll
-    for (int i = 0; i < D; ++i) oacc[i] = 0.f;
-    float m = -INFINITY, l = 0.f, alpha_prev = 1.f;
+    const uint32_t s_cols = tmem + lane_base + grp * 128;
+    const uint32_t o_cols = tmem + lane_base + 256 + grp * 128;
+    const float c = p.scale_log2;
+    float m_run = -INFINITY, l = 0.f;
     bool ok = true;
-    auto correct = [&](int jj, float alpha) -> bool {
-      if (!bar_wait(o_full, jj & 1, p.err, 31) || *abort_flag) return false;
-      fence_after();
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        uint32_t r[32];
-        FA_TMEM_LD_32(tmem + lane_base + 256 + c * 32, r);
-        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-        for (int i = 0; i < 32; ++i) oacc[c * 32 + i] = oacc[c * 32 + i] * alpha + __uint_as_float(r[i]);
-      }
-      fence_before();
-      __syncwarp();
-      if (lane == 0) bar_arrive(o_empty);
-      return true;
-    };
-    for (int j = 0; j < nkv; ++j) {
-      const int st = j & 1;
-      const uint32_t ph = (j >> 1) & 1;
-      if (!bar_wait(&s_full[st], ph, p.err, 32) || *abort_flag) { ok = false; break; }
+    for (int j = 0; j < n; ++j) {
+      if (!bar_wait(&s_full[grp], j & 1, p.err, 31) || *abort_flag) { ok = false; break; }
       fence_after();
       const bool diag = p.causal && j == qt;
-      const uint32_t sbase = tmem + lane_base + st * 128;
-      // pass 1: row max
-      float mx = -INFINITY;
+      uint32_t r[128];
+      FA_TMEM_LD_32(s_cols, r);
+      FA_TMEM_LD_32(s_cols + 32, (r + 32));
+      FA_TMEM_LD_32(s_cols + 64, (r + 64));
+      FA_TMEM_LD_32(s_cols + 96, (r + 96));
+      asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+      if (diag) {
+        const int lim = qpos - j * BKV;  // keys with index > lim are masked
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        uint32_t r[32];
-        FA_TMEM_LD_32(sbase + c * 32, r);
-        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const int kpos = j * BKV + c * 32 + i;
-          const float v = (diag && kpos > qpos) ? -INFINITY : __uint_as_float(r[i]) * p.scale_log2;
-          mx = fmaxf(mx, v);
-        }
+        for (int i = 0; i < 128; ++i)
+          if (i > lim) r[i] = __float_as_uint(-INFINITY);
       }
-      const float m_new = fmaxf(m, mx);
-      const float alpha = exp2f(m - m_new);
-      // P buffer of this stage must have been consumed by the PV MMA two tiles ago
-      if (!bar_wait(&p_empty[st], ph ^ 1, p.err, 33) || *abort_flag) { ok = false; break; }
-      uint8_t* pbuf = sP + st * TILE_BYTES;
+      float mx = __uint_as_float(r[0]);
+#pragma unroll
+      for (int i = 1; i < 128; ++i) mx = fmaxf(mx, __uint_as_float(r[i]));
+      const float m_new = mx * c;
+      // lazy rescale: keep the running max unless this row's max grew by more than the threshold
+      const bool need = m_new > m_run + RESCALE_THRESHOLD;
+      if (j > 0 && __any_sync(0xffffffffu, need)) {
+        // PV_grp(j - 1) has completed: it was issued before S_grp(j), whose commit we just waited on
+        const float alpha = need ? ex2(m_run - m_new) : 1.f;
+#pragma unroll 1
+        for (int q8 = 0; q8 < 8; ++q8) {
+          uint32_t o[16];
+          FA_TMEM_LD_16(o_cols + q8 * 16, o);
+          asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+          for (int i = 0; i < 16; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+          FA_TMEM_ST_16(o_cols + q8 * 16, o);
+        }
+        asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+        if (need) {
+          l *= alpha;
+          m_run = m_new;
+        }
+      } else if (need) {
+        m_run = m_new;  // first tile (O is not read by PV(0)) or no rescale needed in this warp
+        l = 0.f;
+      }
+      // p = 2^(s c - m), row sum, packed bf16 pairs into the first 64 columns of S (the PV MMA's A operand)
+      const float nm = -m_run;
       float sum = 0.f;
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        uint32_t r[32];
-        FA_TMEM_LD_32(sbase + c * 32, r);
-        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-        float pv[32];
+      for (int h2 = 0; h2 < 4; ++h2) {
+        uint32_t pk[16];
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const int kpos = j * BKV + c * 32 + i;
-          const float v = (diag && kpos > qpos) ? -INFINITY : __uint_as_float(r[i]) * p.scale_log2;
-          pv[i] = exp2f(v - m_new);
-          sum += pv[i];
+        for (int i = 0; i < 16; ++i) {
+          const float a = ex2(fmaf(__uint_as_float(r[h2 * 32 + 2 * i]), c, nm));
+          const float b2 = ex2(fmaf(__uint_as_float(r[h2 * 32 + 2 * i + 1]), c, nm));
+          sum += a + b2;
+          __nv_bfloat162 v2 = __floats2bfloat162_rn(a, b2);
+          pk[i] = *reinterpret_cast<uint32_t*>(&v2);
         }
-#pragma unroll
-        for (int v8 = 0; v8 < 4; ++v8) {
-          *reinterpret_cast<uint4*>(pbuf + swz_off(row, c * 32 + v8 * 8)) = pack8(pv + v8 * 8);
-        }
+        FA_TMEM_ST_16(s_cols + h2 * 16, pk);
       }
+      l += sum;
+      asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
       fence_before();
       __syncwarp();
-      if (lane == 0) bar_arrive(&s_empty[st]);
-      // make the generic-proxy writes of P visible to the tensor core before signalling the MMA warp
-      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-      __syncwarp();
-      if (lane == 0) bar_arrive(&p_full[st]);
-      l = l * alpha + sum;
-      m = m_new;
-      if (j >= 1) {
-        if (!correct(j - 1, alpha_prev)) { ok = false; break; }
-      }
-      alpha_prev = alpha;
+      if (lane == 0) bar_arrive(&p_full[grp]);
     }
-    if (ok) ok = correct(nkv - 1, alpha_prev);
-    if (!ok) *abort_flag = 1;
-    if (ok) {
+    if (ok && active) ok = bar_wait(&o_final[grp], 0, p.err, 32) && !*abort_flag;
+    if (!active) {
+      // no second query tile in this CTA
+    } else if (!ok) {
+      *abort_flag = 1;
+    } else {
+      fence_after();
       const float inv = 1.f / l;
       __nv_bfloat16* dst = p.o + (((size_t)qpos * p.b + bidx) * H + h) * D;
+#pragma unroll 1
+      for (int q4 = 0; q4 < 4; ++q4) {
+        uint32_t o[32];
+        FA_TMEM_LD_32(o_cols + q4 * 32, o);
+        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
-      for (int v8 = 0; v8 < D / 8; ++v8) {
-        float f[8];
+        for (int v8 = 0; v8 < 4; ++v8) {
+          float f[8];
 #pragma unroll
-        for (int i = 0; i < 8; ++i) f[i] = oacc[v8 * 8 + i] * inv;
-        reinterpret_cast<uint4*>(dst)[v8] = pack8(f);
+          for (int i = 0; i < 8; ++i) f[i] = __uint_as_float(o[v8 * 8 + i]) * inv;
+          reinterpret_cast<uint4*>(dst + q4 * 32)[v8] = pack8(f);
+        }
       }
-      p.lse[((size_t)bidx * H + h) * p.s + qpos] = (m + log2f(l)) * 0.6931471805599453f;
+      p.lse[((size_t)bidx * H + h) * p.s + qpos] = (m_run + __log2f(l)) * 0.6931471805599453f;
     }
   }
   fence_before();
@@ -396,13 +467,15 @@ std::vector<at::Tensor> attn_fwd(at::Tensor qkv, int64_t hpg, bool causal) {
   p.scale_log2 = (float)(1.4426950408889634 / std::sqrt((double)D));
   p.causal = causal ? 1 : 0;
   p.err = err_flag();
-  static bool attr = false;
-  if (!attr) {
+  static bool attr[kMaxDevices] = {};
+  int dev = 0;
+  EMB_CUDA_CHECK(cudaGetDevice(&dev));
+  if (!attr[dev]) {
     EMB_CUDA_CHECK(cudaFuncSetAttribute(flash_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
-    attr = true;
+    attr[dev] = true;
   }
-  dim3 grid((unsigned)(s / BQ), (unsigned)(b * H));
-  flash_fwd_kernel<<<grid, 192, SMEM_BYTES, cur_stream()>>>(m, p);
+  dim3 grid((unsigned)(b * H), (unsigned)((s / BQ + 1) / 2));
+  flash_fwd_kernel<<<grid, NUM_THREADS, SMEM_BYTES, cur_stream()>>>(m, p);
   EMB_LAUNCH_CHECK();
   count_launch();
   return {o, lse};
