@@ -6,12 +6,13 @@
 // the backward pass.
 //
 // One CTA = two 128-row query tiles (Q0 = rows [256 p, 256 p + 128), Q1 = the next 128) of one (batch, head);
-// both share every K / V tile the CTA loads.  384 threads:
+// both share every K / V tile the CTA loads.  320 threads (10 warps):
 //   warp 0        - TMA: Q0 and Q1 once, then K_j and V_j into 2-deep rings;
 //   warp 1        - TMEM owner (512 columns: S0 | S1 | O0 | O1, 128 fp32 columns each) and MMA issuer (one
 //                   thread), in the order  PV0(j), S0(j+1), PV1(j), S1(j+1):  while softmax group 0 works on
 //                   S0(j+1) the tensor core runs tile 1's work and vice versa (ping-pong);
-//   warps 4..7    - softmax group 0 (one thread per row of Q0 = TMEM lane), warps 8..11 - group 1 (Q1):
+//   warps 2..5    - softmax group 0 (one thread per row of Q0 = TMEM lane; warp w reads lane quarter w % 4),
+//   warps 6..9    - softmax group 1 (Q1):
 //                   read the row of S from TMEM, online max with a lazy rescale (the running max moves only when
 //                   a row's max grows by more than 2^8; then that warp rescales its O rows in TMEM), p = 2^(s*c - m)
 //                   summed in fp32 and written back as packed bf16 INTO the S columns, from where the PV MMA reads
@@ -23,6 +24,8 @@
 // All mbarrier waits are bounded (error flag + early exit); no TMA multicast.
 #include <cudaTypedefs.h>
 
+#include <cstdlib>
+
 #include "../include/common.cuh"
 
 namespace emb {
@@ -31,7 +34,7 @@ namespace fa {
 constexpr int D = 128, BQ = 128, BKV = 128;
 constexpr int TILE_BYTES = 128 * 128 * 2;  // one 128 x 128 bf16 tile = two 16 KiB swizzle panels
 constexpr int SMEM_BYTES = 6 * TILE_BYTES + 1024 + 256;
-constexpr int NUM_THREADS = 384;
+constexpr int NUM_THREADS = 320;
 constexpr float RESCALE_THRESHOLD = 8.0f;  // log2 units: P values stay below 2^8 between rescales
 
 __device__ __forceinline__ uint32_t su32(const void* p) { return static_cast<uint32_t>(__cvta_generic_to_shared(p)); }
@@ -109,6 +112,70 @@ __device__ __forceinline__ float ex2(float x) {
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
 }
+// 2^x on the FMA pipe, for a share of the softmax exponentials (the MUFU unit alone would be as busy as the
+// tensor core).  Range reduction x = j + f with j = round(x) taken from the float adder (adding 1.5 * 2^23
+// leaves round(x) in the low mantissa bits), f in [-1/2, 1/2]; 2^f by a cubic whose coefficients are a
+// relative-error least-squares fit of 2^f on Chebyshev nodes of [-1/2, 1/2] computed for this kernel (max
+// relative error 7.5e-5 in fp32, below the bf16 rounding of P); 2^j is added to the exponent field.  Inputs
+// below -125 are clamped (their result, < 2^-124, is negligible next to the row maximum's 1, and the
+// exponent field stays >= 1).
+__device__ __forceinline__ float ex2_poly(float x) {
+  x = fmaxf(x, -125.f);
+  const float t = x + 12582912.f;  // 1.5 * 2^23
+  const float f = x - (t - 12582912.f);
+  float q = fmaf(0.0551716648042202f, f, 0.2426111251115799f);
+  q = fmaf(q, f, 0.6932609677314758f);
+  q = fmaf(q, f, 0.9999280571937561f);
+  return __int_as_float(__float_as_int(q) + (__float_as_int(t) << 23));
+}
+
+// Packed fp32 pairs (one 64-bit register) for the f32x2 instructions of sm_100: half the issue slots of
+// scalar arithmetic in the softmax, whose instruction count bounds how quickly it hands P to the tensor core.
+__device__ __forceinline__ uint64_t pk2(float a, float b) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+  return r;
+}
+__device__ __forceinline__ void up2(uint64_t v, float& a, float& b) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(v));
+}
+__device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ uint64_t add2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ uint64_t sub2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("sub.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ float max3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+// ex2_poly on a packed pair (same method and coefficients)
+__device__ __forceinline__ uint64_t ex2_poly2(uint64_t x2) {
+  float x0, x1;
+  up2(x2, x0, x1);
+  x2 = pk2(fmaxf(x0, -125.f), fmaxf(x1, -125.f));
+  const uint64_t magic = pk2(12582912.f, 12582912.f);
+  const uint64_t t = add2(x2, magic);
+  const uint64_t f = sub2(x2, sub2(t, magic));
+  uint64_t q = fma2(pk2(0.0551716648042202f, 0.0551716648042202f), f, pk2(0.2426111251115799f, 0.2426111251115799f));
+  q = fma2(q, f, pk2(0.6932609677314758f, 0.6932609677314758f));
+  q = fma2(q, f, pk2(0.9999280571937561f, 0.9999280571937561f));
+  float q0, q1, t0, t1;
+  up2(q, q0, q1);
+  up2(t, t0, t1);
+  return pk2(__int_as_float(__float_as_int(q0) + (__float_as_int(t0) << 23)),
+             __int_as_float(__float_as_int(q1) + (__float_as_int(t1) << 23)));
+}
 
 #define FA_TMEM_LD_32(taddr, r)                                                                                     \
   asm volatile(                                                                                                     \
@@ -142,6 +209,8 @@ __device__ __forceinline__ float ex2(float x) {
       "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])                                       \
       : "memory")
 
+static_assert(SMEM_BYTES <= 232448, "flash_fwd_kernel shared memory above the 227 KiB per-block limit");
+
 struct Params {
   __nv_bfloat16* o;
   float* lse;
@@ -149,7 +218,14 @@ struct Params {
   float scale_log2;  // softmax scale * log2(e)
   int causal;
   int* err;
+  int timing;  // measurement only: accumulate per-role cycle counters into g_fa_dbg
 };
+__device__ unsigned long long g_fa_dbg[16];
+__device__ __forceinline__ unsigned long long clk64() {
+  unsigned long long c;
+  asm volatile("mov.u64 %0, %%clock64;" : "=l"(c));
+  return c;
+}
 
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     flash_fwd_kernel(const __grid_constant__ CUtensorMap tm, Params p) {
@@ -237,24 +313,33 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     if (lane == 0) {
       const uint32_t id_qk = idesc(false), id_pv = idesc(true);
       bool ok = true;
+      unsigned long long t_v = 0, t_p = 0, t_start = p.timing ? clk64() : 0;
       // S_i(j) = Q_i K_j^T into columns [128 i, 128 i + 128)
+      // Descriptors are built once; a k-step (or stage) only adds to the 14-bit start-address field, which never
+      // carries (shared-memory offsets < 2^18 bytes).  K-major Q / K tiles: k-step k at panel k / 4, 32 bytes
+      // per step inside the 128-byte swizzle row; MN-major V: 16 key rows (2048 bytes) per step.
+      const uint64_t q_d0 = desc(su32(sQ), 16, 1024);
+      const uint64_t k_d0 = desc(su32(sK), 16, 1024);
+      const uint64_t v_d0 = desc(su32(sV), 16384, 1024);
+      constexpr uint32_t TILE16 = TILE_BYTES >> 4;
       auto qk = [&](int i, int j) {
-        const uint32_t qa = su32(sQ + i * TILE_BYTES), ka = su32(sK + (j & 1) * TILE_BYTES);
+        const uint64_t qd = q_d0 + (uint64_t)(i * TILE16), kd = k_d0 + (uint64_t)((j & 1) * TILE16);
+        const uint32_t d = tmem + i * 128;
+        mma_ss(d, qd, kd, id_qk, 0);
 #pragma unroll
-        for (int k = 0; k < 8; ++k) {
-          const uint32_t off = (k >> 2) * 16384 + (k & 3) * 32;
-          mma_ss(tmem + i * 128, desc(qa + off, 16, 1024), desc(ka + off, 16, 1024), id_qk, k != 0);
+        for (int k = 1; k < 8; ++k) {
+          const uint32_t off = (k >> 2) * 1024 + (k & 3) * 2;
+          mma_ss(d, qd + off, kd + off, id_qk, 1);
         }
         commit(&s_full[i]);
       };
       // O_i += P_i(j) V_j: P from the first 64 columns of S_i (packed bf16), V as an MN-major B operand
       auto pv = [&](int i, int j) {
-        const uint32_t va = su32(sV + (j & 1) * TILE_BYTES);
+        const uint64_t vd = v_d0 + (uint64_t)((j & 1) * TILE16);
+        const uint32_t d = tmem + 256 + i * 128, a = tmem + i * 128;
+        mma_ts(d, a, vd, id_pv, j != 0);
 #pragma unroll
-        for (int k = 0; k < 8; ++k) {
-          mma_ts(tmem + 256 + i * 128, tmem + i * 128 + k * 8, desc(va + k * 2048, 16384, 1024), id_pv,
-                 (j | k) != 0);
-        }
+        for (int k = 1; k < 8; ++k) mma_ts(d, a + k * 8, vd + k * 128, id_pv, 1);
       };
       auto wait_k = [&](int j) -> bool {
         return bar_wait(&k_full[j & 1], (j >> 1) & 1, p.err, 23) && !*abort_flag;
@@ -268,9 +353,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       }
       for (int j = 0; j < nl && ok; ++j) {
         const uint32_t ph = j & 1;
+        unsigned long long t0 = p.timing ? clk64() : 0;
         if (!bar_wait(&v_full[j & 1], (j >> 1) & 1, p.err, 25)) { ok = false; break; }
+        if (p.timing) { const unsigned long long t1 = clk64(); t_v += t1 - t0; t0 = t1; }
         if (j < n0) {
           if (!bar_wait(&p_full[0], ph, p.err, 26) || *abort_flag) { ok = false; break; }
+          if (p.timing) { const unsigned long long t1 = clk64(); t_p += t1 - t0; t0 = t1; }
           fence_after();
           pv(0, j);
           if (j + 1 < n0) {
@@ -279,7 +367,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           }
         }
         if (j < n1) {
+          if (p.timing) t0 = clk64();
           if (!bar_wait(&p_full[1], ph, p.err, 27) || *abort_flag) { ok = false; break; }
+          if (p.timing) t_p += clk64() - t0;
           fence_after();
           pv(1, j);
         }
@@ -290,6 +380,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           commit(&k_empty[(j + 1) & 1]);
         }
       }
+      if (p.timing) {
+        atomicAdd(&g_fa_dbg[0], t_v);
+        atomicAdd(&g_fa_dbg[1], t_p);
+        atomicAdd(&g_fa_dbg[2], clk64() - t_start);
+        atomicAdd(&g_fa_dbg[3], 1ull);
+      }
       if (ok) {
         commit(&o_final[0]);
         if (has1) commit(&o_final[1]);
@@ -297,9 +393,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         *abort_flag = 1;
       }
     }
-  } else if (warp >= 4) {
+  } else if (warp >= 2) {
     // ------------------------------------------------------------------ softmax groups
-    const int grp = (warp - 4) >> 2;  // query tile
+    const int grp = (warp - 2) >> 2;  // query tile
     const int quarter = warp & 3;     // TMEM lane quarter
     const int row = quarter * 32 + lane;
     const int qt = grp ? qt1 : qt0;
@@ -312,8 +408,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     const float c = p.scale_log2;
     float m_run = -INFINITY, l = 0.f;
     bool ok = true;
+    unsigned long long sw_wait = 0, sw_work = 0, sw_max = 0, sw_resc = 0, sw_exp = 0;
     for (int j = 0; j < n; ++j) {
+      const unsigned long long ta = p.timing ? clk64() : 0;
       if (!bar_wait(&s_full[grp], j & 1, p.err, 31) || *abort_flag) { ok = false; break; }
+      const unsigned long long tb = p.timing ? clk64() : 0;
+      sw_wait += tb - ta;
       fence_after();
       const bool diag = p.causal && j == qt;
       uint32_t r[128];
@@ -328,13 +428,21 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         for (int i = 0; i < 128; ++i)
           if (i > lim) r[i] = __float_as_uint(-INFINITY);
       }
-      float mx = __uint_as_float(r[0]);
+      float mx4[4];
 #pragma unroll
-      for (int i = 1; i < 128; ++i) mx = fmaxf(mx, __uint_as_float(r[i]));
+      for (int k = 0; k < 4; ++k) mx4[k] = fmaxf(__uint_as_float(r[2 * k]), __uint_as_float(r[2 * k + 1]));
+#pragma unroll
+      for (int i = 8; i < 128; i += 2) {
+        mx4[(i >> 1) & 3] = max3(mx4[(i >> 1) & 3], __uint_as_float(r[i]), __uint_as_float(r[i + 1]));
+      }
+      const float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
       const float m_new = mx * c;
+      const unsigned long long tmx = p.timing ? clk64() : 0;
+      if (p.timing) sw_max += tmx - tb;
       // lazy rescale: keep the running max unless this row's max grew by more than the threshold
       const bool need = m_new > m_run + RESCALE_THRESHOLD;
       if (j > 0 && __any_sync(0xffffffffu, need)) {
+        if (p.timing && lane == 0) atomicAdd(&g_fa_dbg[7], 1ull);
         // PV_grp(j - 1) has completed: it was issued before S_grp(j), whose commit we just waited on
         const float alpha = need ? ex2(m_run - m_new) : 1.f;
 #pragma unroll 1
@@ -355,27 +463,67 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         m_run = m_new;  // first tile (O is not read by PV(0)) or no rescale needed in this warp
         l = 0.f;
       }
-      // p = 2^(s c - m), row sum, packed bf16 pairs into the first 64 columns of S (the PV MMA's A operand)
-      const float nm = -m_run;
-      float sum = 0.f;
+      // Row sum in fp32, P packed to bf16 pairs into the first 64 columns of S (the PV MMA's A operand).
+      const unsigned long long tex = p.timing ? clk64() : 0;
+      if (p.timing) sw_resc += tex - tmx;
+      const uint64_t cc = pk2(c, c), nmm = pk2(-m_run, -m_run);
+      uint64_t sum2[2] = {0ull, 0ull};
+      // S is read again from TMEM one 32-column chunk at a time (the row held whole only for the max), so the
+      // exponent pass needs few registers; P chunk h2 goes to columns [16 h2, 16 h2 + 16), all already read.
 #pragma unroll
       for (int h2 = 0; h2 < 4; ++h2) {
+        uint32_t x[32];
+        FA_TMEM_LD_32(s_cols + h2 * 32, x);
+        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+        if (diag) {
+          const int lim = qpos - j * BKV - h2 * 32;
+#pragma unroll
+          for (int i = 0; i < 32; ++i)
+            if (i > lim) x[i] = __float_as_uint(-INFINITY);
+        }
         uint32_t pk[16];
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
-          const float a = ex2(fmaf(__uint_as_float(r[h2 * 32 + 2 * i]), c, nm));
-          const float b2 = ex2(fmaf(__uint_as_float(r[h2 * 32 + 2 * i + 1]), c, nm));
-          sum += a + b2;
-          __nv_bfloat162 v2 = __floats2bfloat162_rn(a, b2);
-          pk[i] = *reinterpret_cast<uint32_t*>(&v2);
+          const uint64_t x2 = fma2(pk2(__uint_as_float(x[2 * i]), __uint_as_float(x[2 * i + 1])), cc, nmm);
+          uint64_t e2;
+          if ((i % 3) == 2) {
+            e2 = ex2_poly2(x2);
+          } else {
+            float x0, x1;
+            up2(x2, x0, x1);
+            e2 = pk2(ex2(x0), ex2(x1));
+          }
+          sum2[i & 1] = add2(sum2[i & 1], e2);
+          float e0, e1;
+          up2(e2, e0, e1);
+          asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(pk[i]) : "f"(e1), "f"(e0));
         }
         FA_TMEM_ST_16(s_cols + h2 * 16, pk);
       }
-      l += sum;
+      {
+        const uint64_t t2 = add2(sum2[0], sum2[1]);
+        float s0, s1;
+        up2(t2, s0, s1);
+        l += s0 + s1;
+      }
       asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
       fence_before();
       __syncwarp();
       if (lane == 0) bar_arrive(&p_full[grp]);
+      if (p.timing) {
+        const unsigned long long te = clk64();
+        sw_work += te - tb;
+        sw_exp += te - tex;
+      }
+    }
+    if (p.timing && lane == 0) {
+      atomicAdd(&g_fa_dbg[4], sw_wait);
+      atomicAdd(&g_fa_dbg[5], sw_work);
+      atomicAdd(&g_fa_dbg[6], 1ull);
+      atomicAdd(&g_fa_dbg[8], sw_max);
+      atomicAdd(&g_fa_dbg[9], sw_resc);
+      atomicAdd(&g_fa_dbg[10], sw_exp);
+      atomicAdd(&g_fa_dbg[11], (unsigned long long)n);
     }
     if (ok && active) ok = bar_wait(&o_final[grp], 0, p.err, 32) && !*abort_flag;
     if (!active) {
@@ -467,6 +615,11 @@ std::vector<at::Tensor> attn_fwd(at::Tensor qkv, int64_t hpg, bool causal) {
   p.scale_log2 = (float)(1.4426950408889634 / std::sqrt((double)D));
   p.causal = causal ? 1 : 0;
   p.err = err_flag();
+  static const int timing = [] {
+    const char* e = std::getenv("EMB_ATTN_TIMING");
+    return (e && std::atoi(e) == 1) ? 1 : 0;
+  }();
+  p.timing = timing;
   static bool attr[kMaxDevices] = {};
   int dev = 0;
   EMB_CUDA_CHECK(cudaGetDevice(&dev));
@@ -479,6 +632,47 @@ std::vector<at::Tensor> attn_fwd(at::Tensor qkv, int64_t hpg, bool causal) {
   EMB_LAUNCH_CHECK();
   count_launch();
   return {o, lse};
+}
+
+namespace fa {
+// scalar and packed forms: even elements through ex2_poly2 in pairs, an odd tail through ex2_poly
+__global__ void exp2_emulated_kernel(const float* x, float* y, int64_t n) {
+  for (int64_t i = 2 * (blockIdx.x * (int64_t)blockDim.x + threadIdx.x); i < n; i += 2 * (int64_t)gridDim.x * blockDim.x) {
+    if (i + 1 < n) {
+      float a, b;
+      up2(ex2_poly2(pk2(x[i], x[i + 1])), a, b);
+      y[i] = a;
+      y[i + 1] = b;
+    } else {
+      y[i] = ex2_poly(x[i]);
+    }
+  }
+}
+}  // namespace fa
+
+// The softmax's FMA-pipe 2^x on a float tensor (accuracy tests against exp2).
+at::Tensor attn_exp2_emulated(at::Tensor x) {
+  TORCH_CHECK(x.is_cuda() && x.scalar_type() == at::kFloat && x.is_contiguous());
+  auto y = at::empty_like(x);
+  const int64_t n = x.numel();
+  if (n) {
+    fa::exp2_emulated_kernel<<<(int)std::min<int64_t>((n + 255) / 256, 4096), 256, 0, cur_stream()>>>(
+        x.data_ptr<float>(), y.data_ptr<float>(), n);
+    EMB_LAUNCH_CHECK();
+    count_launch();
+  }
+  return y;
+}
+
+// Per-role cycle counters of the forward kernel when EMB_ATTN_TIMING=1 (measurement only), then reset:
+// [MMA waits for V, MMA waits for P, MMA total, MMA threads, softmax waits for S, softmax work, softmax warps,
+//  rescales].
+std::vector<int64_t> attn_debug_counters() {
+  unsigned long long h[16];
+  EMB_CUDA_CHECK(cudaMemcpyFromSymbol(h, fa::g_fa_dbg, sizeof(h)));
+  unsigned long long z[16] = {0};
+  EMB_CUDA_CHECK(cudaMemcpyToSymbol(fa::g_fa_dbg, z, sizeof(z)));
+  return std::vector<int64_t>(h, h + 16);
 }
 
 int64_t attn_error_flag() {

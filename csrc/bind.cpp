@@ -41,6 +41,8 @@ torch::Tensor attn_bwd(torch::Tensor dO, torch::Tensor qkv, torch::Tensor o, tor
                        bool causal);
 int64_t attn_bwd_error_flag();
 int64_t gemm_error_flag();
+at::Tensor attn_exp2_emulated(at::Tensor x);
+std::vector<int64_t> attn_debug_counters();
 std::vector<int64_t> gemm_debug_counters();
 void gemm_rs(torch::Tensor a, torch::Tensor b, bool trans_a, bool trans_b, torch::Tensor peers, int64_t my_slot,
              int64_t rows_per_rank);
@@ -105,6 +107,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("causal") = true);
   m.def("attn_bwd_error_flag", &attn_bwd_error_flag);
   m.def("attn_error_flag", &attn_error_flag);
+  m.def("attn_exp2_emulated", &attn_exp2_emulated);
+  m.def("attn_debug_counters", &attn_debug_counters);
   m.def("gemm_error_flag", &gemm_error_flag);
   m.def("gemm_debug_counters", &gemm_debug_counters);
   m.def("gemm_rs", &gemm_rs);

@@ -21,6 +21,8 @@ NVCC_FLAGS = [
 ]
 if os.environ.get("EMB_PTXAS_VERBOSE"):
     NVCC_FLAGS += ["-Xptxas", "-v"]
+if os.environ.get("EMB_NVCC_EXTRA"):  # extra nvcc flags for experiments, e.g. "-DFA_POLY_MASK=0x5555"
+    NVCC_FLAGS += os.environ["EMB_NVCC_EXTRA"].split()
 
 setup(
     name="elasticmegatron_b200",

@@ -69,3 +69,19 @@ def test_attention_autograd_native_path():
     x = qkv.detach().float().requires_grad_(True)
     o_ref, _ = _ref(x, 2, True)
     torch.testing.assert_close(y.float(), o_ref, atol=2e-2, rtol=2e-2)
+
+
+def test_softmax_exp2_emulation_error_bound():
+    """The FMA-pipe 2^x used for part of the softmax stays within 2e-4 relative of exp2 over the softmax's
+    input range (scores minus the running max: at most +8, masked entries at -inf)."""
+    from elasticmegatron_b200.ops.native import ext
+
+    x = torch.cat([torch.linspace(-125.0, 8.0, 1 << 20, device="cuda"),
+                   torch.rand(1 << 20, device="cuda") * -20.0, torch.tensor([0.5], device="cuda")])
+    y = ext().attn_exp2_emulated(x)  # pairs through the packed form, the odd last element through the scalar one
+    ref = torch.exp2(x.double())
+    rel = ((y.double() - ref).abs() / ref).max().item()
+    assert rel < 2e-4, rel
+    # inputs below -125 (and masked -inf) are clamped: a result below 2^-124, negligible next to the row max's 1
+    z = ext().attn_exp2_emulated(torch.tensor([-float("inf"), -1000.0, -125.9], device="cuda"))
+    assert (z >= 0).all() and (z < 2.0 ** -124).all()
