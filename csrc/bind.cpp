@@ -12,7 +12,8 @@ bool ipc_close(torch::Tensor handle);
 int64_t ipc_open_count();
 std::vector<torch::Tensor> rmsnorm_fwd(torch::Tensor x, torch::Tensor w, double eps);
 std::vector<torch::Tensor> rmsnorm_bwd(torch::Tensor dy, torch::Tensor x, torch::Tensor w, torch::Tensor rstd,
-                                       c10::optional<torch::Tensor> dw_accum);
+                                       c10::optional<torch::Tensor> dw_accum, c10::optional<torch::Tensor> dres);
+std::vector<torch::Tensor> add_rmsnorm_fwd(torch::Tensor x, torch::Tensor o, torch::Tensor w, double eps);
 torch::Tensor swiglu_fwd(torch::Tensor h);
 torch::Tensor swiglu_bwd(torch::Tensor dy, torch::Tensor h);
 torch::Tensor rope_fwd(torch::Tensor qkv, torch::Tensor cosv, torch::Tensor sinv, int64_t nrot, bool inverse);
@@ -82,7 +83,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("ipc_open_count", &ipc_open_count);
   m.def("rmsnorm_fwd", &rmsnorm_fwd);
   m.def("rmsnorm_bwd", &rmsnorm_bwd, py::arg("dy"), py::arg("x"), py::arg("w"), py::arg("rstd"),
-        py::arg("dw_accum") = py::none());
+        py::arg("dw_accum") = py::none(), py::arg("dres") = py::none());
+  m.def("add_rmsnorm_fwd", &add_rmsnorm_fwd);
   m.def("swiglu_fwd", &swiglu_fwd);
   m.def("swiglu_bwd", &swiglu_bwd);
   m.def("rope_fwd", &rope_fwd);

@@ -43,6 +43,54 @@ __global__ void rmsnorm_fwd_kernel(const __nv_bfloat16* __restrict__ x, const __
   }
 }
 
+// Residual add fused into the norm that follows it: h = x + o (rounded to bf16, the residual stream's type),
+// y = RMSNorm(h) * w.  One read of x and o, one write of h and y: the unfused pair reads h back.
+template <int VPT>
+__global__ void add_rmsnorm_fwd_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ o,
+                                       const __nv_bfloat16* __restrict__ w, __nv_bfloat16* __restrict__ h,
+                                       __nv_bfloat16* __restrict__ y, float* __restrict__ rstd_out, int H, float eps) {
+  __shared__ float sh[32];
+  const int row = blockIdx.x;
+  const int nvec = H / 8;
+  const uint4* xr = reinterpret_cast<const uint4*>(x + (size_t)row * H);
+  const uint4* orow = reinterpret_cast<const uint4*>(o + (size_t)row * H);
+  uint4* hr = reinterpret_cast<uint4*>(h + (size_t)row * H);
+  float v[VPT][8];
+  float ss = 0.f;
+#pragma unroll
+  for (int k = 0; k < VPT; ++k) {
+    int i = threadIdx.x + k * blockDim.x;
+    if (i < nvec) {
+      float a[8], b[8];
+      unpack8(xr[i], a);
+      unpack8(orow[i], b);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) a[j] += b[j];
+      const uint4 u = pack8(a);
+      hr[i] = u;
+      unpack8(u, v[k]);  // the norm sees the rounded residual, as the unfused pair does
+#pragma unroll
+      for (int j = 0; j < 8; ++j) ss += v[k][j] * v[k][j];
+    }
+  }
+  ss = block_sum(ss, sh);
+  const float r = rsqrtf(ss / H + eps);
+  if (threadIdx.x == 0) rstd_out[row] = r;
+  const uint4* wr = reinterpret_cast<const uint4*>(w);
+  uint4* yr = reinterpret_cast<uint4*>(y + (size_t)row * H);
+#pragma unroll
+  for (int k = 0; k < VPT; ++k) {
+    int i = threadIdx.x + k * blockDim.x;
+    if (i < nvec) {
+      float wf[8], t[8];
+      unpack8(wr[i], wf);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) t[j] = v[k][j] * r * wf[j];
+      yr[i] = pack8(t);
+    }
+  }
+}
+
 // threads per row so that each thread holds at most 4 16-byte vectors of the row in registers
 static int pick_threads(int nvec, int& vpt) {
   int t = ((nvec + 3) / 4 + 31) / 32 * 32;
@@ -72,11 +120,37 @@ std::vector<at::Tensor> rmsnorm_fwd(at::Tensor x, at::Tensor w, double eps) {
   return {y, rstd};
 }
 
+// Returns (h = x + o, y = RMSNorm(h) * w, rstd).
+std::vector<at::Tensor> add_rmsnorm_fwd(at::Tensor x, at::Tensor o, at::Tensor w, double eps) {
+  check_cuda_bf16(x, "x");
+  check_cuda_bf16(o, "o");
+  check_cuda_bf16(w, "w");
+  TORCH_CHECK(x.sizes() == o.sizes() && x.dim() == 2, "add_rmsnorm_fwd: x and o must be equal [T, H]");
+  const int64_t T = x.size(0), H = x.size(1);
+  TORCH_CHECK(H % 8 == 0 && H <= 8 * 4 * 1024, "hidden size must be a multiple of 8 and <= 32768");
+  auto h = at::empty_like(x);
+  auto y = at::empty_like(x);
+  auto rstd = at::empty({T}, x.options().dtype(at::kFloat));
+  if (T == 0) return {h, y, rstd};
+  int vpt;
+  int threads = pick_threads((int)(H / 8), vpt);
+  auto st = cur_stream();
+#define L(V) add_rmsnorm_fwd_kernel<V><<<T, threads, 0, st>>>((const __nv_bfloat16*)x.data_ptr(),                 \
+      (const __nv_bfloat16*)o.data_ptr(), (const __nv_bfloat16*)w.data_ptr(), (__nv_bfloat16*)h.data_ptr(),      \
+      (__nv_bfloat16*)y.data_ptr(), rstd.data_ptr<float>(), (int)H, (float)eps)
+  if (vpt <= 1) L(1); else if (vpt == 2) L(2); else if (vpt == 3) L(3); else L(4);
+#undef L
+  EMB_LAUNCH_CHECK();
+  count_launch();
+  return {h, y, rstd};
+}
+
 // ------------------------------------------------------------------------------------------ RMSNorm bwd
 template <int VPT>
 __global__ void rmsnorm_bwd_kernel(const __nv_bfloat16* __restrict__ dy, const __nv_bfloat16* __restrict__ x,
                                    const __nv_bfloat16* __restrict__ w, const float* __restrict__ rstd,
-                                   __nv_bfloat16* __restrict__ dx, float* __restrict__ dw_part, int T, int H) {
+                                   __nv_bfloat16* __restrict__ dx, float* __restrict__ dw_part, int T, int H,
+                                   const __nv_bfloat16* __restrict__ dres = nullptr) {
   __shared__ float sh[32];
   const int nvec = H / 8;
   const uint4* wr = reinterpret_cast<const uint4*>(w);
@@ -113,6 +187,8 @@ __global__ void rmsnorm_bwd_kernel(const __nv_bfloat16* __restrict__ dy, const _
     }
     dot = block_sum(dot, sh) / H;
     uint4* o = reinterpret_cast<uint4*>(dx + (size_t)row * H);
+    // dres: the residual stream's gradient, added here when the forward fused the residual add into the norm
+    const uint4* rr = dres ? reinterpret_cast<const uint4*>(dres + (size_t)row * H) : nullptr;
 #pragma unroll
     for (int k = 0; k < VPT; ++k) {
       int i = threadIdx.x + k * blockDim.x;
@@ -120,6 +196,12 @@ __global__ void rmsnorm_bwd_kernel(const __nv_bfloat16* __restrict__ dy, const _
         float t[8];
 #pragma unroll
         for (int j = 0; j < 8; ++j) t[j] = r * (gv[k][j] - xv[k][j] * dot);
+        if (rr) {
+          float a[8];
+          unpack8(rr[i], a);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) t[j] += a[j];
+        }
         o[i] = pack8(t);
       }
     }
@@ -146,10 +228,15 @@ __global__ void colsum_kernel(const float* __restrict__ part, float* __restrict_
 }
 
 std::vector<at::Tensor> rmsnorm_bwd(at::Tensor dy, at::Tensor x, at::Tensor w, at::Tensor rstd,
-                                       c10::optional<at::Tensor> dw_accum) {
+                                       c10::optional<at::Tensor> dw_accum, c10::optional<at::Tensor> dres) {
   check_cuda_bf16(dy, "dy");
   check_cuda_bf16(x, "x");
   const int64_t T = x.size(0), H = x.size(1);
+  const bool has_res = dres.has_value() && dres->defined();
+  if (has_res) {
+    check_cuda_bf16(*dres, "dres");
+    TORCH_CHECK(dres->sizes() == x.sizes(), "rmsnorm_bwd: dres must match x");
+  }
   auto dx = at::empty_like(x);
   int vpt;
   int threads = pick_threads((int)(H / 8), vpt);
@@ -157,9 +244,10 @@ std::vector<at::Tensor> rmsnorm_bwd(at::Tensor dy, at::Tensor x, at::Tensor w, a
   if (grid < 1) grid = 1;
   auto part = at::empty({grid, H}, x.options().dtype(at::kFloat));
   auto st = cur_stream();
+  const __nv_bfloat16* rp = has_res ? (const __nv_bfloat16*)dres->data_ptr() : nullptr;
 #define L(V) rmsnorm_bwd_kernel<V><<<grid, threads, 0, st>>>((const __nv_bfloat16*)dy.data_ptr(),                  \
       (const __nv_bfloat16*)x.data_ptr(), (const __nv_bfloat16*)w.data_ptr(), rstd.data_ptr<float>(),               \
-      (__nv_bfloat16*)dx.data_ptr(), part.data_ptr<float>(), (int)T, (int)H)
+      (__nv_bfloat16*)dx.data_ptr(), part.data_ptr<float>(), (int)T, (int)H, rp)
   if (vpt <= 1) L(1); else if (vpt == 2) L(2); else if (vpt == 3) L(3); else L(4);
 #undef L
   EMB_LAUNCH_CHECK();

@@ -106,6 +106,16 @@ class GPTStage(nn.Module):
             return F_.layernorm(x, w, b, self.cfg.norm_epsilon)
         return F_.rmsnorm(x, w, self.cfg.norm_epsilon)
 
+    def _add_norm(self, x: torch.Tensor, pending: Optional[torch.Tensor], weight_name: str):
+        """Residual add of the previous branch's output (``pending``) fused into the norm that follows it:
+        returns (the new residual stream, its normalised copy)."""
+        if pending is None:
+            return x, self._norm(x, weight_name)
+        if self.cfg.normalization == "LayerNorm":
+            x = x + pending
+            return x, self._norm(x, weight_name)
+        return F_.add_rmsnorm(x, pending, self.params_by_name[weight_name], self.cfg.norm_epsilon)
+
     def rebind(self, views: Dict[str, torch.Tensor]) -> None:
         """Point every parameter at a new arena (after a release / rebuild)."""
         for n, p in self.params_by_name.items():
@@ -133,20 +143,23 @@ class GPTStage(nn.Module):
         cos, sin = _ROPE.get(positions, cfg.head_dim, cfg.rotary_base, x.device)
         aux_total = None
         recompute = self.recompute and torch.is_grad_enabled()
+        # the residual stream is carried as (x, pending): the last branch output is added by the norm that
+        # consumes it (the next layer's input norm, or the final norm)
+        pending = None
         for i in range(self.num_local_layers):
             if recompute:
                 # early stop off: every rank replays the whole layer, so its collectives run in full and in
                 # the same order on all ranks of each group
                 with torch.utils.checkpoint.set_checkpoint_early_stop(False):
-                    x, aux = torch.utils.checkpoint.checkpoint(self._layer, i, x, cos, sin, seq_local, b,
-                                                               use_reentrant=False)
+                    x, pending, aux = torch.utils.checkpoint.checkpoint(self._layer, i, x, pending, cos, sin,
+                                                                        seq_local, b, use_reentrant=False)
             else:
-                x, aux = self._layer(i, x, cos, sin, seq_local, b)
+                x, pending, aux = self._layer(i, x, pending, cos, sin, seq_local, b)
             if aux is not None:
                 aux_total = aux if aux_total is None else aux_total + aux
         if not self.last:
-            return x, aux_total
-        x = self._norm(x, "decoder.final_layernorm.weight")
+            return (x + pending if pending is not None else x), aux_total
+        _, x = self._add_norm(x, pending, "decoder.final_layernorm.weight")
         # untied, or the last stage's copy of a tied embedding; at PP=1 a tied head is the embedding itself
         w_out = self.params_by_name.get("output_layer.weight")
         if w_out is None:
@@ -156,12 +169,13 @@ class GPTStage(nn.Module):
         losses = F_.vocab_parallel_cross_entropy(logits, lab, self.vocab_start, self.tp_group)
         return losses, aux_total
 
-    def _layer(self, i: int, x: torch.Tensor, cos, sin, seq_local: int, b: int):
+    def _layer(self, i: int, x: torch.Tensor, pending: Optional[torch.Tensor], cos, sin, seq_local: int, b: int):
+        """One transformer layer on the residual stream ``x + pending``; returns (x', pending', aux) with the
+        layer's output equal to ``x' + pending'`` (the MLP branch's output is left for the next norm to add)."""
         cfg = self.cfg
         G_loc = cfg.num_query_groups // self.tp
         hpg, d = cfg.heads_per_group, cfg.head_dim
-        res = x
-        h = self._norm(x, f"decoder.layers.{i}.self_attention.linear_qkv.layer_norm_weight")
+        x, h = self._add_norm(x, pending, f"decoder.layers.{i}.self_attention.linear_qkv.layer_norm_weight")
         qkv = F_.linear(h, self._p(i, "self_attention.linear_qkv.weight"), self._mode("col"), self.tp_group)
         qkv = qkv.view(seq_local, b, G_loc, hpg + 2, d)
         qkv = F_.rope_qkv(qkv, cos, sin, hpg + 1)
@@ -171,14 +185,13 @@ class GPTStage(nn.Module):
             attn = F_.attention(qkv, hpg)
         o = F_.linear(attn.view(seq_local * b, -1), self._p(i, "self_attention.linear_proj.weight"),
                       self._mode("row"), self.tp_group)
-        x = res + o
         aux = None
         if self.moe is not None:
-            h = self._norm(x, f"decoder.layers.{i}.pre_mlp_layernorm.weight")
+            x, h = self._add_norm(x, o, f"decoder.layers.{i}.pre_mlp_layernorm.weight")
             o, aux = self.moe[i](h)
         else:
-            h = self._norm(x, f"decoder.layers.{i}.mlp.linear_fc1.layer_norm_weight")
+            x, h = self._add_norm(x, o, f"decoder.layers.{i}.mlp.linear_fc1.layer_norm_weight")
             h = F_.linear(h, self._p(i, "mlp.linear_fc1.weight"), self._mode("col"), self.tp_group)
             h = F_.swiglu(h)
             o = F_.linear(h, self._p(i, "mlp.linear_fc2.weight"), self._mode("row"), self.tp_group)
-        return x + o, aux
+        return x, o, aux

@@ -247,6 +247,50 @@ def rmsnorm(x, w, eps):
     return RMSNormFn.apply(x, w, eps)
 
 
+class AddRMSNormFn(torch.autograd.Function):
+    """``h = x + o`` (the residual stream) and ``y = RMSNorm(h) * w`` in one kernel; the backward adds the
+    residual stream's gradient ``dh`` inside the norm's backward kernel, so neither the forward add nor the
+    gradient sum at the branch point is a separate pass over the activations."""
+
+    @staticmethod
+    def forward(ctx, x, o, w, eps):
+        x2, o2 = x.reshape(-1, x.shape[-1]), o.reshape(-1, o.shape[-1])
+        if use_native(x2):
+            h, y, rstd = ext().add_rmsnorm_fwd(x2.contiguous(), o2.contiguous(), w, eps)
+        else:
+            h = x2 + o2
+            y, rstd = ref.rmsnorm_fwd(h, w, eps)
+        ctx.save_for_backward(h, w, rstd)
+        return h.view(x.shape), y.view(x.shape)
+
+    @staticmethod
+    def backward(ctx, dh, dy):
+        h, w, rstd = ctx.saved_tensors
+        dy2 = dy.reshape(-1, dy.shape[-1]).contiguous()
+        dh2 = dh.reshape(-1, dh.shape[-1]).contiguous() if dh is not None else None
+        mg = getattr(w, "main_grad", None)
+        if use_native(h):
+            dx, dw = ext().rmsnorm_bwd(dy2, h, w, rstd, mg.view(-1) if mg is not None else None, dh2)
+        else:
+            dx, dw = ref.rmsnorm_bwd(dy2, h, w, rstd)
+            if dh2 is not None:
+                dx = dx + dh2
+            if mg is not None:
+                mg.view(-1).add_(dw)
+        dx = dx.view(dy.shape)
+        if mg is not None:
+            hook = getattr(w, "_grad_ready", None)
+            if hook is not None:
+                hook()
+            return dx, dx, None, None
+        return dx, dx, dw.to(w.dtype), None
+
+
+def add_rmsnorm(x, o, w, eps):
+    """(x + o, RMSNorm(x + o) * w)."""
+    return AddRMSNormFn.apply(x, o, w, eps)
+
+
 def layernorm(x, w, b, eps):
     """Megatron's LayerNorm (weight and bias) over the last dimension.  It runs the library kernel on both
     host and device (as attention does by default); the weight and bias gradients reach ``main_grad``

@@ -38,6 +38,47 @@ def test_rmsnorm(T, H):
     _close(acc, dw_ref + 1, 5e-2 * math.sqrt(T / 64), 1e-2)
 
 
+@pytest.mark.parametrize("T,H", [(7, 512), (300, 4096)])
+def test_add_rmsnorm_fused(T, H):
+    """Residual add fused into RMSNorm (forward) and the residual gradient added in the norm's backward, against
+    the fp32 reference of the unfused pair."""
+    torch.manual_seed(1)
+    x = torch.randn(T, H, device="cuda").bfloat16()
+    o = torch.randn(T, H, device="cuda").bfloat16()
+    w = (1 + 0.1 * torch.randn(H, device="cuda")).bfloat16()
+    h, y, rstd = _ext().add_rmsnorm_fwd(x, o, w, 1e-5)
+    h_ref = (x.float() + o.float()).bfloat16().float()  # the residual stream is bf16
+    y_ref, rstd_ref = ref.rmsnorm_fwd(h_ref, w.float(), 1e-5)
+    _close(h, h_ref, 1e-6, 1e-6)
+    _close(y, y_ref, 2e-2, 2e-2)
+    _close(rstd, rstd_ref, 1e-4, 1e-4)
+    dy = torch.randn(T, H, device="cuda").bfloat16()
+    dh = torch.randn(T, H, device="cuda").bfloat16()
+    dx, dw = _ext().rmsnorm_bwd(dy, h, w, rstd, None, dh)
+    dx_ref, dw_ref = ref.rmsnorm_bwd(dy.float(), h_ref, w.float(), rstd_ref)
+    _close(dx, dx_ref + dh.float(), 3e-2, 3e-2)
+    _close(dw, dw_ref, 5e-2 * math.sqrt(T / 64), 1e-2)
+
+
+def test_add_rmsnorm_autograd_matches_unfused():
+    from elasticmegatron_b200.ops import functional as F_
+
+    torch.manual_seed(2)
+    T, H = 256, 1024
+    x = torch.randn(T, H, device="cuda").bfloat16().requires_grad_(True)
+    o = torch.randn(T, H, device="cuda").bfloat16().requires_grad_(True)
+    w = (1 + 0.1 * torch.randn(H, device="cuda")).bfloat16().requires_grad_(True)
+    h, y = F_.add_rmsnorm(x, o, w, 1e-5)
+    (h.float().sum() + (y.float() ** 2).sum()).backward()
+    xr, orr, wr = (t.detach().float().requires_grad_(True) for t in (x, o, w))
+    hr = xr + orr
+    yr = hr * torch.rsqrt(hr.pow(2).mean(-1, keepdim=True) + 1e-5) * wr
+    (hr.sum() + (yr ** 2).sum()).backward()
+    _close(x.grad, xr.grad, 5e-2, 3e-2)
+    _close(o.grad, orr.grad, 5e-2, 3e-2)
+    _close(w.grad, wr.grad, 2.0, 3e-2)
+
+
 def test_swiglu():
     torch.manual_seed(0)
     h = torch.randn(333, 2 * 1376, device="cuda").bfloat16()
