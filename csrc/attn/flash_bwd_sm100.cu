@@ -26,7 +26,9 @@ namespace fab {
 
 constexpr int D = 128, T = 128;
 constexpr int TILE = 128 * 128 * 2;
-constexpr int SMEM_BYTES = 6 * TILE + 1024 /*lse, delta*/ + 1024 /*align*/ + 256 /*barriers*/;
+constexpr int DQ_STAGE = 4 * 2 * 4096;  // dQ staging: per softmax warp two 32-row x 128-byte blocks
+constexpr int SMEM_BYTES = 6 * TILE + DQ_STAGE + 1024 /*lse, delta*/ + 1024 /*align*/ + 256 /*barriers*/;
+static_assert(SMEM_BYTES <= 232448, "flash_bwd_kernel shared memory above the 227 KiB per-block limit");
 constexpr uint32_t WAIT_LIMIT = 1u << 26;
 
 __device__ __forceinline__ uint32_t su32(const void* p) { return static_cast<uint32_t>(__cvta_generic_to_shared(p)); }
@@ -79,6 +81,11 @@ __device__ __forceinline__ void commit(uint64_t* bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(su32(bar))
                : "memory");
 }
+__device__ __forceinline__ float ex2f_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
 #define FAB_LD32(taddr, r)                                                                                          \
   asm volatile(                                                                                                     \
       "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19," \
@@ -106,7 +113,8 @@ struct Params {
 };
 
 __global__ void __launch_bounds__(192, 1)
-    flash_bwd_kernel(const __grid_constant__ CUtensorMap tqkv, const __grid_constant__ CUtensorMap tdo, Params p) {
+    flash_bwd_kernel(const __grid_constant__ CUtensorMap tqkv, const __grid_constant__ CUtensorMap tdo,
+                     const __grid_constant__ CUtensorMap tdq, Params p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sK = sm;
@@ -115,9 +123,10 @@ __global__ void __launch_bounds__(192, 1)
   uint8_t* sdO = sm + 3 * TILE;
   uint8_t* sP = sm + 4 * TILE;   // P^T  [key rows x query cols]
   uint8_t* sdS = sm + 5 * TILE;  // dS^T [key rows x query cols]
-  float* s_lse = reinterpret_cast<float*>(sm + 6 * TILE);
+  uint8_t* sdq = sm + 6 * TILE;  // [4 warps][2][32 rows x 128 B], 128-byte swizzle
+  float* s_lse = reinterpret_cast<float*>(sm + 6 * TILE + DQ_STAGE);
   float* s_delta = s_lse + 128;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + 6 * TILE + 1024);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + 6 * TILE + DQ_STAGE + 1024);
   uint64_t* kv_full = bars;
   uint64_t* qdo_full = bars + 1;
   uint64_t* qdo_empty = bars + 2;
@@ -222,6 +231,7 @@ __global__ void __launch_bounds__(192, 1)
     const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
     const int kpos = jt * T + r;
     bool ok = true;
+    uint32_t dq_n = 0;  // dQ blocks this warp has handed to the bulk-copy engine (selects the staging buffer)
     for (int n = 0; n < nsteps; ++n) {
       const int hj = n / (nq - i0), it = i0 + n % (nq - i0);
       const int h = g * p.hpg + hj;
@@ -248,7 +258,7 @@ __global__ void __launch_bounds__(192, 1)
         for (int i = 0; i < 32; ++i) {
           const int q = c * 32 + i;
           const int qpos = it * T + q;
-          float pr = exp2f(__uint_as_float(sv[i]) * p.scale_log2 - s_lse[q]);
+          float pr = ex2f_approx(fmaf(__uint_as_float(sv[i]), p.scale_log2, -s_lse[q]));
           if (diag && qpos < kpos) pr = 0.f;
           pf[i] = pr;
           df[i] = pr * (__uint_as_float(dv[i]) - s_delta[q]) * p.scale;
@@ -263,21 +273,35 @@ __global__ void __launch_bounds__(192, 1)
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       __syncwarp();
       if (lane == 0) bar_arrive(ds_full);
-      // dQ tile (TMEM cols 0..127, lane = query row) -> fp32 accumulator
+      // dQ tile (TMEM cols 0..127, lane = query row) -> fp32 accumulator in global memory: each warp stages its
+      // 32 rows x 32 columns in a 128-byte-swizzled block and one lane adds it with a bulk tensor reduction
+      // (atomic per element against the other key tiles' CTAs), double-buffered per warp
       if (!bar_wait(mma2_done, ph, p.err, 48) || *abort_flag) { ok = false; break; }
       fence_after();
-      float* dst = p.dq_acc + (((size_t)(it * T + r) * p.b + bidx) * H + h) * D;
 #pragma unroll 1
       for (int c = 0; c < 4; ++c) {
         uint32_t qv[32];
         FAB_LD32(tmem + lane_base + c * 32, qv);
         asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+        uint8_t* wbuf = sdq + quarter * 8192 + (dq_n & 1) * 4096;
+        if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+        __syncwarp();
+        uint8_t* myrow = wbuf + lane * 128;
 #pragma unroll
-        for (int v4 = 0; v4 < 8; ++v4) {
-          float4 val = make_float4(__uint_as_float(qv[4 * v4]), __uint_as_float(qv[4 * v4 + 1]),
-                                   __uint_as_float(qv[4 * v4 + 2]), __uint_as_float(qv[4 * v4 + 3]));
-          atomicAdd(reinterpret_cast<float4*>(dst + c * 32 + 4 * v4), val);
+        for (int j = 0; j < 8; ++j)
+          *reinterpret_cast<uint4*>(myrow + ((j ^ (lane & 7)) << 4)) =
+              make_uint4(qv[4 * j], qv[4 * j + 1], qv[4 * j + 2], qv[4 * j + 3]);
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        __syncwarp();
+        if (lane == 0) {
+          asm volatile(
+              "cp.reduce.async.bulk.tensor.3d.global.shared::cta.add.tile.bulk_group [%0, {%1, %2, %3}], [%4];" ::"l"(
+                  reinterpret_cast<uint64_t>(&tdq)),
+              "r"(c * 32), "r"(bidx * H + h), "r"(it * T + quarter * 32), "r"(su32(wbuf))
+              : "memory");
+          asm volatile("cp.async.bulk.commit_group;" ::: "memory");
         }
+        ++dq_n;
       }
       fence_before();
       __syncwarp();
@@ -310,6 +334,7 @@ __global__ void __launch_bounds__(192, 1)
         }
       }
     }
+    if (lane == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");  // staging reads / reductions done
   }
   fence_before();
   __syncthreads();
@@ -400,6 +425,18 @@ at::Tensor attn_bwd(at::Tensor dO, at::Tensor qkv, at::Tensor o, at::Tensor lse,
                                                delta.data_ptr<float>(), (int)s, (int)b, (int)H);
   CUtensorMap tq = fa::qkv_map(qkv);
   CUtensorMap td = do_map(dO, s, b, H);
+  CUtensorMap tdq;
+  {
+    // {d, (b, head), s} view of the fp32 dQ accumulator [s, b, H, d]: 32-column x 32-row boxes of 128 bytes
+    cuuint64_t dims[3] = {(cuuint64_t)D, (cuuint64_t)(b * H), (cuuint64_t)s};
+    cuuint64_t strides[2] = {(cuuint64_t)(D * 4), (cuuint64_t)(b * H * D * 4)};
+    cuuint32_t box[3] = {32, 1, 32};
+    cuuint32_t es[3] = {1, 1, 1};
+    CUresult r = encode_fn()(&tdq, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, dq.data_ptr(), dims, strides, box, es,
+                             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    TORCH_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled(dq) failed: ", (int)r);
+  }
   Params p;
   p.lse = lse.data_ptr<float>();
   p.delta = delta.data_ptr<float>();
@@ -419,7 +456,7 @@ at::Tensor attn_bwd(at::Tensor dO, at::Tensor qkv, at::Tensor o, at::Tensor lse,
     attr = true;
   }
   dim3 grid((unsigned)(s / T), (unsigned)(b * G));
-  flash_bwd_kernel<<<grid, 192, SMEM_BYTES, st>>>(tq, td, p);
+  flash_bwd_kernel<<<grid, 192, SMEM_BYTES, st>>>(tq, td, tdq, p);
   const int64_t n = s * b * G * hpg * (D / 8);
   dq_cast_kernel<<<(int)std::min<int64_t>((n + 255) / 256, (int64_t)num_sms() * 8), 256, 0, st>>>(
       dq.data_ptr<float>(), reinterpret_cast<__nv_bfloat16*>(dqkv.data_ptr()), (int)s, (int)b, (int)G, (int)hpg);

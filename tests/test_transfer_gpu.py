@@ -112,3 +112,49 @@ def test_native_engine_two_gpus():
     from dist_utils import run_distributed
 
     assert all(run_distributed(_two_gpu, 2, backend="nccl"))
+
+
+def _group_zero_two_gpus(rank, world):
+    """Group-ZeRO on two GPUs with the native engine: DP2 with two optimizer instances (each GPU a full replica)
+    -> one GPU (the replica dropped, rank 1 idle) -> DP2 with two instances again (the replica rebuilt by K1
+    over NVLink from the surviving copy).  Every byte of the state must come back, on both GPUs."""
+    import torch
+    torch.cuda.set_device(rank)
+    from elasticmegatron_b200.config import Args, ModelConfig, TrainConfig, set_args
+    from elasticmegatron_b200.parallel.process_groups import create_all_groups
+    from elasticmegatron_b200.parallel.strategy import ParallelStrategy
+    from elasticmegatron_b200.runtime.manager import ElasticMegatronManager
+    from elasticmegatron_b200.runtime.train import train_step
+    from elasticmegatron_b200.runtime.training_state import TrainingState
+
+    cfg = ModelConfig(num_layers=2, hidden_size=256, num_attention_heads=4, ffn_hidden_size=512, vocab_size=1000,
+                      seq_length=128, params_dtype="bf16", max_tensor_parallel_size=2, make_vocab_size_divisible_by=8)
+    set_args(Args(model=cfg, train=TrainConfig(micro_batch_size=2, global_batch_size=4)))
+    strats = [dict(world_size=2, tensor_model_parallel_size=1, pipeline_model_parallel_size=1,
+                   num_distributed_optimizer_instances=2),
+              dict(world_size=1, tensor_model_parallel_size=1, pipeline_model_parallel_size=1)]
+    S = [ParallelStrategy(**s) for s in strats]
+    create_all_groups(S)
+    ts = TrainingState(S[0])
+    ts.init_weights(0)
+    mgr = ElasticMegatronManager(strats, training_state=ts, engine="native")
+    train_step(ts, mgr.build_iterators(0)[0])
+    P0, O0 = ts.param_flat.clone(), ts.opt_flat.clone()
+    mid = mgr.reshard(strats[1])
+    ok = (mid is None) == (rank == 1)
+    if mid is not None:
+        ok &= torch.equal(mid.opt_flat, O0) and torch.equal(mid.param_flat, P0)
+    back = mgr.reshard(strats[0])
+    ok &= torch.equal(back.param_flat, P0) and torch.equal(back.opt_flat, O0)
+    loss = train_step(back, mgr.build_iterators(4)[0])["loss"]
+    return bool(ok), loss
+
+
+def test_group_zero_replica_rebuild_two_gpus():
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    from dist_utils import run_distributed
+
+    res = run_distributed(_group_zero_two_gpus, 2, backend="nccl")
+    assert all(r[0] for r in res), res
+    assert res[0][1] == res[1][1]
