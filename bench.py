@@ -168,7 +168,7 @@ def main():
     cfg = preset(args.model, max_tensor_parallel_size=8, **over)
     gbs = args.per_gpu_batch * world
     tc = TrainConfig(micro_batch_size=1, global_batch_size=gbs, lr=3e-4, min_lr=3e-5, lr_warmup_iters=2,
-                     train_iters=1000, overlap_grad_reduce=world > 1, seed=0)
+                     train_iters=1000, overlap_grad_reduce=world > 1, overlap_param_gather=world > 1, seed=0)
     set_args(Args(model=cfg, train=tc))
     tp, pp = args.tp, args.pp
     base = dict(world_size=world, tensor_model_parallel_size=tp, pipeline_model_parallel_size=pp,

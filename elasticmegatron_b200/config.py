@@ -115,6 +115,9 @@ class TrainConfig:
     # DDP / ZeRO
     use_distributed_optimizer: bool = True
     overlap_grad_reduce: bool = False
+    # leave the parameter all-gathers after the optimizer step in flight; the next forward waits per bucket
+    # (Megatron's --overlap-param-gather)
+    overlap_param_gather: bool = False
     ddp_bucket_size: Optional[int] = None
     grad_reduce_in_fp32: bool = True
     # memory: recompute every transformer layer's activations in backward (keep only layer inputs)

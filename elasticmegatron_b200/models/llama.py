@@ -116,6 +116,14 @@ class GPTStage(nn.Module):
             return x, self._norm(x, weight_name)
         return F_.add_rmsnorm(x, pending, self.params_by_name[weight_name], self.cfg.norm_epsilon)
 
+    def _wait_params(self, key) -> None:
+        """Wait for the parameter all-gathers (left in flight by the last optimizer step) of the buckets that
+        hold the parameters read first by ``key`` (local layer index, 'pre', 'post')."""
+        ts = self.__dict__.get("_training_state")
+        ddp = ts.__dict__.get("ddp") if ts is not None else None
+        if ddp is not None:
+            ddp.wait_params(key)
+
     def rebind(self, views: Dict[str, torch.Tensor]) -> None:
         """Point every parameter at a new arena (after a release / rebuild)."""
         for n, p in self.params_by_name.items():
@@ -131,6 +139,7 @@ class GPTStage(nn.Module):
         cfg = self.cfg
         seq_local = cfg.seq_length // self.cp
         b = self.mbs
+        self._wait_params("pre")
         if self.first:
             # inp: token ids [b, s_local] -> [s_local * b] seq-major
             ids = inp.t().contiguous().view(-1)
@@ -147,6 +156,7 @@ class GPTStage(nn.Module):
         # consumes it (the next layer's input norm, or the final norm)
         pending = None
         for i in range(self.num_local_layers):
+            self._wait_params(i)
             if recompute:
                 # early stop off: every rank replays the whole layer, so its collectives run in full and in
                 # the same order on all ranks of each group
@@ -159,6 +169,7 @@ class GPTStage(nn.Module):
                 aux_total = aux if aux_total is None else aux_total + aux
         if not self.last:
             return (x + pending if pending is not None else x), aux_total
+        self._wait_params("post")
         _, x = self._add_norm(x, pending, "decoder.final_layernorm.weight")
         # untied, or the last stage's copy of a tied embedding; at PP=1 a tied head is the embedding itself
         w_out = self.params_by_name.get("output_layer.weight")

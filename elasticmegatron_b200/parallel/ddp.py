@@ -22,33 +22,44 @@ import torch.distributed as dist
 from ..planner.layout import RankLayout
 
 
-def _rs_inplace(buf: torch.Tensor, shard_index: int, group) -> None:
-    """Reduce-scatter (SUM) ``buf`` over ``group``; shard ``shard_index`` of ``buf`` receives the result."""
+def _rs_inplace(buf: torch.Tensor, shard_index: int, group, async_op: bool = False):
+    """Reduce-scatter (SUM) ``buf`` over ``group``; shard ``shard_index`` of ``buf`` receives the result.
+    With ``async_op`` the collective runs on the communicator's stream and the returned work is waited later
+    (the gradients of the bucket are final, so backward may continue meanwhile)."""
     if group is None:
-        return
+        return None
     n = dist.get_world_size(group)
     if n == 1:
-        return
+        return None
     if buf.is_cuda:
         c = buf.numel() // n
-        dist.reduce_scatter_tensor(buf[shard_index * c:(shard_index + 1) * c], buf, group=group)
-    else:
-        dist.all_reduce(buf, group=group)
+        return dist.reduce_scatter_tensor(buf[shard_index * c:(shard_index + 1) * c], buf, group=group,
+                                          async_op=async_op)
+    return dist.all_reduce(buf, group=group, async_op=async_op)
 
 
-def _ag_inplace(buf: torch.Tensor, shard_index: int, group) -> None:
+def _ag_inplace(buf: torch.Tensor, shard_index: int, group, async_op: bool = False):
     if group is None:
-        return
+        return None
     n = dist.get_world_size(group)
     if n == 1:
-        return
+        return None
     c = buf.numel() // n
     if buf.is_cuda:
-        dist.all_gather_into_tensor(buf, buf[shard_index * c:(shard_index + 1) * c], group=group)
-    else:
-        parts = list(buf.chunk(n))
-        mine = parts[shard_index].clone()
-        dist.all_gather(parts, mine, group=group)
+        return dist.all_gather_into_tensor(buf, buf[shard_index * c:(shard_index + 1) * c], group=group,
+                                           async_op=async_op)
+    parts = list(buf.chunk(n))
+    mine = parts[shard_index].clone()
+    dist.all_gather(parts, mine, group=group)
+    return None
+
+
+def _param_key(lp) -> object:
+    """Which part of the forward first reads a parameter: its layer, 'pre' (embedding) or 'post' (final norm,
+    output layer)."""
+    if lp.layer_local is not None:
+        return lp.layer_local
+    return "pre" if lp.name.startswith("embedding") else "post"
 
 
 class DistributedDataParallel:
@@ -65,6 +76,15 @@ class DistributedDataParallel:
         self._pending: List = []
         self._ready: Dict[int, int] = {}
         self._launched = set()
+        self._rs_works: List = []
+        # in-flight parameter all-gathers: (forward keys the bucket's parameters belong to, work)
+        self._ag_pending: List = []
+        self._bucket_keys = {}
+        for kind, bl in (("dense", layout.dense), ("expert", layout.expert)):
+            if bl is None:
+                continue
+            for b in range(len(bl.buckets)):
+                self._bucket_keys[(kind, b)] = {_param_key(bl.params[j]) for j in bl.bucket_params[b]}
         # gradient reduction is only started from backward hooks while this is True (the last
         # micro-batch); earlier micro-batches just accumulate (the reference's ``no_sync``)
         self.sync_enabled = True
@@ -147,7 +167,10 @@ class DistributedDataParallel:
         if i in self._launched:
             return
         self._launched.add(i)
-        _rs_inplace(self.grad_arena[s:e], zi, g)
+        # asynchronous: the reduction of this bucket overlaps the rest of backward
+        w = _rs_inplace(self.grad_arena[s:e], zi, g, async_op=True)
+        if w is not None:
+            self._rs_works.append(w)
 
     def zero_grad(self) -> None:
         if self.grad_arena is not None:
@@ -172,6 +195,9 @@ class DistributedDataParallel:
             for p in tied:
                 dist.all_reduce(p.main_grad, group=eg)
         views = self._bucket_views()
+        for w in self._rs_works:
+            w.wait()
+        self._rs_works = []
         for i, (kind, b, s, e, zi, g, ig) in enumerate(views):
             if i not in getattr(self, "_launched", set()):
                 _rs_inplace(self.grad_arena[s:e], zi, g)
@@ -182,10 +208,31 @@ class DistributedDataParallel:
                 c = (e - s) // n
                 dist.all_reduce(self.grad_arena[s + zi * c:s + (zi + 1) * c], group=ig)
 
-    def start_param_sync(self) -> None:
-        for kind, b, s, e, zi, g, ig in self._bucket_views():
-            if g is not None:
-                _ag_inplace(self.param_arena[s:e], zi, g)
+    def start_param_sync(self, overlap: bool = False) -> None:
+        """All-gather the updated parameter shards, bucket by bucket.  With ``overlap`` the gathers are left in
+        flight, launched in the order the next forward needs them (the buffer holds parameters in reverse
+        forward order, so the last bucket first); the forward waits for each bucket just before the first layer
+        that reads it (``wait_params``), and every other reader of the arena waits for all of them."""
+        self.wait_params()
+        for kind, b, s, e, zi, g, ig in reversed(self._bucket_views()):
+            if g is None:
+                continue
+            w = _ag_inplace(self.param_arena[s:e], zi, g, async_op=overlap)
+            if w is not None:
+                self._ag_pending.append((self._bucket_keys.get((kind, b), set()), w))
+
+    def wait_params(self, key=None) -> None:
+        """Make the current stream wait for the in-flight parameter all-gathers of the buckets that hold
+        parameters read first by ``key`` (a local layer index, 'pre' or 'post'); all of them when None."""
+        if not self._ag_pending:
+            return
+        keep = []
+        for keys, w in self._ag_pending:
+            if key is None or key in keys:
+                w.wait()
+            else:
+                keep.append((keys, w))
+        self._ag_pending = keep
 
     def remove_hooks(self):
         for h in self._hooks:

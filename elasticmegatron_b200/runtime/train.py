@@ -54,7 +54,7 @@ def train_step(ts, data_iter: Iterator, hetero_dp: Optional[bool] = None, return
     loss_sums = fb(ctx)
     ts.ddp.finish_grad_sync()
     ok, gnorm = ts.optimizer.step()
-    ts.ddp.start_param_sync()
+    ts.ddp.start_param_sync(overlap=tc.overlap_param_gather)
     ts.opt_param_scheduler.step(n_mb * tc.micro_batch_size * s.data_parallel_size if not hetero_dp
                                 else tc.global_batch_size)
     out = {"grad_norm": gnorm, "num_microbatches": n_mb, "update_successful": ok}

@@ -76,6 +76,11 @@ class TrainingState:
     # ------------------------------------------------------------------ arenas
     @property
     def param_flat(self) -> Optional[torch.Tensor]:
+        # a reader of the whole arena (switch, checkpoint, checksum) must see the gathered parameters: wait for
+        # any all-gather the last step left in flight (no-op otherwise)
+        ddp = self.__dict__.get("ddp")
+        if ddp is not None:
+            ddp.wait_params()
         return self.param_arena.view(self.param_dtype, (self.layout.param_numel,)) if self.param_arena else None
 
     @property
@@ -110,6 +115,8 @@ class TrainingState:
     def release_model(self) -> None:
         if self.model_released:
             return
+        if self.__dict__.get("ddp") is not None:
+            self.ddp.wait_params()  # no all-gather may still write into the arena handed back to the pool
         self.pool.free(self.param_arena)
         self.pool.free(self.grad_arena)
         self.param_arena = self.grad_arena = None
