@@ -13,6 +13,10 @@ int64_t ipc_open_count();
 std::vector<torch::Tensor> rmsnorm_fwd(torch::Tensor x, torch::Tensor w, double eps);
 std::vector<torch::Tensor> rmsnorm_bwd(torch::Tensor dy, torch::Tensor x, torch::Tensor w, torch::Tensor rstd,
                                        c10::optional<torch::Tensor> dw_accum, c10::optional<torch::Tensor> dres);
+std::vector<torch::Tensor> layernorm_fwd(torch::Tensor x, torch::Tensor w, torch::Tensor b, double eps);
+std::vector<torch::Tensor> layernorm_bwd(torch::Tensor dy, torch::Tensor x, torch::Tensor w, torch::Tensor mean,
+                                         torch::Tensor rstd, c10::optional<torch::Tensor> dw_accum,
+                                         c10::optional<torch::Tensor> db_accum);
 std::vector<torch::Tensor> add_rmsnorm_fwd(torch::Tensor x, torch::Tensor o, torch::Tensor w, double eps);
 torch::Tensor swiglu_fwd(torch::Tensor h);
 torch::Tensor swiglu_bwd(torch::Tensor dy, torch::Tensor h);
@@ -85,6 +89,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("rmsnorm_bwd", &rmsnorm_bwd, py::arg("dy"), py::arg("x"), py::arg("w"), py::arg("rstd"),
         py::arg("dw_accum") = py::none(), py::arg("dres") = py::none());
   m.def("add_rmsnorm_fwd", &add_rmsnorm_fwd);
+  m.def("layernorm_fwd", &layernorm_fwd);
+  m.def("layernorm_bwd", &layernorm_bwd, py::arg("dy"), py::arg("x"), py::arg("w"), py::arg("mean"), py::arg("rstd"),
+        py::arg("dw_accum") = py::none(), py::arg("db_accum") = py::none());
   m.def("swiglu_fwd", &swiglu_fwd);
   m.def("swiglu_bwd", &swiglu_bwd);
   m.def("rope_fwd", &rope_fwd);

@@ -265,6 +265,196 @@ std::vector<at::Tensor> rmsnorm_bwd(at::Tensor dy, at::Tensor x, at::Tensor w, a
   return {dx, dw};
 }
 
+// ------------------------------------------------------------------------------------------ LayerNorm
+// Megatron's LayerNorm (weight and bias) over the last dimension, bf16 I/O, fp32 statistics: one CTA per row
+// in the forward; the backward runs persistent CTAs that keep per-CTA fp32 partials of dw and db (reduced in
+// a fixed order by colsum_kernel, so the result is deterministic), like the RMSNorm backward.
+template <int VPT>
+__global__ void layernorm_fwd_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ w,
+                                     const __nv_bfloat16* __restrict__ bias, __nv_bfloat16* __restrict__ y,
+                                     float* __restrict__ mean_out, float* __restrict__ rstd_out, int H, float eps) {
+  __shared__ float sh[32];
+  const int row = blockIdx.x;
+  const int nvec = H / 8;
+  const uint4* xr = reinterpret_cast<const uint4*>(x + (size_t)row * H);
+  float v[VPT][8];
+  float sum = 0.f;
+#pragma unroll
+  for (int k = 0; k < VPT; ++k) {
+    int i = threadIdx.x + k * blockDim.x;
+    if (i < nvec) {
+      unpack8(xr[i], v[k]);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) sum += v[k][j];
+    }
+  }
+  const float mu = block_sum(sum, sh) / H;
+  float ss = 0.f;
+#pragma unroll
+  for (int k = 0; k < VPT; ++k) {
+    int i = threadIdx.x + k * blockDim.x;
+    if (i < nvec) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float d = v[k][j] - mu;
+        ss += d * d;
+      }
+    }
+  }
+  const float r = rsqrtf(block_sum(ss, sh) / H + eps);
+  if (threadIdx.x == 0) {
+    mean_out[row] = mu;
+    rstd_out[row] = r;
+  }
+  const uint4* wr = reinterpret_cast<const uint4*>(w);
+  const uint4* br = reinterpret_cast<const uint4*>(bias);
+  uint4* yr = reinterpret_cast<uint4*>(y + (size_t)row * H);
+#pragma unroll
+  for (int k = 0; k < VPT; ++k) {
+    int i = threadIdx.x + k * blockDim.x;
+    if (i < nvec) {
+      float wf[8], bf[8], o[8];
+      unpack8(wr[i], wf);
+      unpack8(br[i], bf);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) o[j] = (v[k][j] - mu) * r * wf[j] + bf[j];
+      yr[i] = pack8(o);
+    }
+  }
+}
+
+template <int VPT>
+__global__ void layernorm_bwd_kernel(const __nv_bfloat16* __restrict__ dy, const __nv_bfloat16* __restrict__ x,
+                                     const __nv_bfloat16* __restrict__ w, const float* __restrict__ mean,
+                                     const float* __restrict__ rstd, __nv_bfloat16* __restrict__ dx,
+                                     float* __restrict__ dw_part, float* __restrict__ db_part, int T, int H) {
+  __shared__ float sh[32];
+  const int nvec = H / 8;
+  const uint4* wr = reinterpret_cast<const uint4*>(w);
+  float wf[VPT][8], accw[VPT][8], accb[VPT][8];
+#pragma unroll
+  for (int k = 0; k < VPT; ++k) {
+    int i = threadIdx.x + k * blockDim.x;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) accw[k][j] = accb[k][j] = 0.f;
+    if (i < nvec) unpack8(wr[i], wf[k]);
+  }
+  for (int row = blockIdx.x; row < T; row += gridDim.x) {
+    const uint4* xr = reinterpret_cast<const uint4*>(x + (size_t)row * H);
+    const uint4* dr = reinterpret_cast<const uint4*>(dy + (size_t)row * H);
+    const float mu = mean[row], r = rstd[row];
+    float xh[VPT][8], g[VPT][8];
+    float sg = 0.f, sgx = 0.f;
+#pragma unroll
+    for (int k = 0; k < VPT; ++k) {
+      int i = threadIdx.x + k * blockDim.x;
+      if (i < nvec) {
+        float d[8];
+        unpack8(xr[i], xh[k]);
+        unpack8(dr[i], d);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          xh[k][j] = (xh[k][j] - mu) * r;
+          g[k][j] = d[j] * wf[k][j];
+          sg += g[k][j];
+          sgx += g[k][j] * xh[k][j];
+          accw[k][j] += d[j] * xh[k][j];
+          accb[k][j] += d[j];
+        }
+      }
+    }
+    // dx = r * (g - mean(g) - xhat * mean(g * xhat))
+    const float mg = block_sum(sg, sh) / H;
+    const float mgx = block_sum(sgx, sh) / H;
+    uint4* o = reinterpret_cast<uint4*>(dx + (size_t)row * H);
+#pragma unroll
+    for (int k = 0; k < VPT; ++k) {
+      int i = threadIdx.x + k * blockDim.x;
+      if (i < nvec) {
+        float t[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) t[j] = r * (g[k][j] - mg - xh[k][j] * mgx);
+        o[i] = pack8(t);
+      }
+    }
+  }
+  float* pw = dw_part + (size_t)blockIdx.x * H;
+  float* pb = db_part + (size_t)blockIdx.x * H;
+#pragma unroll
+  for (int k = 0; k < VPT; ++k) {
+    int i = threadIdx.x + k * blockDim.x;
+    if (i < nvec) {
+      float4* w4 = reinterpret_cast<float4*>(pw + i * 8);
+      float4* b4 = reinterpret_cast<float4*>(pb + i * 8);
+      w4[0] = make_float4(accw[k][0], accw[k][1], accw[k][2], accw[k][3]);
+      w4[1] = make_float4(accw[k][4], accw[k][5], accw[k][6], accw[k][7]);
+      b4[0] = make_float4(accb[k][0], accb[k][1], accb[k][2], accb[k][3]);
+      b4[1] = make_float4(accb[k][4], accb[k][5], accb[k][6], accb[k][7]);
+    }
+  }
+}
+
+// Returns (y, mean, rstd).
+std::vector<at::Tensor> layernorm_fwd(at::Tensor x, at::Tensor w, at::Tensor b, double eps) {
+  check_cuda_bf16(x, "x");
+  check_cuda_bf16(w, "w");
+  check_cuda_bf16(b, "b");
+  TORCH_CHECK(x.dim() == 2, "layernorm_fwd: x must be [T, H]");
+  const int64_t T = x.size(0), H = x.size(1);
+  TORCH_CHECK(H % 8 == 0 && H <= 8 * 4 * 1024, "hidden size must be a multiple of 8 and <= 32768");
+  auto y = at::empty_like(x);
+  auto mean = at::empty({T}, x.options().dtype(at::kFloat));
+  auto rstd = at::empty({T}, x.options().dtype(at::kFloat));
+  if (T == 0) return {y, mean, rstd};
+  int vpt;
+  int threads = pick_threads((int)(H / 8), vpt);
+  auto st = cur_stream();
+#define L(V) layernorm_fwd_kernel<V><<<T, threads, 0, st>>>((const __nv_bfloat16*)x.data_ptr(),                  \
+      (const __nv_bfloat16*)w.data_ptr(), (const __nv_bfloat16*)b.data_ptr(), (__nv_bfloat16*)y.data_ptr(),      \
+      mean.data_ptr<float>(), rstd.data_ptr<float>(), (int)H, (float)eps)
+  if (vpt <= 1) L(1); else if (vpt == 2) L(2); else if (vpt == 3) L(3); else L(4);
+#undef L
+  EMB_LAUNCH_CHECK();
+  count_launch();
+  return {y, mean, rstd};
+}
+
+// Returns (dx, dw, db); dw / db are fp32 and, when given, accumulated into dw_accum / db_accum.
+std::vector<at::Tensor> layernorm_bwd(at::Tensor dy, at::Tensor x, at::Tensor w, at::Tensor mean, at::Tensor rstd,
+                                      c10::optional<at::Tensor> dw_accum, c10::optional<at::Tensor> db_accum) {
+  check_cuda_bf16(dy, "dy");
+  check_cuda_bf16(x, "x");
+  check_cuda_bf16(w, "w");
+  const int64_t T = x.size(0), H = x.size(1);
+  auto dx = at::empty_like(x);
+  int vpt;
+  int threads = pick_threads((int)(H / 8), vpt);
+  int grid = (int)std::min<int64_t>(std::max<int64_t>(T, 1), (int64_t)num_sms() * 2);
+  auto part = at::zeros({2, grid, H}, x.options().dtype(at::kFloat));
+  auto st = cur_stream();
+  if (T > 0) {
+#define L(V) layernorm_bwd_kernel<V><<<grid, threads, 0, st>>>((const __nv_bfloat16*)dy.data_ptr(),                \
+      (const __nv_bfloat16*)x.data_ptr(), (const __nv_bfloat16*)w.data_ptr(), mean.data_ptr<float>(),              \
+      rstd.data_ptr<float>(), (__nv_bfloat16*)dx.data_ptr(), part.data_ptr<float>(),                                \
+      part.data_ptr<float>() + (size_t)grid * H, (int)T, (int)H)
+    if (vpt <= 1) L(1); else if (vpt == 2) L(2); else if (vpt == 3) L(3); else L(4);
+#undef L
+    EMB_LAUNCH_CHECK();
+  }
+  at::Tensor dw, db;
+  const bool aw = dw_accum.has_value() && dw_accum->defined(), ab = db_accum.has_value() && db_accum->defined();
+  dw = aw ? *dw_accum : at::empty({H}, x.options().dtype(at::kFloat));
+  db = ab ? *db_accum : at::empty({H}, x.options().dtype(at::kFloat));
+  TORCH_CHECK(dw.scalar_type() == at::kFloat && dw.is_contiguous() && dw.numel() == H);
+  TORCH_CHECK(db.scalar_type() == at::kFloat && db.is_contiguous() && db.numel() == H);
+  colsum_kernel<<<(H + 255) / 256, 256, 0, st>>>(part.data_ptr<float>(), dw.data_ptr<float>(), grid, (int)H, aw);
+  colsum_kernel<<<(H + 255) / 256, 256, 0, st>>>(part.data_ptr<float>() + (size_t)grid * H, db.data_ptr<float>(),
+                                                 grid, (int)H, ab);
+  EMB_LAUNCH_CHECK();
+  count_launch(T > 0 ? 3 : 2);
+  return {dx, dw, db};
+}
+
 // ------------------------------------------------------------------------------------------ SwiGLU
 __global__ void swiglu_fwd_kernel(const __nv_bfloat16* __restrict__ h, __nv_bfloat16* __restrict__ y, int64_t T,
                                   int F) {

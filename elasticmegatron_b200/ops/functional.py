@@ -291,10 +291,43 @@ def add_rmsnorm(x, o, w, eps):
     return AddRMSNormFn.apply(x, o, w, eps)
 
 
+class LayerNormFn(torch.autograd.Function):
+    """LayerNorm on the native kernels (bf16 on CUDA): fp32 statistics, weight / bias gradients reduced in
+    fp32 straight into ``main_grad`` when the parameters have one (as the RMSNorm path does)."""
+
+    @staticmethod
+    def forward(ctx, x, w, b, eps):
+        x2 = x.reshape(-1, x.shape[-1]).contiguous()
+        y, mean, rstd = ext().layernorm_fwd(x2, w, b, eps)
+        ctx.save_for_backward(x2, w, b, mean, rstd)
+        return y.view(x.shape)
+
+    @staticmethod
+    def backward(ctx, dy):
+        x2, w, b, mean, rstd = ctx.saved_tensors
+        dy2 = dy.reshape(-1, dy.shape[-1]).contiguous()
+        mw, mb = getattr(w, "main_grad", None), getattr(b, "main_grad", None)
+        dx, dw, db = ext().layernorm_bwd(dy2, x2, w, mean, rstd, mw.view(-1) if mw is not None else None,
+                                         mb.view(-1) if mb is not None else None)
+        out_w, out_b = None, None
+        for p, m, g in ((w, mw, dw), (b, mb, db)):
+            if m is not None:
+                hook = getattr(p, "_grad_ready", None)
+                if hook is not None:
+                    hook()
+        if mw is None:
+            out_w = dw.to(w.dtype)
+        if mb is None:
+            out_b = db.to(b.dtype)
+        return dx.view(dy.shape), out_w, out_b, None
+
+
 def layernorm(x, w, b, eps):
-    """Megatron's LayerNorm (weight and bias) over the last dimension.  It runs the library kernel on both
-    host and device (as attention does by default); the weight and bias gradients reach ``main_grad``
-    through the data-parallel layer's accumulation hook."""
+    """Megatron's LayerNorm (weight and bias) over the last dimension: the native kernels for bf16 CUDA
+    tensors (hidden size a multiple of 8), PyTorch's ``layer_norm`` on the host."""
+    if (use_native(x) and x.dtype == torch.bfloat16 and w.dtype == torch.bfloat16 and x.shape[-1] % 8 == 0
+            and hasattr(ext(), "layernorm_fwd")):
+        return LayerNormFn.apply(x, w, b, eps)
     return torch.nn.functional.layer_norm(x, (x.shape[-1],), w, b, eps)
 
 

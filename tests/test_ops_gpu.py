@@ -161,3 +161,50 @@ def test_adam_and_sumsq():
         ref.adam_step(m, e1, e2, G[a:a + k], 1e-3, 0.9, 0.95, 1e-8, wd, 3, 0.5 * clip)
     _close(O, O_ref, 1e-6, 1e-5)
     _close(P, O_ref[0], 1e-2, 1e-2)
+
+
+@pytest.mark.parametrize("T,H", [(9, 512), (300, 4096)])
+def test_layernorm_native(T, H):
+    """Native LayerNorm forward / backward against the fp32 PyTorch reference."""
+    from elasticmegatron_b200.ops import functional as F_
+
+    torch.manual_seed(3)
+    x = torch.randn(T, H, device="cuda").bfloat16().requires_grad_(True)
+    w = (1 + 0.1 * torch.randn(H, device="cuda")).bfloat16().requires_grad_(True)
+    b = (0.1 * torch.randn(H, device="cuda")).bfloat16().requires_grad_(True)
+    n0 = _ext().launch_count()
+    y = F_.layernorm(x, w, b, 1e-5)
+    dy = torch.randn(T, H, device="cuda").bfloat16()
+    y.backward(dy)
+    assert _ext().launch_count() - n0 >= 3  # the native kernels ran
+    xr, wr, br = (t.detach().float().requires_grad_(True) for t in (x, w, b))
+    yr = torch.nn.functional.layer_norm(xr, (H,), wr, br, 1e-5)
+    yr.backward(dy.float())
+    _close(y, yr, 2e-2, 2e-2)
+    _close(x.grad, xr.grad, 3e-2, 3e-2)
+    _close(w.grad, wr.grad, 5e-2 * math.sqrt(T / 8), 2e-2)
+    _close(b.grad, br.grad, 5e-2 * math.sqrt(T / 8), 2e-2)
+
+
+def test_layernorm_model_trains_on_gpu():
+    """The reference demo's LayerNorm model (weight + bias per norm) takes training steps on one GPU through the
+    native kernels: finite losses near ln(vocab) on the uniform synthetic tokens, and the weights move."""
+    from elasticmegatron_b200.config import Args, ModelConfig, TrainConfig, set_args
+    from elasticmegatron_b200.parallel.strategy import ParallelStrategy
+    from elasticmegatron_b200.runtime.data import DataloaderState
+    from elasticmegatron_b200.runtime.train import train_step
+    from elasticmegatron_b200.runtime.training_state import TrainingState
+
+    cfg = ModelConfig(num_layers=2, hidden_size=256, num_attention_heads=4, ffn_hidden_size=512, vocab_size=1000,
+                      seq_length=128, params_dtype="bf16", normalization="LayerNorm",
+                      make_vocab_size_divisible_by=8)
+    set_args(Args(model=cfg, train=TrainConfig(micro_batch_size=2, global_batch_size=4, lr=3e-3)))
+    ts = TrainingState(ParallelStrategy(world_size=1, tensor_model_parallel_size=1, pipeline_model_parallel_size=1))
+    ts.init_weights(0)
+    it = DataloaderState.build_iterators(ts, 0)[0]
+    n0 = _ext().launch_count()
+    p0 = ts.param_flat.clone()
+    losses = [train_step(ts, it)["loss"] for _ in range(3)]
+    assert _ext().launch_count() > n0
+    assert all(5.0 < l < 9.0 for l in losses), losses
+    assert not torch.equal(p0, ts.param_flat)
