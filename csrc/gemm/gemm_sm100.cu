@@ -635,21 +635,20 @@ __global__ void __launch_bounds__(AG ? NUM_THREADS_AG : NUM_THREADS, 1)
           uint8_t* b_dst = sB + s * B_HALF;
           const int k0 = kb * BK;
           // K-major: 64-wide K panels of 128 rows, 16 KiB apart.  MN-major: 64-wide M (N) panels of BK K-rows,
-          // BK * 128 bytes apart, each loaded as 64 x 64 boxes.
+          // BK * 128 bytes apart, one {64, BK} box each (the MN-major tensor maps have BK-row boxes).
+          if (!p.a_mn) {
 #pragma unroll
-          for (int h = 0; h < BK / 64; ++h) {
-            if (!p.a_mn) {
-              tma_load_2d_pair(a_dst + h * 16384, &tmA, bar, k0 + 64 * h, m0);
-            } else {
-              tma_load_2d_pair(a_dst + h * 8192, &tmA, bar, m0, k0 + 64 * h);
-              tma_load_2d_pair(a_dst + BK * 128 + h * 8192, &tmA, bar, m0 + 64, k0 + 64 * h);
-            }
-            if (!p.b_mn) {
-              tma_load_2d_pair(b_dst + h * 16384, &tmB, bar, k0 + 64 * h, n0);
-            } else {
-              tma_load_2d_pair(b_dst + h * 8192, &tmB, bar, n0, k0 + 64 * h);
-              tma_load_2d_pair(b_dst + BK * 128 + h * 8192, &tmB, bar, n0 + 64, k0 + 64 * h);
-            }
+            for (int h = 0; h < BK / 64; ++h) tma_load_2d_pair(a_dst + h * 16384, &tmA, bar, k0 + 64 * h, m0);
+          } else {
+            tma_load_2d_pair(a_dst, &tmA, bar, m0, k0);
+            tma_load_2d_pair(a_dst + BK * 128, &tmA, bar, m0 + 64, k0);
+          }
+          if (!p.b_mn) {
+#pragma unroll
+            for (int h = 0; h < BK / 64; ++h) tma_load_2d_pair(b_dst + h * 16384, &tmB, bar, k0 + 64 * h, n0);
+          } else {
+            tma_load_2d_pair(b_dst, &tmB, bar, n0, k0);
+            tma_load_2d_pair(b_dst + BK * 128, &tmB, bar, n0 + 64, k0);
           }
           if (timing) t_issue += clk() - t1;
         }
@@ -1109,8 +1108,8 @@ at::Tensor gemm_tc(at::Tensor a, at::Tensor b, bool trans_a, bool trans_b, c10::
   p.probe = variant == 13 ? 4 : variant == 14 ? 6 : (variant >= 10 ? variant - 9 : 0);
   if (pair) {
     // 2-SM clusters: each CTA loads a 128-row half of the A tile and of the B tile
-    CUtensorMap tA2 = a_mn ? tA : make_map(a.data_ptr(), M, K, a.stride(0), 64, 128);
-    CUtensorMap tB2 = b_mn ? tB : make_map(b.data_ptr(), N, K, b.stride(0), 64, 128);
+    CUtensorMap tA2 = a_mn ? make_map(a.data_ptr(), K, M, a.stride(0), 64, bk) : make_map(a.data_ptr(), M, K, a.stride(0), 64, 128);
+    CUtensorMap tB2 = b_mn ? make_map(b.data_ptr(), K, N, b.stride(0), 64, bk) : make_map(b.data_ptr(), N, K, b.stride(0), 64, 128);
     // C through a tensor map when its rows are 16-byte aligned: 32-row boxes of 128 bytes, 128-byte swizzle
     CUtensorMap tC = tA2;
     const int esz = p.out_fp32 ? 4 : 2;
@@ -1260,8 +1259,9 @@ void gemm_rs(at::Tensor a, at::Tensor b, bool trans_a, bool trans_b, at::Tensor 
               "gemm_rs: M must equal tp * rows_per_rank, tp <= 8, N % 8 == 0");
   auto pc = peers.to(at::kCPU).contiguous();
   const bool a_mn = trans_a, b_mn = !trans_b;
-  CUtensorMap tA = a_mn ? make_map(a.data_ptr(), K, M, a.stride(0), 64, 64) : make_map(a.data_ptr(), M, K, a.stride(0), 64, 128);
-  CUtensorMap tB = b_mn ? make_map(b.data_ptr(), K, N, b.stride(0), 64, 64) : make_map(b.data_ptr(), N, K, b.stride(0), 64, 128);
+  const int bk2 = gemm2_default_bk();
+  CUtensorMap tA = a_mn ? make_map(a.data_ptr(), K, M, a.stride(0), 64, bk2) : make_map(a.data_ptr(), M, K, a.stride(0), 64, 128);
+  CUtensorMap tB = b_mn ? make_map(b.data_ptr(), K, N, b.stride(0), 64, bk2) : make_map(b.data_ptr(), N, K, b.stride(0), 64, 128);
   Params p{};
   p.C = nullptr;
   p.M = (int)M;
@@ -1306,7 +1306,8 @@ at::Tensor gemm_ag(at::Tensor local, at::Tensor b, bool trans_b, at::Tensor peer
   auto fc = flags.to(at::kCPU).contiguous();
   const bool b_mn = !trans_b;
   CUtensorMap tA = make_map(local.data_ptr(), M, K, local.stride(0), 64, 128);
-  CUtensorMap tB = b_mn ? make_map(b.data_ptr(), K, N, b.stride(0), 64, 64) : make_map(b.data_ptr(), N, K, b.stride(0), 64, 128);
+  CUtensorMap tB = b_mn ? make_map(b.data_ptr(), K, N, b.stride(0), 64, gemm2_default_bk())
+                        : make_map(b.data_ptr(), N, K, b.stride(0), 64, 128);
   auto C = at::empty({M, N}, local.options());
   Params p{};
   p.C = C.data_ptr();
