@@ -57,7 +57,8 @@ class ElasticMegatronManager:
     def __init__(self, parallel_strategy_list: List[Union[Dict, ParallelStrategy, str]], model=None, optimizer=None,
                  opt_param_scheduler=None, send_fn: Optional[Callable] = None, recv_fn: Optional[Callable] = None,
                  broadcast_fn: Optional[Callable] = None, use_p2p_to_collective: Optional[bool] = None,
-                 training_state: Optional[TrainingState] = None, engine: Optional[str] = None):
+                 training_state: Optional[TrainingState] = None, engine: Optional[str] = None,
+                 prebuild_plans: Optional[bool] = None):
         """``send_fn`` / ``recv_fn`` / ``broadcast_fn`` / ``use_p2p_to_collective`` keep the reference's
         injectable communicator (elastic_manager.py:41-58): when any is given, switches run the reference's
         transfer schedule through those functions; otherwise ``engine`` picks the transfer engine
@@ -94,6 +95,22 @@ class ElasticMegatronManager:
         self._warm_only = False
         set_world_group(ProcessGroupPool.get(self.current.ranks))
         self.memory_warnings = self._check_memory()
+        # every declared switch's plan is host work that depends only on the two strategies: build them all now
+        # (default for up to 8 strategies) so a switch's first occurrence does not pay for planning
+        if prebuild_plans is None:
+            prebuild_plans = len(self.strategies) <= 8 and os.environ.get("EMB_PREBUILD_PLANS", "1") != "0"
+        self.plan_prebuild_ms = self.prebuild_plans() if prebuild_plans else 0.0
+
+    def prebuild_plans(self) -> float:
+        """Build the plans of all ordered pairs of declared strategies (host only); returns the time in ms."""
+        import time
+
+        t0 = time.perf_counter()
+        for a in self.strategies:
+            for b in self.strategies:
+                if a != b:
+                    self.plan(a, b)
+        return (time.perf_counter() - t0) * 1e3
 
     def _check_memory(self) -> List[Dict]:
         """Warn (one JSON line each, never fail) about switches whose source and destination state cannot sit
