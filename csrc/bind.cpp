@@ -47,6 +47,11 @@ torch::Tensor attn_bwd(torch::Tensor dO, torch::Tensor qkv, torch::Tensor o, tor
 int64_t attn_bwd_error_flag();
 int64_t gemm_error_flag();
 at::Tensor attn_exp2_emulated(at::Tensor x);
+void dp_signal(at::Tensor flags, int64_t me, int64_t slot0, int64_t nslots, int64_t epoch);
+void dp_rs_pull(at::Tensor peers, int64_t me, int64_t off, int64_t count, at::Tensor flags, int64_t slot,
+                int64_t epoch, int64_t timeout_ms);
+void dp_ag_pull(at::Tensor peers, int64_t me, int64_t off, int64_t shard_bytes, at::Tensor flags, int64_t slot,
+                int64_t epoch, int64_t timeout_ms);
 std::vector<int64_t> attn_debug_counters();
 std::vector<int64_t> gemm_debug_counters();
 void gemm_rs(torch::Tensor a, torch::Tensor b, bool trans_a, bool trans_b, torch::Tensor peers, int64_t my_slot,
@@ -117,6 +122,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("attn_bwd_error_flag", &attn_bwd_error_flag);
   m.def("attn_error_flag", &attn_error_flag);
   m.def("attn_exp2_emulated", &attn_exp2_emulated);
+  m.def("dp_signal", &dp_signal);
+  m.def("dp_rs_pull", &dp_rs_pull);
+  m.def("dp_ag_pull", &dp_ag_pull);
   m.def("attn_debug_counters", &attn_debug_counters);
   m.def("gemm_error_flag", &gemm_error_flag);
   m.def("gemm_debug_counters", &gemm_debug_counters);

@@ -17,7 +17,10 @@ output gradients like a dispatch; dispatch backward returns the input gradients 
 
 Buffers are symmetric arenas of the EP group (``ops/tp_fused.SymmetricBuffer``) with two halves used on
 alternate calls, so a call never overwrites data a peer may still read (each call ends with a barrier that
-every rank passes only after finishing its previous calls).  Reference behaviour being replaced: Megatron's
+every rank passes only after finishing its previous calls).  A plan looks its buffers up at every movement: a
+later layer with more rows grows (replaces) a buffer, and the plan of an earlier layer, kept for its backward,
+must not use the replaced buffer's closed peer mappings.  Every rank of the group asks for the same sizes in the
+same order (the sizes are maxima over the group), so a grow stays collective.  Reference behaviour being replaced: Megatron's
 alltoall token dispatcher (``--moe-token-dispatcher-type alltoall``, run_moe.sh:66).
 """
 from __future__ import annotations
@@ -86,11 +89,20 @@ class EPPlan:
         self.pos_send, self.seg_send, _ = ext().moe_layout(self.gid, counts.to(torch.int32).contiguous(),
                                                            max(self.gid.numel(), 1), 1)
         self.ident = torch.arange(self.T * self.k, device=dev, dtype=torch.int32)
-        nb = self.H * 2
-        self.land = _buffer(group, self.cap_max * nb, dev, "ep_land", 1 << 20)
-        self.org = _buffer(group, self.cap_max * 4, dev, "ep_org", 1 << 16)
-        self.ret = _buffer(group, self.T * self.k * nb, dev, "ep_ret", 1 << 20)
+        self.dev = dev
         self.origin = None
+
+    @property
+    def land(self):
+        return _buffer(self.group, self.cap_max * self.H * 2, self.dev, "ep_land", 1 << 20)
+
+    @property
+    def org(self):
+        return _buffer(self.group, self.cap_max * 4, self.dev, "ep_org", 1 << 16)
+
+    @property
+    def ret(self):
+        return _buffer(self.group, self.T * self.k * self.H * 2, self.dev, "ep_ret", 1 << 20)
 
     def layout(self) -> dict:
         return {"seg": self.seg, "tiles": self.tiles, "counts": self.counts, "cap": self.cap}
@@ -98,17 +110,19 @@ class EPPlan:
     # -------------------------------------------------------------- the four movements
     def push(self, rows: torch.Tensor, w=None, with_origin: bool = False) -> torch.Tensor:
         """rows [T, H] (assignment r uses row r // k, scaled by w[r]) -> this rank's landing rows [cap, H]."""
-        h = self.land.next_half()
+        lb = self.land
+        h = lb.next_half()
         optrs = None
         if with_origin:
-            ho = self.org.next_half()
-            optrs = self.org.peers[ho]
+            ob = self.org
+            ho = ob.next_half()
+            optrs = ob.peers[ho]
         ext().ep_push(rows.contiguous(), self.k, self.gid, self.pos_send, self.seg_send, self.base, self.e_loc,
-                      None if w is None else w.reshape(-1).float().contiguous(), self.land.peers[h], optrs, self.me)
-        self.land.barrier()
-        land = self.land.view(h, torch.bfloat16, self.cap_max * self.H)[:self.cap * self.H].view(self.cap, self.H)
+                      None if w is None else w.reshape(-1).float().contiguous(), lb.peers[h], optrs, self.me)
+        lb.barrier()
+        land = lb.view(h, torch.bfloat16, self.cap_max * self.H)[:self.cap * self.H].view(self.cap, self.H)
         if with_origin:
-            org = self.org.view(ho, torch.int32, self.cap_max)[:self.cap]
+            org = ob.view(ho, torch.int32, self.cap_max)[:self.cap]
             ext().ep_pad(land, self.seg, self.counts, org)
             self.origin = org.clone()
         else:
@@ -117,11 +131,13 @@ class EPPlan:
 
     def send_home(self, rows: torch.Tensor) -> torch.Tensor:
         """Landing-layout rows [cap, H] -> this rank's return rows [T * k, H] (its own assignments)."""
-        h = self.ret.next_half()
-        ext().ep_return(rows.contiguous(), self.origin, self.cap, self.ret.peers[h])
-        self.land.barrier()
+        rb = self.ret
+        lb = self.land
+        h = rb.next_half()
+        ext().ep_return(rows.contiguous(), self.origin, self.cap, rb.peers[h])
+        lb.barrier()
         n = self.T * self.k
-        return self.ret.view(h, torch.bfloat16, n * self.H).view(n, self.H).clone()
+        return rb.view(h, torch.bfloat16, n * self.H).view(n, self.H).clone()
 
 
 class _EPDispatchFn(torch.autograd.Function):

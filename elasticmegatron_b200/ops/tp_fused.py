@@ -73,6 +73,7 @@ class SymmetricBuffer:
         self.flag = torch.zeros(1, dtype=torch.float32, device=device)
         self.epoch = 0
         self.calls = 0
+        self.closed = False
 
     def next_half(self) -> int:
         h = self.calls & 1
@@ -88,6 +89,8 @@ class SymmetricBuffer:
         return self.arena[off: off + numel * torch.empty((), dtype=dtype).element_size()].view(dtype)
 
     def close(self):
+        # holders of this object (e.g. a peer-memory DDP) see ``closed`` and rebuild on the new buffer
+        self.closed = True
         for i, hh in enumerate(self.handles):
             if i != self.idx:
                 ext().ipc_close(torch.frombuffer(bytearray(hh), dtype=torch.uint8))
@@ -97,17 +100,22 @@ _BUFS: Dict[Tuple[int, int], SymmetricBuffer] = {}
 
 
 def _buffer(group, nbytes: int, device, tag: str = "", min_bytes: int = 64 << 20) -> SymmetricBuffer:
-    """The group's symmetric buffer named ``tag``, grown (collectively) to at least ``nbytes`` per half."""
+    """The group's symmetric buffer named ``tag``, grown (collectively) to at least ``nbytes`` per half.
+
+    Growing replaces the buffer: the old one's peer mappings are closed, so callers look the buffer up at every
+    use and never keep a ``SymmetricBuffer`` across calls that may grow it."""
     key = (id(group), device.index, tag)
     b = _BUFS.get(key)
     if b is None or b.half < nbytes:
+        grow = 0
         if b is not None:
             # every rank of the group grows at the same call (same shapes), so the swap stays collective;
             # nobody may still read or write the old arenas when they are unmapped and freed
             dist.all_reduce(b.flag, group=group)
             torch.cuda.synchronize(device)
             b.close()
-        b = SymmetricBuffer(group, max(nbytes, min_bytes), device)
+            grow = nbytes + nbytes // 4  # headroom: sizes that vary from call to call settle after a few grows
+        b = SymmetricBuffer(group, max(nbytes, min_bytes, grow), device)
         _BUFS[key] = b
     return b
 

@@ -20,6 +20,7 @@ import torch
 import torch.distributed as dist
 
 from ..planner.layout import RankLayout
+from . import dp_comm
 
 
 def _rs_inplace(buf: torch.Tensor, shard_index: int, group, async_op: bool = False):
@@ -54,6 +55,16 @@ def _ag_inplace(buf: torch.Tensor, shard_index: int, group, async_op: bool = Fal
     return None
 
 
+class _EventWait:
+    """A CUDA event with the ``wait()`` of a collective's work handle: the current stream waits for it."""
+
+    def __init__(self, ev):
+        self.ev = ev
+
+    def wait(self):
+        torch.cuda.current_stream().wait_event(self.ev)
+
+
 def _param_key(lp) -> object:
     """Which part of the forward first reads a parameter: its layer, 'pre' (embedding) or 'post' (final norm,
     output layer)."""
@@ -72,6 +83,8 @@ class DistributedDataParallel:
         s = pstate.strategy
         self.sp = bool(s.sequence_parallel) and s.tensor_model_parallel_size > 1
         self._hooks = []
+        self.peer = None
+        self._peer_stale = True
         self.bind(param_arena, grad_arena)
         self._pending: List = []
         self._ready: Dict[int, int] = {}
@@ -95,6 +108,7 @@ class DistributedDataParallel:
     # ------------------------------------------------------------------ memory binding
     def bind(self, param_arena: torch.Tensor, grad_arena: Optional[torch.Tensor]) -> None:
         self.param_arena, self.grad_arena = param_arena, grad_arena
+        self._peer_stale = True  # peers map the new arenas at the next step start (a collective point)
         for name, p in self.params.items():
             off = self.layout.offset_by_name[name]
             n = p._local_param.numel
@@ -138,8 +152,28 @@ class DistributedDataParallel:
                 out.append((kind, b, base + s, base + e, zi, self.ps.groups.get(gname), self.ps.groups.get(iname)))
         return out
 
+    def _ensure_peer(self) -> None:
+        """(Re)build the peer-memory collectives after the arenas changed; collective over the shard groups, so
+        it runs at the step start, which every rank of the strategy reaches together."""
+        if not self._peer_stale and self.peer is not None and not self.peer.current(self._bucket_views()):
+            self._peer_stale = True  # its flag buffer was released or the groups were re-created
+        if not self._peer_stale:
+            return
+        self._peer_stale = False
+        self.peer = None
+        if (self.grad_arena is None or not self.grad_arena.is_cuda or not dp_comm.enabled()
+                or not dist.is_initialized()):
+            return
+        views = self._bucket_views()
+        if not any(g is not None and dist.get_world_size(g) > 1 for _, _, _, _, _, g, _ in views):
+            return
+        self.peer = dp_comm.PeerDP(views, self.grad_arena, self.param_arena, self.param_arena.element_size())
+
     def prepare(self):
         """Per-step bucket bookkeeping for overlapped reduction."""
+        self._ensure_peer()
+        if self.peer is not None:
+            self.peer.begin_step()
         self._ready = {}
         self._pending = []
         self._bucket_of = {}
@@ -168,6 +202,9 @@ class DistributedDataParallel:
             return
         self._launched.add(i)
         # asynchronous: the reduction of this bucket overlaps the rest of backward
+        if self.peer is not None:
+            self.peer.reduce_scatter(i)
+            return
         w = _rs_inplace(self.grad_arena[s:e], zi, g, async_op=True)
         if w is not None:
             self._rs_works.append(w)
@@ -200,7 +237,14 @@ class DistributedDataParallel:
         self._rs_works = []
         for i, (kind, b, s, e, zi, g, ig) in enumerate(views):
             if i not in getattr(self, "_launched", set()):
-                _rs_inplace(self.grad_arena[s:e], zi, g)
+                if self.peer is not None:
+                    self.peer.reduce_scatter(i, side_stream=False)
+                else:
+                    _rs_inplace(self.grad_arena[s:e], zi, g)
+        if self.peer is not None:
+            self.peer.wait_reduce_scatters()
+            self.wait_params()  # every all-gather pull of the last step read its peers' shards already
+            self.peer.end_step()  # nobody overwrites gradients a peer may still read
         # Group-ZeRO: replicas of one shard all-reduce across instances
         for i, (kind, b, s, e, zi, g, ig) in enumerate(views):
             if ig is not None and dist.get_world_size(ig) > 1:
@@ -214,7 +258,13 @@ class DistributedDataParallel:
         forward order, so the last bucket first); the forward waits for each bucket just before the first layer
         that reads it (``wait_params``), and every other reader of the arena waits for all of them."""
         self.wait_params()
-        for kind, b, s, e, zi, g, ig in reversed(self._bucket_views()):
+        views = self._bucket_views()
+        if self.peer is not None:
+            for i, ev in self.peer.all_gather(list(reversed(range(len(views)))), overlap):
+                kind, b = views[i][0], views[i][1]
+                self._ag_pending.append((self._bucket_keys.get((kind, b), set()), _EventWait(ev)))
+            return
+        for kind, b, s, e, zi, g, ig in reversed(views):
             if g is None:
                 continue
             w = _ag_inplace(self.param_arena[s:e], zi, g, async_op=overlap)

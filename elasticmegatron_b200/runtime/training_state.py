@@ -52,6 +52,9 @@ class TrainingState:
         self.layout: RankLayout = rank_layout(self.cfg, strategy, self.rank, tc.overlap_grad_reduce,
                                               tc.ddp_bucket_size)
         self.param_dtype = self.cfg.torch_dtype
+        if self.device.type == "cuda" and not is_meta_device and self.param_dtype != torch.bfloat16:
+            raise ValueError(f"CUDA training runs in bf16 (params_dtype={self.cfg.params_dtype}); fp32 parameters "
+                             "are the CPU (gloo) path")
         self.param_arena: Optional[Arena] = None
         self.grad_arena: Optional[Arena] = None
         self.opt_arena: Optional[Arena] = None

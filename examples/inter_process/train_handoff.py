@@ -95,8 +95,7 @@ def main(argv=None):
         over["num_layers"] = a.layers
     if a.seq_length:
         over["seq_length"] = a.seq_length
-    if not use_cuda:
-        over["params_dtype"] = "fp32"
+    over["params_dtype"] = "bf16" if use_cuda else "fp32"  # the CUDA kernels are bf16; CPU ranks run fp32
     set_args(Args(model=preset(a.model, **over),
                   train=TrainConfig(micro_batch_size=a.micro_batch_size, global_batch_size=a.global_batch_size,
                                     lr=a.lr, train_iters=a.train_iters)))

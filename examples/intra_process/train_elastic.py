@@ -102,8 +102,7 @@ def main(argv=None):
         over["num_experts"] = a.num_experts
     if a.moe_ffn:
         over["moe_ffn_hidden_size"] = a.moe_ffn
-    if not use_cuda:
-        over["params_dtype"] = "fp32"
+    over["params_dtype"] = "bf16" if use_cuda else "fp32"  # the CUDA kernels are bf16; CPU ranks run fp32
     cfg = preset(a.model, **over)
     set_args(Args(model=cfg, train=TrainConfig(micro_batch_size=a.micro_batch_size,
                                                global_batch_size=a.global_batch_size, lr=a.lr, min_lr=a.min_lr,

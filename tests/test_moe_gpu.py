@@ -189,3 +189,43 @@ def test_ep_peer_dispatch_matches_nccl_all_to_all():
     a = run_distributed(_moe_ep_train, 2, True, True, backend="nccl")[0]
     b = run_distributed(_moe_ep_train, 2, True, False, backend="nccl")[0]
     torch.testing.assert_close(torch.tensor(a), torch.tensor(b), atol=1e-3, rtol=1e-4)
+
+
+def _ep_plan_outlives_grow(rank, world):
+    """Plan A pushes, plan B (more rows, all routed to rank 0's experts) grows the landing buffer, then plan A
+    moves rows again, as the backward of an earlier layer does after a later layer's forward."""
+    import torch.distributed as dist
+
+    from elasticmegatron_b200.ops import ep_comm, tp_fused
+
+    g = dist.new_group([0, 1])
+    T, k, E, H = 256, 2, 4, 2048
+    gen = torch.Generator(device="cuda").manual_seed(rank)
+
+    def plan(top):
+        counts = torch.bincount(top.reshape(-1), minlength=E).to(torch.int32)
+        return ep_comm.EPPlan(g, top, counts, E // world, H)
+
+    top_a = torch.randint(0, E, (T, k), device="cuda", generator=gen)
+    top_b = torch.randint(0, E // world, (T, k), device="cuda", generator=gen)  # all to rank 0
+    x = torch.randn(T, H, device="cuda", generator=gen).to(torch.bfloat16)
+    a = plan(top_a)
+    first = a.send_home(a.push(x, None, with_origin=True))
+    half_a = a.land.half
+    b = plan(top_b)
+    b.send_home(b.push(x, None, with_origin=True))
+    grown = a.land.half > half_a
+    again = a.send_home(a.push(x, None, with_origin=True))
+    want = x.repeat_interleave(k, 0)
+    ok = bool(torch.equal(first, want)) and bool(torch.equal(again, want))
+    tp_fused.release_buffers()
+    return ok, grown
+
+
+def test_ep_plan_survives_buffer_grow():
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    from dist_utils import run_distributed
+
+    res = run_distributed(_ep_plan_outlives_grow, 2, backend="nccl")
+    assert all(ok for ok, _ in res) and any(grown for _, grown in res), res
