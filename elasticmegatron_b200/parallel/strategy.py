@@ -277,7 +277,8 @@ class ParallelStrategy:
         sg, dg = src.num_distributed_optimizer_instances, dst.num_distributed_optimizer_instances
         if sg == dg:
             if sg != 1:
-                raise ValueError(f"Resharding within a group is not supported, current group size is {sg}")
+                raise ValueError(f"both layouts keep {sg} optimizer instances: a switch that keeps the Group-ZeRO instance "
+                                 "count above 1 is not implemented")
             return None
         assert src.model_parallel_size == dst.model_parallel_size
         assert src.context_parallel_size == dst.context_parallel_size

@@ -108,6 +108,7 @@ class DataloaderState:
 
     train_valid_test_datasets_provider: Optional[Callable] = None
     datasets = None
+    _mock_key = None  # (seq_length, vocab_size, seed) of the cached mock datasets
 
     @classmethod
     def register(cls, provider: Callable) -> None:
@@ -116,11 +117,16 @@ class DataloaderState:
 
     @classmethod
     def get_datasets(cls, model_cfg, seed: int):
-        if cls.datasets is None:
-            if cls.train_valid_test_datasets_provider is not None:
+        """Registered datasets are built once; the synthetic ones are rebuilt when the model's sequence length,
+        vocabulary or the seed changes (a new model in the same process)."""
+        if cls.train_valid_test_datasets_provider is not None:
+            if cls.datasets is None:
                 cls.datasets = cls.train_valid_test_datasets_provider()
-            else:
-                cls.datasets = (MockGPTDataset(1 << 40, model_cfg.seq_length, model_cfg.vocab_size, seed), None, None)
+            return cls.datasets
+        key = (model_cfg.seq_length, model_cfg.vocab_size, seed)
+        if cls.datasets is None or cls._mock_key != key:
+            cls.datasets = (MockGPTDataset(1 << 40, model_cfg.seq_length, model_cfg.vocab_size, seed), None, None)
+            cls._mock_key = key
         return cls.datasets
 
     @classmethod

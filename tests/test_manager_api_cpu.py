@@ -202,3 +202,25 @@ def test_sp_only_switch_hands_over_the_arenas():
     np.testing.assert_allclose(sw[0][0], base[0][0], rtol=1e-5)
     for losses, moved, same in sw:
         assert moved == [0.0, 0.0] and same, (moved, same)
+
+
+def test_synthetic_dataset_follows_the_model_shape():
+    """A second model in the same process (another sequence length / vocabulary) gets samples of its own shape,
+    not the first model's cached ones; a registered dataset provider is still called once."""
+    from elasticmegatron_b200.config import ModelConfig
+    from elasticmegatron_b200.runtime.data import DataloaderState
+
+    DataloaderState.register(None)
+    a = ModelConfig(num_layers=1, hidden_size=64, num_attention_heads=4, ffn_hidden_size=128, vocab_size=1000,
+                    seq_length=64)
+    b = ModelConfig(num_layers=1, hidden_size=64, num_attention_heads=4, ffn_hidden_size=128, vocab_size=500,
+                    seq_length=32)
+    da = DataloaderState.get_datasets(a, 0)[0]
+    db = DataloaderState.get_datasets(b, 0)[0]
+    assert da is not db
+    assert DataloaderState.get_datasets(b, 0)[0] is db
+    calls = []
+    DataloaderState.register(lambda: calls.append(1) or ("ds", None, None))
+    assert DataloaderState.get_datasets(a, 0)[0] == "ds" and DataloaderState.get_datasets(b, 0)[0] == "ds"
+    assert len(calls) == 1
+    DataloaderState.register(None)
