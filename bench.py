@@ -27,6 +27,8 @@ Phases (all device times are CUDA events on the compute stream, MAX over ranks):
 5. (N > 1) ``context_engines``: the first pair once more with this repository's batched-NCCL engine and with
    its re-implementation of the reference's transfer schedule (both repo code, labelled as such; they are not
    the reference's own build).
+6. (N > 1) ``allreduce_256mb``: a 256 MB fp32 all-reduce over all N GPUs with NCCL, with the NVSwitch multicast
+   kernel (``multimem``) and with the peer-memory kernel (``tools/comm_bench.py``), device time MAX over ranks.
 """
 from __future__ import annotations
 
@@ -132,6 +134,7 @@ def main():
     ap.add_argument("--strategy-steps", type=int, default=2, help="timed steps per strategy of the schedule")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-context", action="store_true", help="skip the other engines' timings")
+    ap.add_argument("--no-allreduce", action="store_true", help="skip the all-reduce comparison (phase 6)")
     args = ap.parse_args()
     if args.impl == "reference":
         reference_arm(args)
@@ -237,6 +240,14 @@ def main():
                 args, world, strategies, sched, ts, tokens_per_step, timed_steps, barrier, max_over_ranks)
         except Exception as e:  # report, never lose the throughput line
             per_strategy = {"error": repr(e)[:400]}
+    allreduce = None
+    if world > 1 and not args.no_allreduce:
+        try:
+            from elasticmegatron_b200.tools.comm_bench import run as allreduce_bench
+
+            allreduce = allreduce_bench(dist.group.WORLD, [256], iters=10, warmup=3)
+        except Exception as e:
+            allreduce = {"error": repr(e)[:400]}
     if rank == 0:
         h2d = args.per_gpu_batch * cfg.seq_length * 8 * 2 * world  # ids + labels, int64
         line = {
@@ -257,6 +268,7 @@ def main():
             "link_gbs_nominal": 900.0,
             "checksum_ok": checksum_ok,
             "context_engines": context,
+            "allreduce_256mb": allreduce,
         }
         print(json.dumps(line), flush=True)
     if world > 1:

@@ -76,6 +76,8 @@ void ep_push(torch::Tensor src, int64_t k_div, torch::Tensor gid, torch::Tensor 
 void ep_return(torch::Tensor src, torch::Tensor origin, int64_t rows, torch::Tensor rets);
 void ep_pad(torch::Tensor land, torch::Tensor seg, torch::Tensor counts, c10::optional<torch::Tensor> origin);
 void sym_barrier(torch::Tensor sig_ptrs, int64_t me, int64_t epoch, int64_t timeout_ms);
+void nvls_allreduce_f32(int64_t mc_slice, int64_t count);
+void p2p_allreduce_f32(torch::Tensor bufs, int64_t off, int64_t count);
 int64_t comm_error_flag();
 void comm_clear_error();
 }  // namespace emb
@@ -131,6 +133,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_rs", &gemm_rs);
   m.def("rs_reduce", &rs_reduce);
   m.def("gemm_ag", &gemm_ag);
+  m.def("nvls_allreduce_f32", &nvls_allreduce_f32);
+  m.def("p2p_allreduce_f32", &p2p_allreduce_f32);
   m.def("sym_barrier", &sym_barrier, py::arg("sig_ptrs"), py::arg("me"), py::arg("epoch"),
         py::arg("timeout_ms") = 60000);
   m.def("comm_error_flag", &comm_error_flag);

@@ -427,14 +427,15 @@ class AttentionFn(torch.autograd.Function):
 
 
 def _has_native_attention() -> bool:
-    """Native flash attention is used when EMB_NATIVE_ATTENTION=1.
+    """The native flash attention kernels (``csrc/attn``) are the CUDA path for bf16, head dim 128 and sequence
+    lengths that are multiples of 128; ``EMB_NATIVE_ATTENTION=0`` selects PyTorch SDPA (library) instead.
 
-    Measured at the Llama-2 7B shape (s=4096, 32 heads, d=128) the native forward reaches 0.21 PFLOP/s and the
-    backward 0.35 PFLOP/s, below PyTorch SDPA on this build, so SDPA remains the default CUDA path for now.
+    Measured at the Llama-2 7B shape (s=4096, 32 heads, d=128, causal) the forward takes 0.163 ms and the backward
+    0.799 ms, against 0.114 / ~0.70 ms for SDPA (cuDNN); a 7B training step is ~3 % slower than with SDPA.
     """
     import os
 
-    if os.environ.get("EMB_NATIVE_ATTENTION", "0") != "1":
+    if os.environ.get("EMB_NATIVE_ATTENTION", "1") == "0":
         return False
     try:
         return hasattr(ext(), "attn_bwd")

@@ -20,7 +20,7 @@ import torch
 import torch.distributed as dist
 
 from ..planner.layout import RankLayout
-from . import dp_comm
+from . import dp_comm, nvls
 
 
 def _rs_inplace(buf: torch.Tensor, shard_index: int, group, async_op: bool = False):
@@ -250,7 +250,8 @@ class DistributedDataParallel:
             if ig is not None and dist.get_world_size(ig) > 1:
                 n = dist.get_world_size(g) if g is not None else 1
                 c = (e - s) // n
-                dist.all_reduce(self.grad_arena[s + zi * c:s + (zi + 1) * c], group=ig)
+                # NVSwitch multicast reduction (peer memory without it; NCCL with EMB_NVLS=0)
+                nvls.all_reduce_(self.grad_arena[s + zi * c:s + (zi + 1) * c], ig)
 
     def start_param_sync(self, overlap: bool = False) -> None:
         """All-gather the updated parameter shards, bucket by bucket.  With ``overlap`` the gathers are left in

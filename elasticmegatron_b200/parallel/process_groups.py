@@ -91,6 +91,9 @@ class _ProcessGroupPool:
         tp_fused = sys.modules.get("elasticmegatron_b200.ops.tp_fused")
         if tp_fused is not None:
             tp_fused.release_buffers()  # symmetric buffers belong to the old communicators
+        nvls = sys.modules.get("elasticmegatron_b200.parallel.nvls")
+        if nvls is not None:
+            nvls.release()  # so do the multicast staging buffers (rendezvoused on the old groups)
         keys = sorted([k for k in self._groups if k[1] == "nccl"], key=lambda k: (len(k[0]), sorted(k[0])))
         for k in keys:
             pg = self._groups.pop(k)
