@@ -450,10 +450,12 @@ at::Tensor attn_bwd(at::Tensor dO, at::Tensor qkv, at::Tensor o, at::Tensor lse,
   p.scale_log2 = (float)(1.4426950408889634 / std::sqrt((double)D));
   p.causal = causal ? 1 : 0;
   p.err = err_flag();
-  static bool attr = false;
-  if (!attr) {
+  static bool attr[kMaxDevices] = {};
+  int dev = 0;
+  EMB_CUDA_CHECK(cudaGetDevice(&dev));
+  if (!attr[dev]) {
     EMB_CUDA_CHECK(cudaFuncSetAttribute(flash_bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
-    attr = true;
+    attr[dev] = true;
   }
   dim3 grid((unsigned)(s / T), (unsigned)(b * G));
   flash_bwd_kernel<<<grid, 192, SMEM_BYTES, st>>>(tq, td, tdq, p);

@@ -45,6 +45,7 @@ int64_t attn_error_flag();
 torch::Tensor attn_bwd(torch::Tensor dO, torch::Tensor qkv, torch::Tensor o, torch::Tensor lse, int64_t hpg,
                        bool causal);
 int64_t attn_bwd_error_flag();
+void attn_merge(torch::Tensor out, torch::Tensor lse, torch::Tensor o_b, torch::Tensor l_b);
 int64_t gemm_error_flag();
 at::Tensor attn_exp2_emulated(at::Tensor x);
 void dp_signal(at::Tensor flags, int64_t me, int64_t slot0, int64_t nslots, int64_t epoch);
@@ -122,6 +123,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("attn_bwd", &attn_bwd, py::arg("dO"), py::arg("qkv"), py::arg("o"), py::arg("lse"), py::arg("hpg"),
         py::arg("causal") = true);
   m.def("attn_bwd_error_flag", &attn_bwd_error_flag);
+  m.def("attn_merge", &attn_merge);
   m.def("attn_error_flag", &attn_error_flag);
   m.def("attn_exp2_emulated", &attn_exp2_emulated);
   m.def("dp_signal", &dp_signal);

@@ -1043,6 +1043,18 @@ static bool ok_2d(const at::Tensor& t) {
   return t.dim() == 2 && t.stride(1) == 1 && t.stride(0) % 8 == 0 && (reinterpret_cast<uintptr_t>(t.data_ptr()) % 16) == 0;
 }
 
+// The 1-SM kernel's dynamic shared-memory limit, raised once per device (a function attribute belongs to the
+// device's context).
+static void gemm1_smem_attr() {
+  static bool done[kMaxDevices] = {};
+  int dev = 0;
+  EMB_CUDA_CHECK(cudaGetDevice(&dev));
+  if (!done[dev]) {
+    EMB_CUDA_CHECK(cudaFuncSetAttribute(gk::gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, gk::SMEM_BYTES));
+    done[dev] = true;
+  }
+}
+
 bool gemm_tc_supported(at::Tensor a, at::Tensor b, bool trans_a, bool trans_b, c10::optional<at::Tensor> out,
                        bool accumulate) {
   if (!a.is_cuda() || a.scalar_type() != at::kBFloat16 || b.scalar_type() != at::kBFloat16) return false;
@@ -1128,11 +1140,7 @@ at::Tensor gemm_tc(at::Tensor a, at::Tensor b, bool trans_a, bool trans_b, c10::
     const int clusters = (int)std::min<int64_t>(tiles2, num_sms() / 2);
     gk2::launch<false>(bk, tA2, tB2, tC, p, clusters);
   } else {
-    static bool attr_set = false;
-    if (!attr_set) {
-      EMB_CUDA_CHECK(cudaFuncSetAttribute(gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
-      attr_set = true;
-    }
+    gemm1_smem_attr();
     const int tiles = (int)(((M + BM - 1) / BM) * ((N + BN - 1) / BN));
     const int grid = std::min(tiles, num_sms());
     gemm_kernel<<<grid, NUM_THREADS, SMEM_BYTES, cur_stream()>>>(tA, tB, p);
@@ -1173,11 +1181,7 @@ at::Tensor gemm_grouped(at::Tensor a, at::Tensor w, bool trans_b, at::Tensor til
   p.group_info = tile_group.data_ptr<int>();
   p.groups = (int)G;
   p.group_b_stride = (int)(trans_b ? N : K);
-  static bool attr_set = false;
-  if (!attr_set) {
-    EMB_CUDA_CHECK(cudaFuncSetAttribute(gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
-    attr_set = true;
-  }
+  gemm1_smem_attr();
   const int tiles = (int)((R / BM) * ((N + BN - 1) / BN));
   gemm_kernel<<<std::min(tiles, num_sms()), NUM_THREADS, SMEM_BYTES, cur_stream()>>>(tA, tB, p);
   EMB_LAUNCH_CHECK();
@@ -1217,11 +1221,7 @@ void gemm_grouped_wgrad(at::Tensor dy, at::Tensor x, at::Tensor seg, at::Tensor 
   p.group_info = seg.data_ptr<int>();
   p.groups = (int)G;
   p.group_c_stride = (long long)M * N;
-  static bool attr_set = false;
-  if (!attr_set) {
-    EMB_CUDA_CHECK(cudaFuncSetAttribute(gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
-    attr_set = true;
-  }
+  gemm1_smem_attr();
   const int64_t tiles = G * ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
   gemm_kernel<<<(int)std::min<int64_t>(tiles, num_sms()), NUM_THREADS, SMEM_BYTES, cur_stream()>>>(tA, tB, p);
   EMB_LAUNCH_CHECK();

@@ -16,6 +16,13 @@ ways to exchange keys and values over the CP group (Megatron's ``--cp-comm-type`
   query-group count divisible by CP; moves 2 x (q + k + v + out) / CP of the activations per rank instead of
   all of K/V.
 
+On CUDA (bf16, head dim 128, chunks a multiple of 128 rows) every variant runs on the native flash-attention
+kernels (``csrc/attn``): the all-gather and ring variants as one kernel call per (query chunk, key chunk) block -
+the diagonal block causal, earlier chunks in full - whose partial outputs are merged by their log-sum-exp in
+fp32 (``attn_merge``); the backward calls the native backward kernel per block with the final output and
+log-sum-exp, so every block's probabilities are the global softmax's.  Ulysses runs one native causal call over
+the whole sequence.  Elsewhere (CPU, other shapes) the blocks are fp32 tensor algebra / library attention.
+
 In the reference CP lives entirely in Megatron/TE (context_parallel_size is only carried and folded into the
 ZeRO group, parallel_strategy.py:131-147).
 """
@@ -42,6 +49,116 @@ def _global_chunk_starts(s: int, cp: int):
     return out
 
 
+def _native_blocks(qkv: torch.Tensor) -> bool:
+    """Whether the per-block math runs on the native flash-attention kernels."""
+    return (qkv.is_cuda and qkv.dtype == torch.bfloat16 and qkv.shape[-1] == 128 and (qkv.shape[0] // 2) % 128 == 0
+            and F_._has_native_attention())
+
+
+class _Blocks:
+    """Attention of this rank's two query chunks against one key / value chunk at a time on the native kernels.
+
+    Each query chunk has a fused ``[c, b, G, hpg + 2, d]`` buffer (the kernels' input layout) whose query slots are
+    filled once; a block copies its key / value chunk into the other slots and runs one kernel call."""
+
+    def __init__(self, qkv: torch.Tensor, hpg: int):
+        from ..ops.native import ext
+
+        self.ext = ext()
+        s, b, G, w, d = qkv.shape
+        self.c, self.b, self.G, self.hpg, self.H, self.d = s // 2, b, G, hpg, G * hpg, d
+        c = self.c
+        self.buf = [torch.empty(c, b, G, w, d, dtype=qkv.dtype, device=qkv.device) for _ in range(2)]
+        for h in range(2):
+            self.buf[h][:, :, :, :hpg].copy_(qkv[h * c:(h + 1) * c, :, :, :hpg])
+
+    def _load(self, hq: int, kv_chunk: torch.Tensor) -> torch.Tensor:
+        self.buf[hq][:, :, :, self.hpg:].copy_(kv_chunk)
+        return self.buf[hq]
+
+    def start(self):
+        """Fresh accumulators: fp32 outputs [c, b, H, d] and log-sum-exps [b, H, c] (-inf) per query chunk."""
+        dev = self.buf[0].device
+        out = [torch.empty(self.c, self.b, self.H, self.d, dtype=torch.float32, device=dev) for _ in range(2)]
+        lse = [torch.full((self.b, self.H, self.c), float("-inf"), dtype=torch.float32, device=dev)
+               for _ in range(2)]
+        return out, lse
+
+    def forward(self, hq: int, kv_chunk: torch.Tensor, causal: bool, out, lse) -> None:
+        o_b, l_b = self.ext.attn_fwd(self._load(hq, kv_chunk), self.hpg, causal)
+        self.ext.attn_merge(out[hq], lse[hq], o_b, l_b)
+
+    def backward(self, hq: int, kv_chunk: torch.Tensor, causal: bool, dout_h, o_h, lse_h, dq, dkv_chunk) -> None:
+        """dq[hq] ([c, b, G, hpg, d] fp32) and dkv_chunk ([c, b, G, 2, d] fp32) += this block's gradients."""
+        g = self.ext.attn_bwd(dout_h, self._load(hq, kv_chunk), o_h, lse_h, self.hpg, causal)
+        dq[hq] += g[:, :, :, :self.hpg]
+        dkv_chunk += g[:, :, :, self.hpg:]
+
+    @staticmethod
+    def finish(out, dtype) -> torch.Tensor:
+        """The two chunks' merged outputs as [s, b, H * d] in ``dtype``."""
+        c, b, H, d = out[0].shape
+        return torch.cat([o.view(c, b, H * d) for o in out], 0).to(dtype)
+
+
+def _assemble_dqkv(qkv, hpg, dq, dkv):
+    c = qkv.shape[0] // 2
+    dqkv = torch.empty_like(qkv)
+    for h in range(2):
+        dqkv[h * c:(h + 1) * c, :, :, :hpg] = dq[h]
+    dqkv[:, :, :, hpg:] = dkv
+    return dqkv
+
+
+class _AGNativeFn(torch.autograd.Function):
+    """All-gather CP on the native kernels: K/V gathered in forward, their gradients reduce-scattered back."""
+
+    @staticmethod
+    def _gather(qkv, hpg, group, cp):
+        s, b, G, _, d = qkv.shape
+        kv = qkv[:, :, :, hpg:].contiguous()
+        kv_all = torch.empty(cp * s, b, G, 2, d, dtype=kv.dtype, device=kv.device)
+        dist.all_gather_into_tensor(kv_all, kv, group=group)
+        return kv_all
+
+    @staticmethod
+    def forward(ctx, qkv, hpg, group, cp_rank, cp):
+        s = qkv.shape[0]
+        c = s // 2
+        kv_all = _AGNativeFn._gather(qkv, hpg, group, cp)
+        starts = _global_chunk_starts(s, cp)
+        blk = _Blocks(qkv, hpg)
+        out, lse = blk.start()
+        for hq, ci in enumerate(_chunks_of(cp_rank, cp)):
+            for kj in range(ci + 1):
+                blk.forward(hq, kv_all[starts[kj]:starts[kj] + c], kj == ci, out, lse)
+        o = _Blocks.finish(out, qkv.dtype)
+        ctx.save_for_backward(qkv, o, *lse)
+        ctx.hpg, ctx.group, ctx.cp_rank, ctx.cp = hpg, group, cp_rank, cp
+        return o
+
+    @staticmethod
+    def backward(ctx, dout):
+        qkv, o, l0, l1 = ctx.saved_tensors
+        hpg, group, cp_rank, cp = ctx.hpg, ctx.group, ctx.cp_rank, ctx.cp
+        s, b, G, _, d = qkv.shape
+        c = s // 2
+        kv_all = _AGNativeFn._gather(qkv, hpg, group, cp)
+        starts = _global_chunk_starts(s, cp)
+        blk = _Blocks(qkv, hpg)
+        dout = dout.contiguous()
+        dq = [torch.zeros(c, b, G, hpg, d, dtype=torch.float32, device=qkv.device) for _ in range(2)]
+        dkv_all = torch.zeros(cp * s, b, G, 2, d, dtype=torch.float32, device=qkv.device)
+        for hq, ci in enumerate(_chunks_of(cp_rank, cp)):
+            dout_h, o_h, l_h = dout[hq * c:(hq + 1) * c], o[hq * c:(hq + 1) * c], (l0, l1)[hq]
+            for kj in range(ci + 1):
+                st = starts[kj]
+                blk.backward(hq, kv_all[st:st + c], kj == ci, dout_h, o_h, l_h, dq, dkv_all[st:st + c])
+        dkv = torch.empty(s, b, G, 2, d, dtype=torch.float32, device=qkv.device)
+        dist.reduce_scatter_tensor(dkv, dkv_all, group=group)  # every rank's contribution to my chunks
+        return _assemble_dqkv(qkv, hpg, dq, dkv), None, None, None, None
+
+
 def cp_attention(qkv: torch.Tensor, hpg: int, group, cp_rank: int, cp: int) -> torch.Tensor:
     """Causal attention of this rank's two query chunks against the gathered keys / values.
 
@@ -51,6 +168,8 @@ def cp_attention(qkv: torch.Tensor, hpg: int, group, cp_rank: int, cp: int) -> t
     mask tensor and no K/V head replication (grouped-query attention is native to the call)."""
     from torch.nn.attention.bias import causal_lower_right
 
+    if _native_blocks(qkv):
+        return _AGNativeFn.apply(qkv, hpg, group, cp_rank, cp)
     s, b, G, _, d = qkv.shape
     c = s // 2
     kv = qkv[:, :, :, hpg:].contiguous()  # [s, b, G, 2, d]
@@ -119,6 +238,72 @@ def _split_kv(kv: torch.Tensor) -> List[Tuple[torch.Tensor, torch.Tensor]]:
     c = kv.shape[0] // 2
     return [(kv[h * c:(h + 1) * c, :, :, 0].permute(1, 2, 0, 3), kv[h * c:(h + 1) * c, :, :, 1].permute(1, 2, 0, 3))
             for h in range(2)]
+
+
+class _RingNativeFn(torch.autograd.Function):
+    """The ring on the native kernels: same exchange as :class:`_RingAttnFn`, one kernel call per block."""
+
+    @staticmethod
+    def forward(ctx, qkv, hpg, group, cp_rank, cp):
+        s = qkv.shape[0]
+        c = s // 2
+        my = _chunks_of(cp_rank, cp)
+        ring = _Ring(group, cp_rank, cp)
+        kv = qkv[:, :, :, hpg:].contiguous()
+        blk = _Blocks(qkv, hpg)
+        out, lse = blk.start()
+        for t in range(cp):
+            if t + 1 < cp:
+                nxt, reqs = ring.start(kv)
+            src = (cp_rank - t) % cp
+            for hk in range(2):
+                kj = _chunks_of(src, cp)[hk]
+                for hq in range(2):
+                    rel = _relation(my[hq], kj)
+                    if rel:
+                        blk.forward(hq, kv[hk * c:(hk + 1) * c], rel == 1, out, lse)
+            if t + 1 < cp:
+                _Ring.wait(reqs)
+                kv = nxt
+        o = _Blocks.finish(out, qkv.dtype)
+        ctx.save_for_backward(qkv, o, *lse)
+        ctx.hpg, ctx.group, ctx.cp_rank, ctx.cp = hpg, group, cp_rank, cp
+        return o
+
+    @staticmethod
+    def backward(ctx, dout):
+        qkv, o, l0, l1 = ctx.saved_tensors
+        hpg, group, cp_rank, cp = ctx.hpg, ctx.group, ctx.cp_rank, ctx.cp
+        s, b, G, _, d = qkv.shape
+        c = s // 2
+        my = _chunks_of(cp_rank, cp)
+        ring = _Ring(group, cp_rank, cp)
+        blk = _Blocks(qkv, hpg)
+        dout = dout.contiguous()
+        dq = [torch.zeros(c, b, G, hpg, d, dtype=torch.float32, device=qkv.device) for _ in range(2)]
+        kv = qkv[:, :, :, hpg:].contiguous()
+        incoming = None
+        for t in range(cp):
+            if t + 1 < cp:
+                nxt_kv, reqs_kv = ring.start(kv)
+            src = (cp_rank - t) % cp
+            acc = torch.zeros(kv.shape, dtype=torch.float32, device=qkv.device)
+            for hk in range(2):
+                kj = _chunks_of(src, cp)[hk]
+                for hq in range(2):
+                    rel = _relation(my[hq], kj)
+                    if rel:
+                        blk.backward(hq, kv[hk * c:(hk + 1) * c], rel == 1, dout[hq * c:(hq + 1) * c],
+                                     o[hq * c:(hq + 1) * c], (l0, l1)[hq], dq, acc[hk * c:(hk + 1) * c])
+            if incoming is not None:
+                _Ring.wait(incoming[1])
+                acc += incoming[0]
+            incoming = ring.start(acc)
+            if t + 1 < cp:
+                _Ring.wait(reqs_kv)
+                kv = nxt_kv
+        _Ring.wait(incoming[1])
+        return _assemble_dqkv(qkv, hpg, dq, incoming[0]), None, None, None, None
 
 
 class _RingAttnFn(torch.autograd.Function):
@@ -215,7 +400,10 @@ def cp_ring_attention(qkv: torch.Tensor, hpg: int, group, cp_rank: int, cp: int)
 
     Same inputs and output as :func:`cp_attention` (``qkv`` [s, b, G, hpg+2, d] after RoPE, out
     [s, b, G*hpg*d]).  Scores, softmax statistics and accumulators are fp32 whatever the input dtype; the
-    math is plain tensor algebra, so the same code runs on the host and on the device."""
+    math is plain tensor algebra, so the same code runs on the host and on the device; on CUDA it runs on the native
+    kernels (:class:`_RingNativeFn`)."""
+    if _native_blocks(qkv):
+        return _RingNativeFn.apply(qkv, hpg, group, cp_rank, cp)
     return _RingAttnFn.apply(qkv, hpg, group, cp_rank, cp)
 
 
@@ -258,11 +446,15 @@ def cp_ulysses_attention(qkv: torch.Tensor, hpg: int, group, cp_rank: int, cp: i
     y = _AllToAll.apply(x.contiguous(), group)  # [source rank, s, b, gp, hpg+2, d]
     chunks = [y[g, :c] if g < cp else y[2 * cp - 1 - g, c:] for g in range(2 * cp)]
     full = torch.cat(chunks, 0)  # [S, b, gp, hpg+2, d], global sequence order
-    q = full[:, :, :, :hpg].reshape(S, b, gp * hpg, d).permute(1, 2, 0, 3)
-    k = full[:, :, :, hpg].permute(1, 2, 0, 3)
-    v = full[:, :, :, hpg + 1].permute(1, 2, 0, 3)
-    o = torch.nn.functional.scaled_dot_product_attention(q, k, v, is_causal=True, enable_gqa=hpg > 1)
-    o = o.permute(2, 0, 1, 3).reshape(S, b, gp, hpg * d)
+    if full.is_cuda:
+        # the gathered sequence is already the fused layout of the attention op (native kernels on CUDA)
+        o = F_.attention(full.contiguous(), hpg).view(S, b, gp, hpg * d)
+    else:
+        q = full[:, :, :, :hpg].reshape(S, b, gp * hpg, d).permute(1, 2, 0, 3)
+        k = full[:, :, :, hpg].permute(1, 2, 0, 3)
+        v = full[:, :, :, hpg + 1].permute(1, 2, 0, 3)
+        o = torch.nn.functional.scaled_dot_product_attention(q, k, v, is_causal=True, enable_gqa=hpg > 1)
+        o = o.permute(2, 0, 1, 3).reshape(S, b, gp, hpg * d)
     back = torch.stack([torch.cat([o[j * c:(j + 1) * c], o[(2 * cp - 1 - j) * c:(2 * cp - j) * c]], 0)
                         for j in range(cp)])  # [dest rank, s, b, gp, hpg*d]
     r = _AllToAll.apply(back, group)  # [query group slice, s, b, gp, hpg*d]
