@@ -146,6 +146,10 @@ std::vector<at::Tensor> add_rmsnorm_fwd(at::Tensor x, at::Tensor o, at::Tensor w
 }
 
 // ------------------------------------------------------------------------------------------ RMSNorm bwd
+// Persistent CTAs, several per SM (rows_in_flight), each walking rows r, r + grid, ...  A row is read twice: the
+// first pass forms the dot product the second needs (and the fp32 dw partial), the second - served from L1, where
+// the first pass left the row's 2 x H bf16 values - writes dx.  Holding only w and the dw partial in registers
+// keeps the CTA small enough for four per SM, so four rows' loads are in flight per SM instead of two.
 template <int VPT>
 __global__ void rmsnorm_bwd_kernel(const __nv_bfloat16* __restrict__ dy, const __nv_bfloat16* __restrict__ x,
                                    const __nv_bfloat16* __restrict__ w, const float* __restrict__ rstd,
@@ -166,21 +170,27 @@ __global__ void rmsnorm_bwd_kernel(const __nv_bfloat16* __restrict__ dy, const _
     const uint4* xr = reinterpret_cast<const uint4*>(x + (size_t)row * H);
     const uint4* dr = reinterpret_cast<const uint4*>(dy + (size_t)row * H);
     const float r = rstd[row];
-    float xv[VPT][8], gv[VPT][8];
     float dot = 0.f;
+    uint4 xv[VPT], dv[VPT];
 #pragma unroll
     for (int k = 0; k < VPT; ++k) {
       int i = threadIdx.x + k * blockDim.x;
       if (i < nvec) {
-        float d[8];
-        unpack8(xr[i], xv[k]);
-        unpack8(dr[i], d);
+        xv[k] = xr[i];
+        dv[k] = dr[i];
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < VPT; ++k) {
+      int i = threadIdx.x + k * blockDim.x;
+      if (i < nvec) {
+        float xf[8], d[8];
+        unpack8(xv[k], xf);
+        unpack8(dv[k], d);
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
-          float xh = xv[k][j] * r;
-          xv[k][j] = xh;
-          gv[k][j] = d[j] * wf[k][j];
-          dot += gv[k][j] * xh;
+          const float xh = xf[j] * r;
+          dot += d[j] * wf[k][j] * xh;
           acc[k][j] += d[j] * xh;
         }
       }
@@ -193,9 +203,11 @@ __global__ void rmsnorm_bwd_kernel(const __nv_bfloat16* __restrict__ dy, const _
     for (int k = 0; k < VPT; ++k) {
       int i = threadIdx.x + k * blockDim.x;
       if (i < nvec) {
-        float t[8];
+        float xf[8], d[8], t[8];
+        unpack8(xr[i], xf);  // second read of the row: an L1 hit
+        unpack8(dr[i], d);
 #pragma unroll
-        for (int j = 0; j < 8; ++j) t[j] = r * (gv[k][j] - xv[k][j] * dot);
+        for (int j = 0; j < 8; ++j) t[j] = r * (d[j] * wf[k][j] - xf[j] * r * dot);
         if (rr) {
           float a[8];
           unpack8(rr[i], a);
@@ -218,13 +230,32 @@ __global__ void rmsnorm_bwd_kernel(const __nv_bfloat16* __restrict__ dy, const _
   }
 }
 
-// dw[h] = sum_b part[b, h] in a fixed order; optionally accumulated into an fp32 target.
+// Rows in flight per SM for the norm backward kernels (persistent grid = SMs x this, at most T).
+constexpr int kNormBwdCtasPerSm = 4;
+static int64_t norm_bwd_grid(int64_t T) {
+  return std::max<int64_t>(1, std::min<int64_t>(T, (int64_t)num_sms() * kNormBwdCtasPerSm));
+}
+
+// dw[h] = sum_b part[b, h] in a fixed order (warp w adds rows w, w + 8, ...; then the 8 warp sums in order);
+// optionally accumulated into an fp32 target.  32 columns per CTA.
 __global__ void colsum_kernel(const float* __restrict__ part, float* __restrict__ out, int nb, int H, int accumulate) {
-  int h = blockIdx.x * blockDim.x + threadIdx.x;
-  if (h >= H) return;
+  __shared__ float sm[8][33];
+  const int lane = threadIdx.x & 31, wp = threadIdx.x >> 5;
+  const int h = blockIdx.x * 32 + lane;
   float s = 0.f;
-  for (int b = 0; b < nb; ++b) s += part[(size_t)b * H + h];
-  out[h] = accumulate ? out[h] + s : s;
+  if (h < H)
+    for (int b = wp; b < nb; b += 8) s += part[(size_t)b * H + h];
+  sm[wp][lane] = s;
+  __syncthreads();
+  if (wp == 0 && h < H) {
+    float t = 0.f;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) t += sm[k][lane];
+    out[h] = accumulate ? out[h] + t : t;
+  }
+}
+static void launch_colsum(const float* part, float* out, int nb, int H, int accumulate, cudaStream_t st) {
+  colsum_kernel<<<(H + 31) / 32, 256, 0, st>>>(part, out, nb, H, accumulate);
 }
 
 std::vector<at::Tensor> rmsnorm_bwd(at::Tensor dy, at::Tensor x, at::Tensor w, at::Tensor rstd,
@@ -240,8 +271,7 @@ std::vector<at::Tensor> rmsnorm_bwd(at::Tensor dy, at::Tensor x, at::Tensor w, a
   auto dx = at::empty_like(x);
   int vpt;
   int threads = pick_threads((int)(H / 8), vpt);
-  int grid = (int)std::min<int64_t>(T, (int64_t)num_sms() * 2);
-  if (grid < 1) grid = 1;
+  const int grid = (int)norm_bwd_grid(T);
   auto part = at::empty({grid, H}, x.options().dtype(at::kFloat));
   auto st = cur_stream();
   const __nv_bfloat16* rp = has_res ? (const __nv_bfloat16*)dres->data_ptr() : nullptr;
@@ -259,7 +289,7 @@ std::vector<at::Tensor> rmsnorm_bwd(at::Tensor dy, at::Tensor x, at::Tensor w, a
   } else {
     dw = at::empty({H}, x.options().dtype(at::kFloat));
   }
-  colsum_kernel<<<(H + 255) / 256, 256, 0, st>>>(part.data_ptr<float>(), dw.data_ptr<float>(), grid, (int)H, acc);
+  launch_colsum(part.data_ptr<float>(), dw.data_ptr<float>(), grid, (int)H, acc, st);
   EMB_LAUNCH_CHECK();
   count_launch(2);
   return {dx, dw};
@@ -447,9 +477,8 @@ std::vector<at::Tensor> layernorm_bwd(at::Tensor dy, at::Tensor x, at::Tensor w,
   db = ab ? *db_accum : at::empty({H}, x.options().dtype(at::kFloat));
   TORCH_CHECK(dw.scalar_type() == at::kFloat && dw.is_contiguous() && dw.numel() == H);
   TORCH_CHECK(db.scalar_type() == at::kFloat && db.is_contiguous() && db.numel() == H);
-  colsum_kernel<<<(H + 255) / 256, 256, 0, st>>>(part.data_ptr<float>(), dw.data_ptr<float>(), grid, (int)H, aw);
-  colsum_kernel<<<(H + 255) / 256, 256, 0, st>>>(part.data_ptr<float>() + (size_t)grid * H, db.data_ptr<float>(),
-                                                 grid, (int)H, ab);
+  launch_colsum(part.data_ptr<float>(), dw.data_ptr<float>(), grid, (int)H, aw, st);
+  launch_colsum(part.data_ptr<float>() + (size_t)grid * H, db.data_ptr<float>(), grid, (int)H, ab, st);
   EMB_LAUNCH_CHECK();
   count_launch(T > 0 ? 3 : 2);
   return {dx, dw, db};
@@ -647,7 +676,7 @@ extern "C" int emb_rmsnorm_bwd_noalloc(const void* dy, const void* x, const void
   if (e != cudaSuccess) return (int)e;
   int vpt;
   const int threads = pick_threads((int)(H / 8), vpt);
-  int64_t grid = std::min<int64_t>(T, (int64_t)num_sms() * 2);
+  int64_t grid = norm_bwd_grid(T);
   grid = std::min<int64_t>(grid, EMB_NOALLOC_SCRATCH_FLOATS / H);
   if (grid < 1) grid = 1;
   const __nv_bfloat16* dyp = static_cast<const __nv_bfloat16*>(dy);
@@ -657,7 +686,7 @@ extern "C" int emb_rmsnorm_bwd_noalloc(const void* dy, const void* x, const void
 #define L(V) rmsnorm_bwd_kernel<V><<<(int)grid, threads, 0, stream>>>(dyp, xp, wp, rstd, dxp, scratch, (int)T, (int)H)
   if (vpt <= 1) L(1); else if (vpt == 2) L(2); else if (vpt == 3) L(3); else L(4);
 #undef L
-  colsum_kernel<<<(int)((H + 255) / 256), 256, 0, stream>>>(scratch, dw, (int)grid, (int)H, accumulate ? 1 : 0);
+  launch_colsum(scratch, dw, (int)grid, (int)H, accumulate ? 1 : 0, stream);
   e = cudaGetLastError();
   count_launch(2);
   return (int)e;
