@@ -152,6 +152,7 @@ struct Params {
   int a_mn, b_mn;  // operand majorness
   int* err;
   int split_tail;  // 2-SM kernel: run the last partial wave as 256 x 128 half tiles when they fit in one wave
+  int m_fast;      // measurement only (EMB_GEMM_RASTER=m): m blocks vary fastest whatever the shape
   int no_store;    // 2-SM kernel, measurement only: read the accumulators but write no output
   int c_tma;       // 2-SM kernel: C is written (or add-reduced) through the tensor map tmC, one 32-row block per
                    // epilogue warp and bulk operation (else row by row)
@@ -195,7 +196,8 @@ struct TileInfo {
   long long c_off;
 };
 
-// Output tile t of the persistent schedule (m fastest); false when the tile has no work (grouped modes).
+// Output tile t of the persistent schedule (the dimension with fewer tiles fastest; m fastest in the grouped
+// modes, whose per-tile group lookup is by m block); false when the tile has no work (grouped modes).
 __device__ __forceinline__ bool tile_info(const Params& p, int t, int tiles_m, int tiles_n, int nk, TileInfo& ti) {
   if (p.group_mode == 2) {
     const int per = tiles_m * tiles_n;
@@ -208,8 +210,13 @@ __device__ __forceinline__ bool tile_info(const Params& p, int t, int tiles_m, i
     ti.c_off = (long long)g * p.group_c_stride;
     return ti.kb1 > ti.kb0;
   }
-  ti.m0 = (t % tiles_m) * BM;
-  ti.n0 = (t / tiles_m) * BN;
+  if (p.group_mode == 0 && tiles_n < tiles_m && !p.m_fast) {
+    ti.m0 = (t / tiles_n) * BM;
+    ti.n0 = (t % tiles_n) * BN;
+  } else {
+    ti.m0 = (t % tiles_m) * BM;
+    ti.n0 = (t / tiles_m) * BN;
+  }
   ti.kb0 = 0;
   ti.kb1 = nk;
   ti.b_off = 0;
@@ -552,15 +559,19 @@ __global__ void __launch_bounds__(AG ? NUM_THREADS_AG : NUM_THREADS, 1)
   const int tiles_n = (p.N + BN - 1) / BN;
   const int num_tiles = tiles_m * tiles_n;
   const int nk = (p.K + BK - 1) / BK;
-  // tile -> (m block, n block).  With the all-gather prologue, n varies fastest and m blocks start at this
-  // rank's own chunk, so the first tiles never wait for a peer's rows.
+  // tile -> (m block, n block).  The dimension with fewer tiles varies fastest, so the tiles in flight at once
+  // share few panels of the long operand and those panels stay in L2 while every tile that needs them runs
+  // (a 32000 x 4096 weight gradient with m fastest streamed each 2 MB A panel from DRAM once per n block:
+  // 0.75x of cuBLAS).  With the all-gather prologue, n varies fastest and m blocks start at this rank's own
+  // chunk, so the first tiles never wait for a peer's rows.
   const int my_chunk = AG ? p.my_slot : 0;
   const int mt_per_chunk = AG ? p.rows_per_rank / BM : 1;
+  const bool n_fast = AG || (tiles_n < tiles_m && !p.m_fast);
   auto tile_m = [&](int t) -> int {
-    if (!AG) return t % tiles_m;
-    return (t / tiles_n + my_chunk * mt_per_chunk) % tiles_m;
+    if (AG) return (t / tiles_n + my_chunk * mt_per_chunk) % tiles_m;
+    return n_fast ? t / tiles_n : t % tiles_m;
   };
-  auto tile_n = [&](int t) -> int { return AG ? t % tiles_n : t / tiles_m; };
+  auto tile_n = [&](int t) -> int { return n_fast ? t % tiles_n : t / tiles_m; };
   // Tail split (not with the all-gather prologue): when the tiles of the last, partial wave could run as twice
   // as many 256 x 128 halves in one wave, they do - the last wave then takes half as long (4096 x 4096
   // outputs: 256 tiles on 74 clusters = 3 full waves + 34 tiles -> 3.5 wave-times instead of 4).  Work unit u
@@ -990,6 +1001,14 @@ static int* err_flag() { return device_err_flag(kErrGemm); }
 }  // namespace gk
 
 // Output through a tensor map in the 2-SM kernel (EMB_GEMM_C_TMA=0 selects the row-by-row epilogue).
+static int raster_m_fast() {
+  static int v = [] {
+    const char* e = std::getenv("EMB_GEMM_RASTER");
+    return (e && e[0] == 'm') ? 1 : 0;
+  }();
+  return v;
+}
+
 static bool c_tma_enabled() {
   static bool on = [] {
     const char* e = std::getenv("EMB_GEMM_C_TMA");
@@ -1092,6 +1111,7 @@ at::Tensor gemm_tc(at::Tensor a, at::Tensor b, bool trans_a, bool trans_b, c10::
   CUtensorMap tA = a_mn ? make_map(a.data_ptr(), K, M, a.stride(0), 64, 64) : make_map(a.data_ptr(), M, K, a.stride(0), 64, BM);
   CUtensorMap tB = b_mn ? make_map(b.data_ptr(), K, N, b.stride(0), 64, 64) : make_map(b.data_ptr(), N, K, b.stride(0), 64, BN);
   Params p{};
+  p.m_fast = raster_m_fast();
   p.C = C.data_ptr();
   p.M = (int)M;
   p.N = (int)N;
@@ -1169,6 +1189,7 @@ at::Tensor gemm_grouped(at::Tensor a, at::Tensor w, bool trans_b, at::Tensor til
   CUtensorMap tA = make_map(a.data_ptr(), R, K, K, 64, BM);
   CUtensorMap tB = trans_b ? make_map(w.data_ptr(), G * N, K, K, 64, BN) : make_map(w.data_ptr(), G * K, N, N, 64, 64);
   Params p{};
+  p.m_fast = raster_m_fast();
   p.C = C.data_ptr();
   p.M = (int)R;
   p.N = (int)N;
@@ -1207,6 +1228,7 @@ void gemm_grouped_wgrad(at::Tensor dy, at::Tensor x, at::Tensor seg, at::Tensor 
   CUtensorMap tA = make_map(dy.data_ptr(), R, M, M, 64, 64);
   CUtensorMap tB = make_map(x.data_ptr(), R, N, N, 64, 64);
   Params p{};
+  p.m_fast = raster_m_fast();
   p.C = out.data_ptr();
   p.M = (int)M;
   p.N = (int)N;
@@ -1263,6 +1285,7 @@ void gemm_rs(at::Tensor a, at::Tensor b, bool trans_a, bool trans_b, at::Tensor 
   CUtensorMap tA = a_mn ? make_map(a.data_ptr(), K, M, a.stride(0), 64, bk2) : make_map(a.data_ptr(), M, K, a.stride(0), 64, 128);
   CUtensorMap tB = b_mn ? make_map(b.data_ptr(), K, N, b.stride(0), 64, bk2) : make_map(b.data_ptr(), N, K, b.stride(0), 64, 128);
   Params p{};
+  p.m_fast = raster_m_fast();
   p.C = nullptr;
   p.M = (int)M;
   p.N = (int)N;
@@ -1310,6 +1333,7 @@ at::Tensor gemm_ag(at::Tensor local, at::Tensor b, bool trans_b, at::Tensor peer
                         : make_map(b.data_ptr(), N, K, b.stride(0), 64, 128);
   auto C = at::empty({M, N}, local.options());
   Params p{};
+  p.m_fast = raster_m_fast();
   p.C = C.data_ptr();
   p.M = (int)M;
   p.N = (int)N;
