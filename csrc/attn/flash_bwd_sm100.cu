@@ -5,12 +5,15 @@
 // across all of them and are written once, with no atomics.  Per (head, query tile) step:
 //   S^T  = K_j Q_i^T          (TMEM cols   0..127; later reused for dQ)
 //   dP^T = V_j dO_i^T         (TMEM cols 128..255)
-//   one thread per key row:   P^T = exp(S^T * scale - lse), dS^T = P^T * (dP^T - Delta) * scale, both written
-//                             as bf16 128-byte-swizzled tiles [key rows x query cols]
-//   dV  += P^T dO_i            (cols 256..383; dO as an MN-major operand)
+//   one thread per key row:   P^T = exp(S^T * scale - lse) written back as packed bf16 into TMEM cols 0..63,
+//                             dS^T = P^T * (dP^T - Delta) * scale as a bf16 128-byte-swizzled shared tile
+//   dV  += P^T dO_i            (cols 256..383; P^T from TMEM as the A operand, dO as an MN-major operand)
 //   dK  += dS^T Q_i            (cols 384..511; Q as an MN-major operand)
-//   dQ_i = dS K_j              (cols 0..127; the dS^T tile read as an MN-major A operand, K_j as MN-major B)
-//   one thread per query row adds its dQ row into an fp32 accumulator with 16-byte vector atomics.
+//   dQ_i = dS K_j              (cols 128..255, where dP^T was; dS^T read as an MN-major A operand, K_j MN-major B)
+//   one thread per query row adds its dQ row into an fp32 accumulator with bulk tensor add-reductions.
+// Q tiles are double-buffered, so the next step's Q arrives while this step runs, and S^T of the next step is
+// issued right after this step's MMAs (its columns hold only P^T, which the dV MMA before it has read): it
+// overlaps the dQ read-out, and only dP^T of the next step waits for that read-out (it overwrites dQ).
 // Delta = rowsum(dO * O) comes from a small preprocessing kernel; a finishing kernel casts the dQ accumulator
 // into the query slots of dqkv.  Waits are bounded (error flag); no TMA multicast.
 #include <cudaTypedefs.h>
@@ -27,7 +30,7 @@ namespace fab {
 constexpr int D = 128, T = 128;
 constexpr int TILE = 128 * 128 * 2;
 constexpr int DQ_STAGE = 4 * 2 * 4096;  // dQ staging: per softmax warp two 32-row x 128-byte blocks
-constexpr int SMEM_BYTES = 6 * TILE + DQ_STAGE + 1024 /*lse, delta*/ + 1024 /*align*/ + 256 /*barriers*/;
+constexpr int SMEM_BYTES = 6 * TILE + DQ_STAGE + 1024 /*lse, delta*/ + 1024 /*align*/ + 256 /*barriers*/;  // K V Q0 Q1 dO dS
 static_assert(SMEM_BYTES <= 232448, "flash_bwd_kernel shared memory above the 227 KiB per-block limit");
 constexpr uint32_t WAIT_LIMIT = 1u << 26;
 
@@ -77,6 +80,12 @@ __device__ __forceinline__ void mma(uint32_t d, uint64_t a, uint64_t b, uint32_t
       "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(d),
       "l"(a), "l"(b), "r"(id), "r"(acc));
 }
+// A from tensor memory (128 lanes x 16 bf16 packed in 8 columns), B from shared memory
+__device__ __forceinline__ void mma_ts(uint32_t d, uint32_t a_tmem, uint64_t b, uint32_t id, uint32_t acc) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n}\n" ::"r"(d),
+      "r"(a_tmem), "l"(b), "r"(id), "r"(acc));
+}
 __device__ __forceinline__ void commit(uint64_t* bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(su32(bar))
                : "memory");
@@ -95,6 +104,14 @@ __device__ __forceinline__ float ex2f_approx(float x) {
         "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),     \
         "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])                   \
       : "r"(taddr))
+
+#define FAB_ST16(taddr, r)                                                                                          \
+  asm volatile(                                                                                                     \
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"( \
+          taddr),                                                                                                   \
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]), \
+      "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])                                       \
+      : "memory")
 
 __device__ __forceinline__ uint32_t swz_off(int row, int col) {
   const int panel = col >> 6, c = col & 63;
@@ -119,23 +136,24 @@ __global__ void __launch_bounds__(192, 1)
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sK = sm;
   uint8_t* sV = sm + TILE;
-  uint8_t* sQ = sm + 2 * TILE;
-  uint8_t* sdO = sm + 3 * TILE;
-  uint8_t* sP = sm + 4 * TILE;   // P^T  [key rows x query cols]
+  uint8_t* sQ = sm + 2 * TILE;   // [2]: Q of steps n (n even) and n (n odd)
+  uint8_t* sdO = sm + 4 * TILE;
   uint8_t* sdS = sm + 5 * TILE;  // dS^T [key rows x query cols]
   uint8_t* sdq = sm + 6 * TILE;  // [4 warps][2][32 rows x 128 B], 128-byte swizzle
   float* s_lse = reinterpret_cast<float*>(sm + 6 * TILE + DQ_STAGE);
   float* s_delta = s_lse + 128;
   uint64_t* bars = reinterpret_cast<uint64_t*>(sm + 6 * TILE + DQ_STAGE + 1024);
   uint64_t* kv_full = bars;
-  uint64_t* qdo_full = bars + 1;
-  uint64_t* qdo_empty = bars + 2;
-  uint64_t* s_full = bars + 3;
-  uint64_t* ds_full = bars + 4;
-  uint64_t* mma2_done = bars + 5;
-  uint64_t* dq_empty = bars + 6;
-  uint64_t* stats_full = bars + 7;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 8);
+  uint64_t* q_full = bars + 1;   // [2]
+  uint64_t* q_empty = bars + 3;  // [2]
+  uint64_t* do_full = bars + 5;
+  uint64_t* do_empty = bars + 6;
+  uint64_t* s_full = bars + 7;
+  uint64_t* ds_full = bars + 8;
+  uint64_t* mma2_done = bars + 9;
+  uint64_t* dq_empty = bars + 10;
+  uint64_t* stats_full = bars + 11;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 12);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -151,8 +169,12 @@ __global__ void __launch_bounds__(192, 1)
 
   if (threadIdx.x == 0) {
     bar_init(kv_full, 1);
-    bar_init(qdo_full, 1);
-    bar_init(qdo_empty, 1);
+    for (int i = 0; i < 2; ++i) {
+      bar_init(&q_full[i], 1);
+      bar_init(&q_empty[i], 1);
+    }
+    bar_init(do_full, 1);
+    bar_init(do_empty, 1);
     bar_init(s_full, 1);
     bar_init(ds_full, 4);
     bar_init(mma2_done, 1);
@@ -180,30 +202,46 @@ __global__ void __launch_bounds__(192, 1)
       for (int n = 0; n < nsteps; ++n) {
         const int hj = n / (nq - i0), it = i0 + n % (nq - i0);
         const int h = g * p.hpg + hj;
-        if (!bar_wait(qdo_empty, (n & 1) ^ 1, p.err, 41) || *abort_flag) { *abort_flag = 1; break; }
-        bar_expect(qdo_full, 2 * TILE);
-        tma4(sQ, &tqkv, qdo_full, 0, g * slots + hj, bidx, it * T);
-        tma4(sQ + 16384, &tqkv, qdo_full, 64, g * slots + hj, bidx, it * T);
-        tma4(sdO, &tdo, qdo_full, 0, h, bidx, it * T);
-        tma4(sdO + 16384, &tdo, qdo_full, 64, h, bidx, it * T);
+        const int qb = n & 1;
+        // Q(n) goes into the buffer step n - 2 used (free once that step's MMAs completed)
+        if (!bar_wait(&q_empty[qb], ((n >> 1) & 1) ^ 1, p.err, 41) || *abort_flag) { *abort_flag = 1; break; }
+        bar_expect(&q_full[qb], TILE);
+        tma4(sQ + qb * TILE, &tqkv, &q_full[qb], 0, g * slots + hj, bidx, it * T);
+        tma4(sQ + qb * TILE + 16384, &tqkv, &q_full[qb], 64, g * slots + hj, bidx, it * T);
+        // dO(n) into the single dO buffer once step n - 1's MMAs completed
+        if (!bar_wait(do_empty, (n & 1) ^ 1, p.err, 50) || *abort_flag) { *abort_flag = 1; break; }
+        bar_expect(do_full, TILE);
+        tma4(sdO, &tdo, do_full, 0, h, bidx, it * T);
+        tma4(sdO + 16384, &tdo, do_full, 64, h, bidx, it * T);
       }
     }
   } else if (warp == 1) {
     if (lane == 0) {
       const uint32_t id_kk = idesc(false, false), id_kmn = idesc(false, true), id_mnmn = idesc(true, true);
-      const uint32_t aK = su32(sK), aV = su32(sV), aQ = su32(sQ), adO = su32(sdO), aP = su32(sP), adS = su32(sdS);
+      const uint32_t aK = su32(sK), aV = su32(sV), adO = su32(sdO), adS = su32(sdS);
       bool ok = bar_wait(kv_full, 0, p.err, 42) && !*abort_flag;
       for (int n = 0; n < nsteps && ok; ++n) {
         const uint32_t ph = n & 1;
-        if (!bar_wait(qdo_full, ph, p.err, 43) || !bar_wait(dq_empty, ph ^ 1, p.err, 44) || *abort_flag) {
+        const int qb = n & 1;
+        const uint32_t aQ = su32(sQ + qb * TILE);
+        // S^T = K Q^T (cols 0..127): needs only this step's Q; its columns last held P^T(n - 1), which the
+        // dV MMA of step n - 1, issued before on this thread, has read (the tensor pipe runs them in order)
+        if (!bar_wait(&q_full[qb], (n >> 1) & 1, p.err, 43) || *abort_flag) { ok = false; break; }
+        fence_after();
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {  // reduce over d: K-major panels of the K / Q tiles
+          const uint32_t off = (k >> 2) * 16384 + (k & 3) * 32;
+          mma(tmem + 0, desc(aK + off, 16, 1024), desc(aQ + off, 16, 1024), id_kk, k != 0);
+        }
+        // dP^T = V dO^T (cols 128..255): needs dO(n) and dQ(n - 1) read out of these columns
+        if (!bar_wait(do_full, ph, p.err, 51) || !bar_wait(dq_empty, ph ^ 1, p.err, 44) || *abort_flag) {
           ok = false;
           break;
         }
         fence_after();
 #pragma unroll
-        for (int k = 0; k < 8; ++k) {  // reduce over d: K-major panels of the K/V/Q/dO tiles
+        for (int k = 0; k < 8; ++k) {
           const uint32_t off = (k >> 2) * 16384 + (k & 3) * 32;
-          mma(tmem + 0, desc(aK + off, 16, 1024), desc(aQ + off, 16, 1024), id_kk, k != 0);
           mma(tmem + 128, desc(aV + off, 16, 1024), desc(adO + off, 16, 1024), id_kk, k != 0);
         }
         commit(s_full);
@@ -211,16 +249,18 @@ __global__ void __launch_bounds__(192, 1)
         fence_after();
 #pragma unroll
         for (int k = 0; k < 8; ++k) {  // reduce over the query index
-          const uint32_t offa = (k >> 2) * 16384 + (k & 3) * 32;  // P^T / dS^T as K-major A (rows = keys)
+          const uint32_t offa = (k >> 2) * 16384 + (k & 3) * 32;  // dS^T as K-major A (rows = keys)
           const uint32_t offb = k * 2048;                          // dO / Q as MN-major B (rows = queries)
-          mma(tmem + 256, desc(aP + offa, 16, 1024), desc(adO + offb, 16384, 1024), id_kmn, (n | k) != 0);
+          // P^T from TMEM: 16 queries of bf16 pairs = 8 columns per k-step
+          mma_ts(tmem + 256, tmem + k * 8, desc(adO + offb, 16384, 1024), id_kmn, (n | k) != 0);
           mma(tmem + 384, desc(adS + offa, 16, 1024), desc(aQ + offb, 16384, 1024), id_kmn, (n | k) != 0);
         }
 #pragma unroll
         for (int k = 0; k < 8; ++k) {  // dQ = dS K: reduce over keys; dS^T tile as MN-major A, K tile MN-major B
-          mma(tmem + 0, desc(adS + k * 2048, 16384, 1024), desc(aK + k * 2048, 16384, 1024), id_mnmn, k != 0);
+          mma(tmem + 128, desc(adS + k * 2048, 16384, 1024), desc(aK + k * 2048, 16384, 1024), id_mnmn, k != 0);
         }
-        commit(qdo_empty);
+        commit(&q_empty[qb]);
+        commit(do_empty);
         commit(mma2_done);
       }
       if (!ok) *abort_flag = 1;
@@ -253,22 +293,29 @@ __global__ void __launch_bounds__(192, 1)
         FAB_LD32(tmem + lane_base + c * 32, sv);
         FAB_LD32(tmem + lane_base + 128 + c * 32, dv);
         asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-        float pf[32], df[32];
+        float df[32];
+        uint32_t pk[16];
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const int q = c * 32 + i;
-          const int qpos = it * T + q;
-          float pr = ex2f_approx(fmaf(__uint_as_float(sv[i]), p.scale_log2, -s_lse[q]));
-          if (diag && qpos < kpos) pr = 0.f;
-          pf[i] = pr;
-          df[i] = pr * (__uint_as_float(dv[i]) - s_delta[q]) * p.scale;
+        for (int i = 0; i < 32; i += 2) {
+          float pr2[2];
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            const int q = c * 32 + i + e;
+            const int qpos = it * T + q;
+            float pr = ex2f_approx(fmaf(__uint_as_float(sv[i + e]), p.scale_log2, -s_lse[q]));
+            if (diag && qpos < kpos) pr = 0.f;
+            pr2[e] = pr;
+            df[i + e] = pr * (__uint_as_float(dv[i + e]) - s_delta[q]) * p.scale;
+          }
+          asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(pk[i >> 1]) : "f"(pr2[1]), "f"(pr2[0]));
         }
+        // P^T chunk c -> TMEM columns [16 c, 16 c + 16) of S^T: columns this thread has already read
+        FAB_ST16(tmem + lane_base + c * 16, pk);
 #pragma unroll
-        for (int v8 = 0; v8 < 4; ++v8) {
-          *reinterpret_cast<uint4*>(sP + swz_off(r, c * 32 + v8 * 8)) = pack8(pf + v8 * 8);
+        for (int v8 = 0; v8 < 4; ++v8)
           *reinterpret_cast<uint4*>(sdS + swz_off(r, c * 32 + v8 * 8)) = pack8(df + v8 * 8);
-        }
       }
+      asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
       fence_before();
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       __syncwarp();
@@ -281,7 +328,7 @@ __global__ void __launch_bounds__(192, 1)
 #pragma unroll 1
       for (int c = 0; c < 4; ++c) {
         uint32_t qv[32];
-        FAB_LD32(tmem + lane_base + c * 32, qv);
+        FAB_LD32(tmem + lane_base + 128 + c * 32, qv);
         asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
         uint8_t* wbuf = sdq + quarter * 8192 + (dq_n & 1) * 4096;
         if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
