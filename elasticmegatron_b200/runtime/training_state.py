@@ -8,6 +8,8 @@ optimizer, scheduler) survives a release.
 """
 from __future__ import annotations
 
+import contextlib
+
 from typing import Callable, Dict, List, Optional
 
 import torch
@@ -21,6 +23,32 @@ from ..parallel.scheduler import OptimizerParamScheduler
 from ..parallel.strategy import ParallelStrategy
 from ..planner.layout import RankLayout, rank_layout
 from .memory import Arena, get_pool
+
+
+class StepHooks:
+    """The per-layout hooks a training loop calls around forward / backward (see ``TrainingState.refresh_config``)."""
+
+    def __init__(self, ddp):
+        self.ddp = ddp
+
+    @contextlib.contextmanager
+    def no_sync_func(self):
+        prev = self.ddp.sync_enabled
+        self.ddp.sync_enabled = False
+        try:
+            yield
+        finally:
+            self.ddp.sync_enabled = prev
+
+    def grad_sync_func(self) -> None:
+        self.ddp.finish_grad_sync()
+
+    def param_sync_func(self, overlap: bool = False) -> None:
+        self.ddp.start_param_sync(overlap=overlap)
+
+    @staticmethod
+    def grad_scale_func(loss):
+        return loss
 
 
 class TrainingState:
@@ -236,8 +264,25 @@ class TrainingState:
 
     @staticmethod
     def refresh_config(model, optimizer):
-        """Re-wire grad-sync hooks for the active model (hooks are owned by DDP here, so nothing to do)."""
-        return None
+        """Bind the step hooks of the layout that owns ``model`` (reference: training_state.py:110-135, which
+        points Megatron's model config at the new DDP's ``no_sync`` / ``start_grad_sync`` / ``start_param_sync``
+        and the optimizer's loss scaling after a switch).
+
+        Returns a :class:`StepHooks` and stores it on every model chunk as ``step_hooks``: ``no_sync_func`` (a
+        context in which backward only accumulates gradients), ``grad_sync_func`` (finish the DP reduction of
+        the step), ``param_sync_func`` (start the parameter all-gathers, in flight until the forward needs each
+        bucket when ``overlap`` is true) and ``grad_scale_func`` (bf16 training has no loss scale: identity).
+        Custom training loops call these instead of holding on to a previous layout's DDP."""
+        chunks = list(model) if isinstance(model, (list, tuple)) else [model]
+        ts = chunks[0].__dict__.get("_training_state") if chunks else None
+        if ts is None:
+            raise ValueError("refresh_config: the model does not belong to a TrainingState")
+        if optimizer is not None and optimizer is not ts.optimizer:
+            raise ValueError("refresh_config: the optimizer belongs to another layout than the model")
+        hooks = StepHooks(ts.ddp)
+        for c in chunks:
+            c.step_hooks = hooks
+        return hooks
 
     def update_model_weight(self) -> None:
         """Regenerate params from the fp32 master of the own shard and all-gather over DP (reference:

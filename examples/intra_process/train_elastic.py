@@ -132,6 +132,9 @@ def main(argv=None):
                     if a.save_around_reshard else {}
                 ts = mgr.reshard(strategies[k], **ckpt)
                 it = mgr.build_iterators(args.consumed_train_samples)[0] if ts is not None else None
+                if ts is not None:
+                    # the new layout's step hooks (the reference's loop re-binds its model config here)
+                    ts.refresh_config(ts.model, ts.optimizer)
         if ts is None:
             args.consumed_train_samples += a.global_batch_size
             args.iteration = iteration

@@ -83,7 +83,17 @@ def _api(rank, world):
     back.param_flat.zero_()
     back.update_model_weight()
     out["update_model_weight"] = torch.equal(back.param_flat, good)
-    out["refresh_config"] = back.refresh_config(back.model, back.optimizer) is None
+    hooks = back.refresh_config(back.model, back.optimizer)
+    ok = all(getattr(c, "step_hooks", None) is hooks for c in back.model) and hooks.ddp is back.ddp
+    with hooks.no_sync_func():
+        ok &= back.ddp.sync_enabled is False
+    ok &= back.ddp.sync_enabled is True and hooks.grad_scale_func(3.0) == 3.0
+    try:
+        back.refresh_config(back.model, object())  # an optimizer of another layout
+        ok = False
+    except ValueError:
+        pass
+    out["refresh_config"] = bool(ok)
     # the reference's constructor form: the live model (and its optimizer / scheduler) instead of the state
     m2 = ElasticMegatronManager(specs, model=back.model, optimizer=back.optimizer,
                                 opt_param_scheduler=back.opt_param_scheduler, engine="torch")
