@@ -224,7 +224,8 @@ class ElasticMegatronManager:
         # released nor a released state rebuilt (the reference turns release / rebuild into no-ops for its fake
         # transfers, elastic_manager.py:268-304)
         is_meta_device = is_meta_device or self._warm_only
-        assert not (is_meta_device and save_ckpt), "Can't save checkpoint in meta device"
+        if is_meta_device and save_ckpt:
+            raise ValueError("reshard: save_ckpt needs real tensors; a meta-device switch moves no data to save")
         dst_s = ParallelStrategy.from_any(new_parallel_strategy)
         assert dst_s in self._states, f"strategy {dst_s} was not declared at construction"
         src_s = self.current
