@@ -7,6 +7,10 @@ backward, then all-reduced across Group-ZeRO instances; after the optimizer step
 are all-gathered.  The layout comes from ``planner/layout.py`` so the reshard planner sees exactly the
 buffers used here.
 
+On CUDA the bucket collectives are this framework's kernels: the reduce-scatter and the parameter all-gather
+pull over NVLink peer memory (``dp_comm.py``, ``EMB_DP_PEER=0`` for NCCL), and the Group-ZeRO cross-instance
+all-reduce goes through NVSwitch multicast or peer memory (``nvls.py``, ``EMB_NVLS=0`` for NCCL).
+
 Gradient scaling: buckets are reduced with SUM and the optimizer scales the own shard by ``1/(DP*CP)``
 (dense and expert alike: expert replicas jointly see the tokens of every DP*CP rank).  Parameters whose
 gradients are partial sums across TP ranks under sequence parallelism (norm weights, router) are first
