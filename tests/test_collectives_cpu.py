@@ -120,3 +120,32 @@ def test_gather_inverts_scatter():
     for vp in virtual_params(cfg):
         assert torch.equal(outp[vp.index], g[vp.index]), vp
         assert torch.equal(outo[vp.index], og[vp.index]), vp
+
+
+def _nvls_fallback(rank, world):
+    import os
+
+    import torch
+    import torch.distributed as dist
+
+    from elasticmegatron_b200.parallel import nvls
+
+    out = {}
+    for v, want in (("1", "auto"), ("nvls", "nvls"), ("p2p", "p2p"), ("0", "off"), ("nccl", "off")):
+        os.environ["EMB_NVLS"] = v
+        out[v] = nvls.mode() == want
+    os.environ["EMB_NVLS"] = "1"
+    # host tensors on a gloo group take the library all-reduce (the symmetric reducers are CUDA-only)
+    x = torch.arange(6, dtype=torch.float32) * (rank + 1)
+    ref = x.clone()
+    dist.all_reduce(ref)
+    nvls.all_reduce_(x, dist.group.WORLD)
+    out["sum"] = bool(torch.equal(x, ref))
+    out["no_reducer"] = len(nvls._CACHE) == 0
+    return out
+
+
+def test_symmetric_all_reduce_host_fallback():
+    """EMB_NVLS parsing, and the NCCL / gloo fallback for tensors the symmetric reducers do not take."""
+    for r in run_distributed(_nvls_fallback, 2):
+        assert all(r.values()), r
