@@ -262,6 +262,8 @@ def main():
                     "unit": "tokens/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": 4 * world,
                     "loss": loss},
             "gpu_launches": int(launches),
+            # GEMM calls that ran on the library because the tcgen05 kernels could not take their operands
+            "gemm_fallbacks": int(getattr(ext(), "gemm_fallback_count", lambda: -1)()),
             "strategies": per_strategy,
             "switches": switches,
             "link_gbs_measured": link_gbs,

@@ -47,6 +47,7 @@ torch::Tensor attn_bwd(torch::Tensor dO, torch::Tensor qkv, torch::Tensor o, tor
 int64_t attn_bwd_error_flag();
 void attn_merge(torch::Tensor out, torch::Tensor lse, torch::Tensor o_b, torch::Tensor l_b);
 int64_t gemm_error_flag();
+int64_t gemm_fallback_count();
 at::Tensor attn_exp2_emulated(at::Tensor x);
 void dp_signal(at::Tensor flags, int64_t me, int64_t slot0, int64_t nslots, int64_t epoch);
 void dp_rs_pull(at::Tensor peers, int64_t me, int64_t off, int64_t count, at::Tensor flags, int64_t slot,
@@ -130,6 +131,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("dp_rs_pull", &dp_rs_pull);
   m.def("dp_ag_pull", &dp_ag_pull);
   m.def("attn_debug_counters", &attn_debug_counters);
+  m.def("gemm_fallback_count", &gemm_fallback_count);
   m.def("gemm_error_flag", &gemm_error_flag);
   m.def("gemm_debug_counters", &gemm_debug_counters);
   m.def("gemm_rs", &gemm_rs);

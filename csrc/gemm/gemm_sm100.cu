@@ -24,6 +24,8 @@
 
 #include <cstdlib>
 
+#include <atomic>
+
 #include "../include/common.cuh"
 
 namespace emb {
@@ -1395,9 +1397,17 @@ std::vector<int64_t> gemm_debug_counters() {
 void gemm_clear_error() { EMB_CUDA_CHECK(cudaMemset(gk::err_flag(), 0, sizeof(int))); }
 
 // Library fallback for operands the tensor-core kernel does not take (e.g. fp32 inputs or unaligned strides).
+// Calls of gemm() that the tcgen05 kernels could not take (dtype, layout or a row stride that breaks TMA's
+// 16-byte rule) and that therefore ran on at::matmul; the first one also prints a warning.
+static std::atomic<int64_t> g_gemm_fallbacks{0};
+int64_t gemm_fallback_count() { return g_gemm_fallbacks.load(); }
+
 at::Tensor gemm(at::Tensor a, at::Tensor b, bool trans_a, bool trans_b, c10::optional<at::Tensor> out,
                    bool accumulate) {
   if (gemm_tc_supported(a, b, trans_a, trans_b, out, accumulate)) return gemm_tc(a, b, trans_a, trans_b, out, accumulate, 0);
+  g_gemm_fallbacks.fetch_add(1);
+  TORCH_WARN_ONCE("gemm: operands the tcgen05 kernels cannot take (dtype, layout or a row stride that is not a "
+                  "multiple of 16 bytes) run on at::matmul; gemm_fallback_count() counts them");
   auto A = trans_a ? a.t() : a;
   auto B = trans_b ? b.t() : b;
   if (out.has_value() && out->defined()) {
