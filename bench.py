@@ -288,7 +288,9 @@ def switching_phases(args, world, strategies, sched, ts, tokens_per_step, timed_
     from elasticmegatron_b200.transfer.validate import state_checksum
     from elasticmegatron_b200.utils.links import measure_peer_copy_gbs
 
-    mgr = ElasticMegatronManager(strategies, training_state=ts, engine="native")
+    # the NVLink kernel engine on GPUs; host ranks (the CPU plumbing test of these phases) use batched P2P
+    mgr = ElasticMegatronManager(strategies, training_state=ts,
+                                 engine="native" if torch.cuda.is_available() else "torch")
     world_g = ProcessGroupPool.get(list(range(world)))
     # 3. tokens/s per strategy of the schedule
     per = []
@@ -300,7 +302,7 @@ def switching_phases(args, world, strategies, sched, ts, tokens_per_step, timed_
         per.append({"strategy": short(s), "tokens_per_s": tokens_per_step * args.strategy_steps / (ms / 1e3),
                     "ms_per_step": ms / args.strategy_steps, "steps": args.strategy_steps})
     # 4. switch latency per consecutive pair (schedule is a cycle: it ends at the base layout)
-    link = measure_peer_copy_gbs()
+    link = measure_peer_copy_gbs() if torch.cuda.is_available() else None
     chain = [sched[-1]] + sched
     switches, all_ok = [], True
     for a, b in zip(chain[:-1], chain[1:]):
@@ -336,12 +338,12 @@ def switching_phases(args, world, strategies, sched, ts, tokens_per_step, timed_
                            "schedule on this framework's layouts; not the reference's own build"}
         a, b = sched[-1], sched[0]
         mgr.reshard(a)
-        native_engine = mgr.engine
+        native_engine, native_name = mgr.engine, mgr.engine_name
         for name in ("torch", "reference"):
             mgr.engine, mgr.engine_name = mgr._make_engine(name), name
             mgr.reshard(b)
             context[name] = {"src": short(a), "dst": short(b), "transfer_ms": mgr.last_switch["transfer_ms"]}
-            mgr.engine, mgr.engine_name = native_engine, "native"
+            mgr.engine, mgr.engine_name = native_engine, native_name
             mgr.reshard(a)
     barrier()
     return per, switches, context, link, bool(all_ok)
