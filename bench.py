@@ -17,7 +17,8 @@ Phases (all device times are CUDA events on the compute stream, MAX over ranks):
    pinned host memory and the loss read back to the host, timed by the host clock.
 3. (N > 1) ``strategies``: the switching schedule of BASELINE config 2 scaled to N GPUs (at 8: TP8 -> TP4*DP2 ->
    TP2*PP2*DP2 -> TP1*DP8, sequence parallelism on whenever TP > 1): switch with the native engine, run one
-   untimed step, then time ``--strategy-steps`` steps -> tokens/s per strategy.
+   untimed step, then time ``--strategy-steps`` steps -> tokens/s per strategy (released state arenas are handed
+   back to the driver first when less than a quarter of the GPU is free, so the step's activations fit).
 4. (N > 1) ``switches``: for every consecutive pair of the schedule, ``--reshard-iters`` round trips without
    training in between; p50 device latency per direction, GB moved, and the roofline fraction at the nominal
    900 GB/s per direction and at the peer-copy rate measured at the start of this phase (``link_gbs_measured``,
@@ -297,6 +298,7 @@ def switching_phases(args, world, strategies, sched, ts, tokens_per_step, timed_
     for s in sched:
         st = mgr.reshard(s)
         itr = mgr.build_iterators(0)[0]
+        make_room_for_activations()
         train_step_untimed(st, itr)
         ms = max_over_ranks([timed_steps(st, itr, args.strategy_steps)])[0]
         per.append({"strategy": short(s), "tokens_per_s": tokens_per_step * args.strategy_steps / (ms / 1e3),
@@ -347,6 +349,22 @@ def switching_phases(args, world, strategies, sched, ts, tokens_per_step, timed_
             mgr.reshard(a)
     barrier()
     return per, switches, context, link, bool(all_ok)
+
+
+def make_room_for_activations(min_free_frac: float = 0.25) -> None:
+    """Before training under a new layout: when less than ``min_free_frac`` of the GPU is free, return the arena
+    pool's cached (released) state arenas to the driver.  The cache keeps up to 40 % of the device for fast
+    switch-backs; with 2 GPUs a 7B state plus a full cache plus a step's activations comes close to the device's
+    size.  Local to each rank (no collective)."""
+    import torch
+
+    if not torch.cuda.is_available():
+        return
+    free, total = torch.cuda.mem_get_info()
+    if free < min_free_frac * total:
+        from elasticmegatron_b200.runtime.memory import get_pool
+
+        get_pool(torch.device("cuda", torch.cuda.current_device())).trim()
 
 
 def train_step_untimed(st, itr):
